@@ -1,0 +1,60 @@
+import asyncio
+
+import pytest
+import torch
+
+from kunserve_b200.config import BalloonConfig, BenchConfig, CacheConfig, ParallelConfig, SchedConfig
+from kunserve_b200.engine.instance import InstanceEngine
+from kunserve_b200.engine.worker import Worker
+from kunserve_b200.runtime import LocalActor
+
+from helpers import drive, hf_from_weights, hf_greedy, make_requests, tiny_model
+
+
+def _engine(num_pages=64, chunked=False, budget=64, policy="prefill-first", max_bs=256):
+    mc = tiny_model()
+    pc = ParallelConfig()
+    cc = CacheConfig(block_size=16)
+    w = Worker(0, mc, cc, pc, backend="torch", device="cpu", seed=7)
+    sc = SchedConfig(policy=policy, enable_chunked_prefill=chunked, chunked_prefill_budget=budget,
+                     max_batch_size=max_bs)
+    eng = InstanceEngine(0, 0, mc, pc, cc, sc, BalloonConfig(), BenchConfig(), [[LocalActor(w)]])
+    return eng, w, mc
+
+
+@pytest.mark.parametrize("chunked,policy", [(False, "prefill-first"), (True, "prefill-first"), (True, "mixed")])
+def test_tokens_match_hf(chunked, policy):
+    eng, w, mc = _engine(chunked=chunked, policy=policy, budget=48)
+    reqs = make_requests(6, seed=1)
+    prompts = {r.request_id: list(r.prompt_token_ids) for r in reqs}
+    lens = {r.request_id: r.sampling_params.max_tokens for r in reqs}
+
+    async def run():
+        await eng.initialize(num_gpu_blocks=64)
+        return await drive(eng, reqs)
+
+    got = asyncio.run(run())
+    hf = hf_from_weights(mc, w.runner.w)
+    for rid, toks in got.items():
+        assert toks == hf_greedy(hf, prompts[rid], lens[rid]), rid
+    eng.block_managers[0].check_invariants()
+
+
+def test_preemption_under_small_pool():
+    eng, w, mc = _engine(num_pages=12)
+    reqs = make_requests(10, seed=2, plen=(20, 40), olen=(20, 30))
+    prompts = {r.request_id: list(r.prompt_token_ids) for r in reqs}
+    lens = {r.request_id: r.sampling_params.max_tokens for r in reqs}
+
+    async def run():
+        await eng.initialize(num_gpu_blocks=12)
+        return await drive(eng, reqs)
+
+    got = asyncio.run(run())
+    assert eng.get_num_preemption() > 0
+    hf = hf_from_weights(mc, w.runner.w)
+    for rid in list(got)[:4]:
+        assert got[rid] == hf_greedy(hf, prompts[rid], lens[rid])
+    bm = eng.block_managers[0]
+    bm.check_invariants()
+    assert bm.num_free_whole() == bm.P
