@@ -1,0 +1,110 @@
+"""Building a serving job: workers (one per device or CPU rank), instances,
+balloon groups and the front end.
+
+Parity: ``kunserve/setup.py`` (``connect_to_ray_cluster`` :10-36,
+``setup_kunserve`` :38-73) and the worker/communicator set-up of
+``flash_backend.py:323-376``.  Workers are process actors (or Ray actors when
+``KUNSERVE_USE_RAY=1``); a single-device job keeps its worker in-process.
+Each worker process joins one ``torch.distributed`` job (NCCL on GPU, gloo on
+CPU) and builds the five communicators of ``parallel/topology.py``.
+"""
+import os
+import socket
+from typing import List, Optional
+
+import torch
+
+from .config.kunserve_config import KunServeConfig
+from .config.runtime import CacheConfig, ModelConfig, ParallelConfig, SchedConfig
+from .engine.instance import InstanceEngine
+from .engine.worker import Worker
+from .parallel.topology import Topology
+from .runtime.actors import LocalActor, ProcessActor, make_actor, ray_available
+from .utils.logger import init_logger
+
+logger = init_logger(__name__)
+
+
+def free_port() -> int:
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def connect_to_ray_cluster(address: Optional[str] = None) -> bool:
+    """Join a Ray cluster when Ray is installed and enabled; otherwise the
+    built-in process actors are used and this is a no-op."""
+    if not ray_available():
+        return False
+    import ray
+
+    if not ray.is_initialized():
+        ray.init(address=address or "auto", namespace="kunserve", ignore_reinit_error=True)
+    return True
+
+
+def make_worker_process(rank: int, world: int, port: int, topo: Topology, mc: ModelConfig, cc: CacheConfig,
+                        pc: ParallelConfig, backend: str, device: str, seed: int, timeout_s: float = 120.0):
+    """Runs inside a worker process: joins the job and builds the Worker."""
+    from .parallel.comm import Communicator, init_default_group
+
+    if device.startswith("cuda"):
+        torch.cuda.set_device(torch.device(device))
+    dist_backend = "nccl" if device.startswith("cuda") else "gloo"
+    init_default_group(dist_backend, rank, world, timeout_s=timeout_s, master_port=port)
+    comm = Communicator(topo, rank, dist_backend)
+    return Worker(rank, mc, cc, pc, backend=backend, device=device, comm=comm, seed=seed)
+
+
+def build_instances(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: SchedConfig,
+                    server_id: int = 0, backend: str = "auto", actor_kind: str = "auto",
+                    devices: Optional[List[str]] = None, seed: int = 0, tokenizer=None,
+                    output_callback=None) -> List[List[InstanceEngine]]:
+    ec = cfg.engine_config
+    topo = Topology(1, ec.ngroups, ec.group_size, ec.pp, ec.tp)
+    world = topo.world_size
+    if devices is None:
+        n = torch.cuda.device_count()
+        devices = [f"cuda:{r % n}" for r in range(world)] if n else ["cpu"] * world
+    if actor_kind == "auto":
+        actor_kind = "ray" if ray_available() else ("local" if world == 1 else "process")
+    port = free_port()
+    handles = {}
+    for rank in range(world):
+        _, g, i, st, t = topo.coords(rank)
+        pc = ParallelConfig(tensor_parallel_size=ec.tp, tensor_parallel_rank=t, pipeline_parallel_size=ec.pp,
+                            pipeline_parallel_rank=st, group_parallel_size=ec.group_size * ec.pp,
+                            group_parallel_rank=i * ec.pp + st, replica_size=ec.group_size, replica_rank=i,
+                            global_rank=rank, global_size=world)
+        if actor_kind == "local":
+            handles[rank] = LocalActor(Worker(rank, mc, cc, pc, backend=backend, device=devices[rank], seed=seed))
+        elif actor_kind == "process":
+            env = {"KUNSERVE_WORKER_RANK": str(rank)}
+            handles[rank] = ProcessActor(make_worker_process, rank, world, port, topo, mc, cc, pc, backend,
+                                         devices[rank], seed, env=env)
+        else:
+            handles[rank] = make_actor("ray", make_worker_process, rank, world, port, topo, mc, cc, pc, backend,
+                                       devices[rank], seed, num_gpus=1 if devices[rank] != "cpu" else 0)
+    groups = []
+    for g in range(ec.ngroups):
+        insts = []
+        for i in range(ec.group_size):
+            workers = [[handles[topo.rank_of(0, g, i, st, t)] for t in range(ec.tp)] for st in range(ec.pp)]
+            pc = ParallelConfig(tensor_parallel_size=ec.tp, pipeline_parallel_size=ec.pp,
+                                replica_size=ec.group_size, replica_rank=i)
+            inst = InstanceEngine(server_id, g * ec.group_size + i, mc, pc, cc, sc, cfg.balloon_config,
+                                  cfg.bench_config, workers, tokenizer=tokenizer, output_callback=output_callback)
+            insts.append(inst)
+        groups.append(insts)
+    return groups
+
+
+async def setup_kunserve(cfg: KunServeConfig, model_config: Optional[ModelConfig] = None, **kw):
+    """Create ``nservers`` front ends (``AsyncLLM``) and initialise them."""
+    from .llm import AsyncLLM
+
+    servers = []
+    for s in range(cfg.engine_config.nservers):
+        llm = await AsyncLLM.create(cfg, model_config=model_config, server_id=s, **kw)
+        servers.append(llm)
+    return servers

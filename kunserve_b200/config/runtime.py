@@ -44,6 +44,8 @@ class LlamaArch:
 # Built-in architectures: the BASELINE configurations plus common sizes.
 ARCHS = {
     "tiny-llama": LlamaArch(2, 256, 4, 2, 688, 32000, 4096, 1e-5, 10000.0),
+    # head_dim 128 variant: the smallest model the native engine runs
+    "tiny-llama-128": LlamaArch(2, 512, 4, 2, 1376, 32000, 4096, 1e-5, 10000.0),
     "llama-3-8b": LlamaArch(32, 4096, 32, 8, 14336, 128256, 8192, 1e-5, 500000.0),
     "llama-2-7b": LlamaArch(32, 4096, 32, 32, 11008, 32000, 4096, 1e-5, 10000.0),
     "llama-2-13b": LlamaArch(40, 5120, 40, 40, 13824, 32000, 4096, 1e-5, 10000.0),

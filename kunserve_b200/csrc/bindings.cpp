@@ -1,0 +1,215 @@
+// Python bindings of the native library (module kunserve_b200._C).
+//
+// Besides the Engine, every kernel is exposed as a standalone op on torch
+// tensors so the tests can compare it against a PyTorch fp32 reference.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "engine/arena.h"
+#include "engine/engine.h"
+#include "kernels/gemm.h"
+#include "kernels/kernels.h"
+
+namespace py = pybind11;
+using namespace kus;
+
+namespace {
+
+#define CHECK_CUDA_BF16(t) TORCH_CHECK((t).is_cuda() && (t).scalar_type() == torch::kBFloat16 && (t).is_contiguous(), #t " must be a contiguous bf16 CUDA tensor")
+
+__nv_bfloat16* bp(const torch::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+
+struct Scratch {
+  torch::Tensor ws, counters;
+};
+Scratch& scratch(int device) {
+  static std::vector<Scratch> all(16);
+  Scratch& s = all.at(device);
+  if (!s.ws.defined()) {
+    auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA, device);
+    s.ws = torch::empty({(int64_t)148 * 16 * 128 * 256}, f32);
+    s.counters = torch::zeros({1 << 16}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, device));
+  }
+  return s;
+}
+
+// out = A @ B^T with the chosen epilogue; returns the split-K factor used.
+int64_t gemm_op(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> residual,
+                int64_t bn, int64_t max_split) {
+  CHECK_CUDA_BF16(A);
+  CHECK_CUDA_BF16(B);
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.size(1) == B.size(1), "A [M,K], B [N,K]");
+  TORCH_CHECK(A.size(1) % 8 == 0, "K must be a multiple of 8");
+  c10::cuda::CUDAGuard g(A.device());
+  const int M = A.size(0), K = A.size(1), N = B.size(0);
+  GemmPlan p = plan_gemm(M, N, K, (int)epi, (int)bn, (int)max_split);
+  Scratch& sc = scratch(A.get_device());
+  TORCH_CHECK(workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn) <= (size_t)sc.ws.numel(),
+              "split-K workspace too small");
+  const __nv_bfloat16* res = nullptr;
+  if (epi == EPI_ADD) {
+    TORCH_CHECK(residual.has_value(), "EPI_ADD needs a residual");
+    CHECK_CUDA_BF16(*residual);
+    res = bp(*residual);
+  }
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous(), "out");
+  TORCH_CHECK(finalize_plan(p, A.data_ptr(), K, B.data_ptr(), K, out.data_ptr(), (int)out.size(1), res,
+                            (int)out.size(1), sc.ws.data_ptr<float>(), sc.counters.data_ptr<int>()),
+              "tensor map encoding failed");
+  run_gemm(p, at::cuda::getCurrentCUDAStream());
+  return p.args.split_k;
+}
+
+void rmsnorm_op(torch::Tensor x, c10::optional<torch::Tensor> add, torch::Tensor w, torch::Tensor y,
+                c10::optional<torch::Tensor> rows, double eps) {
+  CHECK_CUDA_BF16(x);
+  CHECK_CUDA_BF16(w);
+  CHECK_CUDA_BF16(y);
+  c10::cuda::CUDAGuard g(x.device());
+  const int R = rows.has_value() ? rows->numel() : x.size(0);
+  rmsnorm(bp(x), add.has_value() ? bp(*add) : nullptr, bp(w), bp(y),
+          rows.has_value() ? rows->data_ptr<int>() : nullptr, R, x.size(1), (float)eps,
+          at::cuda::getCurrentCUDAStream());
+}
+
+KVGeom make_geom(torch::Tensor pool, int64_t P, int64_t N, int64_t Ls, int64_t L, int64_t block_size, int64_t kvh,
+                 int64_t hd) {
+  KVGeom g;
+  g.base = reinterpret_cast<char*>(pool.data_ptr());
+  g.P = (int)P;
+  g.N = (int)N;
+  g.Ls = (int)Ls;
+  g.layer_stride = 2LL * block_size * kvh * hd * 2;
+  g.page_stride = g.layer_stride * L;
+  g.block_size = (int)block_size;
+  g.kvh = (int)kvh;
+  g.hd = (int)hd;
+  return g;
+}
+
+void rope_append_op(torch::Tensor qkv, torch::Tensor positions, torch::Tensor pages, torch::Tensor slots,
+                    torch::Tensor cos_sin, torch::Tensor pool, int64_t P, int64_t N, int64_t Ls, int64_t L,
+                    int64_t block_size, int64_t nq, int64_t nkv, int64_t hd, int64_t layer) {
+  CHECK_CUDA_BF16(qkv);
+  c10::cuda::CUDAGuard g(qkv.device());
+  KVGeom geo = make_geom(pool, P, N, Ls, L, block_size, nkv, hd);
+  rope_append(bp(qkv), positions.data_ptr<int>(), pages.data_ptr<int>(), slots.data_ptr<int>(),
+              cos_sin.data_ptr<float>(), geo, (int)layer, qkv.size(0), (int)nq, (int)nkv, cos_sin.size(0),
+              at::cuda::getCurrentCUDAStream());
+}
+
+void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::Tensor pool, int64_t P, int64_t N,
+                  int64_t Ls, int64_t L, int64_t block_size, int64_t nkv, int64_t layer, torch::Tensor q_start,
+                  torch::Tensor ctx_len, torch::Tensor page_table, torch::Tensor items, int64_t splits,
+                  torch::Tensor o_part, torch::Tensor ml_part, int64_t nq, double scale) {
+  c10::cuda::CUDAGuard g(q.device());
+  KVGeom geo = make_geom(pool, P, N, Ls, L, block_size, nkv, 128);
+  AttnBatch b;
+  b.q_start = q_start.data_ptr<int>();
+  b.ctx_len = ctx_len.data_ptr<int>();
+  b.page_table = page_table.data_ptr<int>();
+  b.max_pages = page_table.size(1);
+  b.items = reinterpret_cast<const int2*>(items.data_ptr<int>());
+  b.n_items = items.size(0);
+  b.splits = (int)splits;
+  AttnScratch sc{o_part.data_ptr<float>(), ml_part.data_ptr<float>()};
+  paged_attention(bp(q), (int)q_stride, bp(out), geo, (int)layer, b, sc, q.size(0), (int)nq, (float)scale,
+                  at::cuda::getCurrentCUDAStream());
+}
+
+void sample_op(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, int64_t step, torch::Tensor out) {
+  c10::cuda::CUDAGuard g(logits.device());
+  sample(logits.data_ptr<float>(), logits.size(0), logits.size(1), logits.size(1), temps.data_ptr<float>(),
+         reinterpret_cast<const unsigned*>(seeds.data_ptr<int>()), (unsigned long long)step, out.data_ptr<int>(),
+         at::cuda::getCurrentCUDAStream());
+}
+
+void embed_op(torch::Tensor tokens, torch::Tensor table, torch::Tensor out) {
+  c10::cuda::CUDAGuard g(table.device());
+  embed(tokens.data_ptr<int>(), bp(table), bp(out), tokens.numel(), table.size(1), table.size(0),
+        at::cuda::getCurrentCUDAStream());
+}
+
+void copy_chunks_op(int64_t dst_ptr, int64_t src_ptr, torch::Tensor dst_off, torch::Tensor src_off, int64_t chunk,
+                    int64_t max_blocks) {
+  c10::cuda::CUDAGuard g(dst_off.device());
+  copy_chunks(reinterpret_cast<void*>(dst_ptr), reinterpret_cast<const void*>(src_ptr), reinterpret_cast<const long long*>(dst_off.data_ptr<int64_t>()),
+              reinterpret_cast<const long long*>(src_off.data_ptr<int64_t>()), dst_off.numel(), chunk, (int)max_blocks, at::cuda::getCurrentCUDAStream());
+}
+
+void fill_normal_op(torch::Tensor t, int64_t seed, double std) {
+  CHECK_CUDA_BF16(t);
+  c10::cuda::CUDAGuard g(t.device());
+  fill_normal_bf16(bp(t), t.numel(), (unsigned long long)seed, (float)std, at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "kunserve_b200 native library: sm_100a kernels and the Llama engine";
+  py::class_<EngineShape>(m, "EngineShape")
+      .def(py::init<>())
+      .def_readwrite("layers", &EngineShape::layers)
+      .def_readwrite("nq", &EngineShape::nq)
+      .def_readwrite("nkv", &EngineShape::nkv)
+      .def_readwrite("hd", &EngineShape::hd)
+      .def_readwrite("hidden", &EngineShape::hidden)
+      .def_readwrite("ffn", &EngineShape::ffn)
+      .def_readwrite("vocab", &EngineShape::vocab)
+      .def_readwrite("max_tokens", &EngineShape::max_tokens)
+      .def_readwrite("max_batch", &EngineShape::max_batch)
+      .def_readwrite("max_pos", &EngineShape::max_pos)
+      .def_readwrite("block_size", &EngineShape::block_size)
+      .def_readwrite("eps", &EngineShape::eps)
+      .def_readwrite("rope_theta", &EngineShape::rope_theta)
+      .def_readwrite("tp", &EngineShape::tp);
+  py::class_<Engine>(m, "Engine")
+      .def(py::init<const EngineShape&, int>())
+      .def("init_memory", &Engine::init_memory)
+      .def("num_pages", &Engine::num_pages)
+      .def("page_bytes", &Engine::page_bytes)
+      .def("layer_slot_bytes", &Engine::layer_slot_bytes)
+      .def("layer_weight_bytes", &Engine::layer_weight_bytes)
+      .def("kv_base_ptr", &Engine::kv_base_ptr)
+      .def("load_layer", &Engine::load_layer)
+      .def("load_globals", &Engine::load_globals)
+      .def("random_init", &Engine::random_init)
+      .def("random_init_layers", &Engine::random_init_layers)
+      .def("layer_bytes_view", &Engine::layer_bytes_view)
+      .def("forward", &Engine::forward, py::call_guard<py::gil_scoped_release>())
+      .def("hidden", &Engine::hidden)
+      .def("logits", &Engine::logits)
+      .def("drop_layers", &Engine::drop_layers)
+      .def("restore_layers", &Engine::restore_layers)
+      .def("dropped", &Engine::dropped)
+      .def("copy_chunks", &Engine::copy_chunks)
+      .def("export_kv_fd", &Engine::export_kv_fd)
+      .def("export_layer_fd", &Engine::export_layer_fd)
+      .def("kv_phys_bytes", &Engine::kv_phys_bytes)
+      .def("layer_segment_bytes", &Engine::layer_segment_bytes)
+      .def("layer_ptr", &Engine::layer_ptr)
+      .def("init_tp_comm", &Engine::init_tp_comm)
+      .def("launches", &Engine::launches)
+      .def("reset_launches", &Engine::reset_launches);
+  py::class_<PeerMapping>(m, "PeerMapping")
+      .def(py::init<int, int, size_t>())
+      .def("ptr", [](const PeerMapping& p) { return reinterpret_cast<int64_t>(p.ptr()); })
+      .def("bytes", &PeerMapping::bytes);
+  m.def("gemm", &gemm_op, py::arg("A"), py::arg("B"), py::arg("out"), py::arg("epi") = 0,
+        py::arg("residual") = py::none(), py::arg("bn") = 0, py::arg("max_split") = 16);
+  m.def("rmsnorm", &rmsnorm_op);
+  m.def("rope_append", &rope_append_op);
+  m.def("attention", &attention_op);
+  m.def("sample", &sample_op);
+  m.def("embed", &embed_op);
+  m.def("copy_chunks", &copy_chunks_op);
+  m.def("fill_normal", &fill_normal_op);
+  m.def("nccl_unique_id", &nccl_unique_id);
+  m.def("error_flag", &read_error_flag, py::arg("reset") = true);
+  m.def("num_sms", &num_sms);
+  m.attr("EPI_BF16") = (int)EPI_BF16;
+  m.attr("EPI_F32") = (int)EPI_F32;
+  m.attr("EPI_SILU") = (int)EPI_SILU;
+  m.attr("EPI_ADD") = (int)EPI_ADD;
+}

@@ -1,0 +1,395 @@
+#include "engine.h"
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include <cmath>
+#include <stdexcept>
+
+namespace kus {
+
+#define KUS_CHECK(cond, msg)                                        \
+  do {                                                              \
+    if (!(cond)) throw std::runtime_error(std::string("kus: ") + msg); \
+  } while (0)
+
+static void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+static void check_nccl(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Byte layout of one layer segment: in_norm, post_norm, qkv, o, gu (interleaved), down.
+struct LayerLayout {
+  size_t in_norm, post_norm, qkv, o, gu, down, total;
+  LayerLayout(const EngineShape& s, int f_pad, int qkv_n) {
+    size_t off = 0;
+    auto put = [&](size_t elems) {
+      size_t at = off;
+      off = align256(off + elems * 2);
+      return at;
+    };
+    in_norm = put(s.hidden);
+    post_norm = put(s.hidden);
+    qkv = put((size_t)qkv_n * s.hidden);
+    o = put((size_t)s.hidden * s.nq * s.hd);
+    gu = put((size_t)2 * f_pad * s.hidden);
+    down = put((size_t)s.hidden * f_pad);
+    total = off;
+  }
+};
+
+Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
+  KUS_CHECK(s.hd == 128, "the attention kernel needs head_dim 128");
+  KUS_CHECK(s.hidden % 64 == 0, "hidden size must be a multiple of 64");
+  KUS_CHECK(s.nq % s.nkv == 0, "query heads must be a multiple of KV heads");
+  f_pad_ = (s.ffn + 127) / 128 * 128;
+  qkv_n_ = (s.nq + 2 * s.nkv) * s.hd;
+  c10::cuda::CUDAGuard g(device_);
+  auto bf = torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, device_);
+  auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA, device_);
+  auto i32 = torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, device_);
+  const int64_t T = s.max_tokens, B = s.max_batch;
+  h_ = torch::empty({T, s.hidden}, bf);
+  y_ = torch::empty({T, s.hidden}, bf);
+  qkv_ = torch::empty({T, qkv_n_}, bf);
+  attn_ = torch::empty({T, (int64_t)s.nq * s.hd}, bf);
+  act_ = torch::empty({T, f_pad_}, bf);
+  tmp_ = torch::empty({T, s.hidden}, bf);
+  ylast_ = torch::zeros({std::max<int64_t>(B, 128), s.hidden}, bf);
+  logits_ = torch::empty({B, s.vocab}, f32);
+  // split-K workspace: enough for the largest decode GEMM split
+  const int64_t ws_floats = (int64_t)148 * 16 * 128 * 256;
+  gemm_ws_ = torch::empty({ws_floats}, f32);
+  counters_ = torch::zeros({1 << 16}, i32);
+  attn_split_tokens_ = std::min<int64_t>(T, 512);
+  attn_o_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * s.hd}, f32);
+  attn_ml_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * 2}, f32);
+  const int64_t max_items = T * std::max(1, s.nq / s.nkv) / 64 + B + 1;
+  const int64_t meta_ints = 2 * max_items + 4 * T + 5 * B + 1 +
+                            B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + 64;
+  meta_dev_ = torch::empty({meta_ints}, i32);
+  tokens_dev_ = torch::empty({B}, i32);
+  tokens_host_ = torch::empty({B}, torch::TensorOptions().dtype(torch::kInt32).pinned_memory(true));
+  // RoPE table: [max_pos, hd] = cos (hd/2) then sin (hd/2), computed in double
+  auto cs = torch::empty({s.max_pos, s.hd}, torch::kFloat32);
+  float* p = cs.data_ptr<float>();
+  const int half = s.hd / 2;
+  for (int pos = 0; pos < s.max_pos; ++pos)
+    for (int i = 0; i < half; ++i) {
+      const double inv = std::pow(s.rope_theta, -2.0 * i / s.hd);
+      const double a = pos * inv;
+      p[(size_t)pos * s.hd + i] = (float)std::cos(a);
+      p[(size_t)pos * s.hd + half + i] = (float)std::sin(a);
+    }
+  cos_sin_ = cs.to(torch::Device(torch::kCUDA, device_));
+  embed_ = torch::empty({s.vocab, s.hidden}, bf);
+  final_norm_ = torch::ones({s.hidden}, bf);
+  lm_head_ = torch::empty({s.vocab, s.hidden}, bf);
+  KUS_CHECK(make_tmap_bf16(&m_y_, y_.data_ptr(), T, s.hidden, s.hidden, 128), "tmap y");
+  KUS_CHECK(make_tmap_bf16(&m_attn_, attn_.data_ptr(), T, s.nq * s.hd, s.nq * s.hd, 128), "tmap attn");
+  KUS_CHECK(make_tmap_bf16(&m_act_, act_.data_ptr(), T, f_pad_, f_pad_, 128), "tmap act");
+  KUS_CHECK(make_tmap_bf16(&m_ylast_, ylast_.data_ptr(), ylast_.size(0), s.hidden, s.hidden, 128), "tmap ylast");
+  KUS_CHECK(make_tmap_bf16(&m_lm_head_, lm_head_.data_ptr(), s.vocab, s.hidden, s.hidden, 256), "tmap lm_head");
+}
+
+Engine::~Engine() {
+  if (tp_comm_) ncclCommDestroy(tp_comm_);
+}
+
+int64_t Engine::layer_slot_bytes() const { return 2LL * s_.block_size * s_.nkv * s_.hd * 2; }
+int64_t Engine::page_bytes() const { return layer_slot_bytes() * s_.layers; }
+int64_t Engine::layer_weight_bytes() const { return (int64_t)LayerLayout(s_, f_pad_, qkv_n_).total; }
+
+void Engine::init_memory(int64_t num_pages) {
+  c10::cuda::CUDAGuard g(device_);
+  num_pages_ = num_pages;
+  LayerLayout ll(s_, f_pad_, qkv_n_);
+  std::vector<size_t> lb(s_.layers, ll.total);
+  arena_ = std::make_unique<Arena>(device_, lb, (size_t)num_pages * page_bytes(), true);
+  layers_.resize(s_.layers);
+  for (int l = 0; l < s_.layers; ++l) {
+    char* base = arena_->layer_ptr(l);
+    LayerW& w = layers_[l];
+    w.in_norm = reinterpret_cast<__nv_bfloat16*>(base + ll.in_norm);
+    w.post_norm = reinterpret_cast<__nv_bfloat16*>(base + ll.post_norm);
+    w.qkv = reinterpret_cast<__nv_bfloat16*>(base + ll.qkv);
+    w.o = reinterpret_cast<__nv_bfloat16*>(base + ll.o);
+    w.gu = reinterpret_cast<__nv_bfloat16*>(base + ll.gu);
+    w.down = reinterpret_cast<__nv_bfloat16*>(base + ll.down);
+    build_layer_maps(l);
+  }
+  check_cuda(cudaMemset(arena_->kv_base(), 0, arena_->kv_phys_bytes()), "zero kv");
+}
+
+void Engine::build_layer_maps(int l) {
+  LayerW& w = layers_[l];
+  const int H = s_.hidden;
+  KUS_CHECK(make_tmap_bf16(&w.m_qkv, w.qkv, qkv_n_, H, H, 256), "tmap qkv");
+  KUS_CHECK(make_tmap_bf16(&w.m_o, w.o, H, s_.nq * s_.hd, s_.nq * s_.hd, 256), "tmap o");
+  KUS_CHECK(make_tmap_bf16(&w.m_gu, w.gu, 2 * f_pad_, H, H, 256), "tmap gu");
+  KUS_CHECK(make_tmap_bf16(&w.m_down, w.down, H, f_pad_, f_pad_, 256), "tmap down");
+}
+
+static torch::Tensor dev_view(void* p, std::vector<int64_t> shape, int device) {
+  return torch::from_blob(p, shape, torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, device));
+}
+
+void Engine::load_layer(int l, const std::vector<torch::Tensor>& w) {
+  KUS_CHECK(l >= 0 && l < s_.layers && w.size() == 6, "load_layer arguments");
+  c10::cuda::CUDAGuard g(device_);
+  const LayerW& L = layers_[l];
+  const int H = s_.hidden, F = s_.ffn;
+  auto dev = torch::Device(torch::kCUDA, device_);
+  auto cvt = [&](const torch::Tensor& t) { return t.to(dev, torch::kBFloat16).contiguous(); };
+  dev_view(L.in_norm, {H}, device_).copy_(cvt(w[0]));
+  dev_view(L.qkv, {qkv_n_, H}, device_).copy_(cvt(w[1]));
+  dev_view(L.o, {H, s_.nq * s_.hd}, device_).copy_(cvt(w[2]));
+  dev_view(L.post_norm, {H}, device_).copy_(cvt(w[3]));
+  // gate/up: [gate (F); up (F)] -> per 128 features: 128 gate rows, 128 up rows
+  auto gu = cvt(w[4]);
+  auto gate = torch::zeros({f_pad_, H}, gu.options());
+  auto up = torch::zeros({f_pad_, H}, gu.options());
+  gate.narrow(0, 0, F).copy_(gu.narrow(0, 0, F));
+  up.narrow(0, 0, F).copy_(gu.narrow(0, F, F));
+  auto inter = torch::stack({gate.view({f_pad_ / 128, 128, H}), up.view({f_pad_ / 128, 128, H})}, 1);
+  dev_view(L.gu, {2 * f_pad_, H}, device_).copy_(inter.reshape({2 * f_pad_, H}));
+  auto down = torch::zeros({H, f_pad_}, gu.options());
+  down.narrow(1, 0, F).copy_(cvt(w[5]));
+  dev_view(L.down, {H, f_pad_}, device_).copy_(down);
+}
+
+void Engine::load_globals(torch::Tensor embed, torch::Tensor final_norm, torch::Tensor lm_head) {
+  c10::cuda::CUDAGuard g(device_);
+  embed_.copy_(embed.to(embed_.device(), torch::kBFloat16));
+  final_norm_.copy_(final_norm.to(final_norm_.device(), torch::kBFloat16));
+  lm_head_.copy_(lm_head.to(lm_head_.device(), torch::kBFloat16));
+}
+
+void Engine::random_init_layers(const std::vector<int64_t>& layers, int64_t seed, double stdv) {
+  c10::cuda::CUDAGuard g(device_);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(device_);
+  const int H = s_.hidden;
+  for (int64_t l : layers) {
+    const LayerW& L = layers_[l];
+    const uint64_t sd = (uint64_t)seed * 1000003ull + (uint64_t)l * 7919ull;
+    fill_value_bf16(L.in_norm, H, 1.f, st);
+    fill_value_bf16(L.post_norm, H, 1.f, st);
+    fill_normal_bf16(L.qkv, (long long)qkv_n_ * H, sd + 1, (float)stdv, st);
+    fill_normal_bf16(L.o, (long long)H * s_.nq * s_.hd, sd + 2, (float)stdv, st);
+    fill_normal_bf16(L.gu, 2LL * f_pad_ * H, sd + 3, (float)stdv, st);
+    fill_normal_bf16(L.down, (long long)H * f_pad_, sd + 4, (float)stdv, st);
+  }
+}
+
+void Engine::random_init(int64_t seed, double stdv) {
+  std::vector<int64_t> all;
+  for (int l = 0; l < s_.layers; ++l) all.push_back(l);
+  random_init_layers(all, seed, stdv);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(device_);
+  fill_normal_bf16(reinterpret_cast<__nv_bfloat16*>(embed_.data_ptr()), embed_.numel(), seed * 31 + 5, (float)stdv, st);
+  fill_normal_bf16(reinterpret_cast<__nv_bfloat16*>(lm_head_.data_ptr()), lm_head_.numel(), seed * 31 + 6, (float)stdv,
+                   st);
+  fill_value_bf16(reinterpret_cast<__nv_bfloat16*>(final_norm_.data_ptr()), s_.hidden, 1.f, st);
+}
+
+torch::Tensor Engine::layer_bytes_view(int l) {
+  return torch::from_blob(arena_->layer_ptr(l), {(int64_t)arena_->layer_bytes(l)},
+                          torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device_));
+}
+
+torch::Tensor Engine::hidden() { return h_; }
+torch::Tensor Engine::logits() { return logits_; }
+
+void Engine::gemm(const CUtensorMap& mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
+                  const __nv_bfloat16* res, cudaStream_t st) {
+  GemmPlan p = plan_gemm(M, N, K, epi, 256, 16);
+  const size_t need = workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn);
+  while (p.args.split_k > 1 && (need > (size_t)gemm_ws_.numel() || p.args.m_tiles * p.args.n_tiles > counters_.numel())) {
+    p = plan_gemm(M, N, K, epi, 256, p.args.split_k - 1);
+    if (workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn) <= (size_t)gemm_ws_.numel()) break;
+  }
+  p.tmA = mA;
+  p.tmB = mB;
+  p.args.out = out;
+  p.args.ldc = ldc;
+  p.args.residual = res;
+  p.args.ld_res = ldc;
+  p.args.workspace = gemm_ws_.data_ptr<float>();
+  p.args.tile_counters = counters_.data_ptr<int>();
+  run_gemm(p, st);
+  ++launches_;
+}
+
+void Engine::all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t st) {
+  check_nccl(ncclAllReduce(buf, buf, n, ncclBfloat16, ncclSum, tp_comm_, st), "ncclAllReduce");
+}
+
+std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, int64_t max_pages, int64_t n_items,
+                                     int64_t splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
+                                     bool first_stage, bool last_stage, int64_t sample_mode, int64_t step) {
+  c10::cuda::CUDAGuard g(device_);
+  KUS_CHECK(T > 0 && T <= s_.max_tokens, "step tokens exceed max_tokens");
+  KUS_CHECK(B > 0 && B <= s_.max_batch, "step requests exceed max_batch");
+  KUS_CHECK(layer_start >= 0 && layer_end <= s_.layers && layer_start < layer_end, "bad layer slice");
+  KUS_CHECK(splits >= 1 && splits <= attn_max_splits_, "bad attention split");
+  KUS_CHECK(splits == 1 || T <= attn_split_tokens_, "split attention only for small steps");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(device_);
+  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 2 * B;
+  KUS_CHECK(meta.numel() >= n_meta && n_meta <= meta_dev_.numel(), "meta buffer too small");
+  check_cuda(cudaMemcpyAsync(meta_dev_.data_ptr(), meta.data_ptr(), n_meta * 4, cudaMemcpyHostToDevice, st), "meta H2D");
+  // meta layout (int32): items[2n] | tokens[T] | positions[T] | kv_page[T] | kv_slot[T] |
+  // q_start[B+1] | ctx_len[B] | last_idx[B] | page_table[B*max_pages] | temps[B] (f32) | seeds[B]
+  const int* m = meta_dev_.data_ptr<int>();
+  const int2* items = reinterpret_cast<const int2*>(m);
+  const int* tokens = m + 2 * n_items;
+  const int* positions = tokens + T;
+  const int* kv_page = positions + T;
+  const int* kv_slot = kv_page + T;
+  const int* q_start = kv_slot + T;
+  const int* ctx_len = q_start + B + 1;
+  const int* last_idx = ctx_len + B;
+  const int* table = last_idx + B;
+  const float* temps = reinterpret_cast<const float*>(table + B * max_pages);
+  const unsigned* seeds = reinterpret_cast<const unsigned*>(temps + B);
+
+  KVGeom geo;
+  geo.base = arena_->kv_base();
+  geo.P = (int)num_pages_;
+  geo.N = (int)fusion_size;
+  geo.Ls = (int)(layer_end - layer_start);
+  geo.page_stride = page_bytes();
+  geo.layer_stride = layer_slot_bytes();
+  geo.block_size = s_.block_size;
+  geo.kvh = s_.nkv;
+  geo.hd = s_.hd;
+
+  AttnBatch ab;
+  ab.q_start = q_start;
+  ab.ctx_len = ctx_len;
+  ab.page_table = table;
+  ab.max_pages = (int)max_pages;
+  ab.items = items;
+  ab.n_items = (int)n_items;
+  ab.splits = (int)splits;
+  AttnScratch sc{attn_o_.data_ptr<float>(), attn_ml_.data_ptr<float>()};
+
+  const int H = s_.hidden;
+  auto* h = reinterpret_cast<__nv_bfloat16*>(h_.data_ptr());
+  auto* y = reinterpret_cast<__nv_bfloat16*>(y_.data_ptr());
+  auto* qkv = reinterpret_cast<__nv_bfloat16*>(qkv_.data_ptr());
+  auto* attn = reinterpret_cast<__nv_bfloat16*>(attn_.data_ptr());
+  auto* act = reinterpret_cast<__nv_bfloat16*>(act_.data_ptr());
+  auto* tmp = reinterpret_cast<__nv_bfloat16*>(tmp_.data_ptr());
+  const bool tp = s_.tp > 1;
+  const float scale = 1.0f / std::sqrt((float)s_.hd);
+  const auto& dropped = arena_->dropped();
+
+  if (first_stage) {
+    embed(tokens, reinterpret_cast<const __nv_bfloat16*>(embed_.data_ptr()), h, (int)T, H, s_.vocab, st);
+    ++launches_;
+  }
+  bool pending = false;   // tmp holds an all-reduced partial still to be added to h
+  for (int64_t l = layer_start; l < layer_end; ++l) {
+    for (int d : dropped) KUS_CHECK(d != l, "step touches a dropped layer");
+    const LayerW& W = layers_[l];
+    const int ll = (int)(l - layer_start);
+    rmsnorm(h, pending ? tmp : nullptr, W.in_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+    gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
+    rope_append(qkv, positions, kv_page, kv_slot, cos_sin_.data_ptr<float>(), geo, ll, (int)T, s_.nq, s_.nkv,
+                s_.max_pos, st);
+    paged_attention(qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
+    launches_ += 3 + (splits > 1 ? 1 : 0);
+    if (tp) {
+      gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_BF16, tmp, H, nullptr, st);
+      all_reduce(tmp, T * H, st);
+      rmsnorm(h, tmp, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+    } else {
+      gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_ADD, h, H, h, st);
+      rmsnorm(h, nullptr, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+    }
+    ++launches_;
+    gemm(m_y_, W.m_gu, (int)T, 2 * f_pad_, H, EPI_SILU, act, f_pad_, nullptr, st);
+    if (tp) {
+      gemm(m_act_, W.m_down, (int)T, H, f_pad_, EPI_BF16, tmp, H, nullptr, st);
+      all_reduce(tmp, T * H, st);
+      pending = true;
+    } else {
+      gemm(m_act_, W.m_down, (int)T, H, f_pad_, EPI_ADD, h, H, h, st);
+      pending = false;
+    }
+  }
+  if (pending) {
+    add_inplace(h, tmp, T * H, st);
+    ++launches_;
+  }
+  std::vector<int64_t> out;
+  if (!last_stage) return out;
+  auto* yl = reinterpret_cast<__nv_bfloat16*>(ylast_.data_ptr());
+  rmsnorm(h, nullptr, reinterpret_cast<const __nv_bfloat16*>(final_norm_.data_ptr()), yl, last_idx, (int)B, H,
+          (float)s_.eps, st);
+  ++launches_;
+  gemm(m_ylast_, m_lm_head_, (int)B, s_.vocab, H, EPI_F32, logits_.data_ptr(), s_.vocab, nullptr, st);
+  if (sample_mode == 1) return out;   // caller samples from logits()
+  sample(logits_.data_ptr<float>(), (int)B, s_.vocab, s_.vocab, temps, seeds, (unsigned long long)step,
+         tokens_dev_.data_ptr<int>(), st);
+  ++launches_;
+  check_cuda(cudaMemcpyAsync(tokens_host_.data_ptr(), tokens_dev_.data_ptr(), B * 4, cudaMemcpyDeviceToHost, st),
+             "tokens D2H");
+  check_cuda(cudaStreamSynchronize(st), "step sync");
+  const int* th = tokens_host_.data_ptr<int>();
+  out.assign(th, th + B);
+  return out;
+}
+
+int64_t Engine::drop_layers(const std::vector<int64_t>& layers) {
+  std::vector<int> ls(layers.begin(), layers.end());
+  return (int64_t)arena_->drop_layers(ls);
+}
+
+std::vector<int64_t> Engine::restore_layers() {
+  auto r = arena_->restore_layers();
+  for (int l : r) build_layer_maps(l);
+  return std::vector<int64_t>(r.begin(), r.end());
+}
+
+std::vector<int64_t> Engine::dropped() const {
+  const auto& d = arena_->dropped();
+  return std::vector<int64_t>(d.begin(), d.end());
+}
+
+void Engine::copy_chunks(int64_t dst_ptr, int64_t src_ptr, torch::Tensor dst_off, torch::Tensor src_off,
+                         int64_t chunk_bytes, int64_t max_blocks) {
+  c10::cuda::CUDAGuard g(device_);
+  KUS_CHECK(chunk_bytes % 16 == 0, "chunk must be a multiple of 16 bytes");
+  KUS_CHECK(dst_off.is_cuda() && src_off.is_cuda() && dst_off.numel() == src_off.numel(), "offset tensors");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(device_);
+  kus::copy_chunks(reinterpret_cast<void*>(dst_ptr), reinterpret_cast<const void*>(src_ptr),
+                   reinterpret_cast<const long long*>(dst_off.data_ptr<int64_t>()),
+                   reinterpret_cast<const long long*>(src_off.data_ptr<int64_t>()), (int)dst_off.numel(), chunk_bytes,
+                   (int)max_blocks, st);
+  ++launches_;
+}
+
+void Engine::init_tp_comm(const std::vector<int64_t>& uid, int64_t rank, int64_t size) {
+  c10::cuda::CUDAGuard g(device_);
+  ncclUniqueId id;
+  KUS_CHECK(uid.size() == sizeof(id.internal), "nccl unique id size");
+  for (size_t i = 0; i < uid.size(); ++i) id.internal[i] = (char)uid[i];
+  check_nccl(ncclCommInitRank(&tp_comm_, (int)size, id, (int)rank), "ncclCommInitRank");
+}
+
+std::vector<int64_t> nccl_unique_id() {
+  ncclUniqueId id;
+  check_nccl(ncclGetUniqueId(&id), "ncclGetUniqueId");
+  std::vector<int64_t> out(sizeof(id.internal));
+  for (size_t i = 0; i < out.size(); ++i) out[i] = (int64_t)(unsigned char)id.internal[i];
+  return out;
+}
+
+int64_t read_error_flag(bool reset) { return error_flag(reset); }
+
+}  // namespace kus

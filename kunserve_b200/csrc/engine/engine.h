@@ -1,0 +1,119 @@
+// The native Llama engine (the B200 counterpart of the reference's
+// torch.classes.gpt_ops.LlamaOp, kunserve/models.py:52-65).
+//
+// Owns this rank's decoder-layer weights and paged KV pool in a VMM arena,
+// the replicated embedding / final norm / LM head, all step workspaces and
+// precomputed TMA descriptors, and runs one step over a layer slice:
+// embedding (first stage) -> per layer [RMSNorm -> QKV GEMM -> RoPE + KV
+// append -> paged attention -> O GEMM (+residual, or + TP all-reduce) ->
+// RMSNorm -> gate/up GEMM with fused SiLU*up -> down GEMM (+residual)] ->
+// final norm + LM head + sampling (last stage).
+#pragma once
+#include <torch/extension.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../kernels/gemm.h"
+#include "../kernels/kernels.h"
+#include "arena.h"
+
+#include <nccl.h>
+
+namespace kus {
+
+struct EngineShape {
+  int layers;      // decoder layers on this pipeline stage
+  int nq, nkv, hd;
+  int hidden, ffn, vocab;
+  int max_tokens, max_batch, max_pos;
+  int block_size;
+  double eps, rope_theta;
+  int tp;
+};
+
+struct LayerW {
+  __nv_bfloat16 *in_norm, *post_norm, *qkv, *o, *gu, *down;
+  CUtensorMap m_qkv, m_o, m_gu, m_down;
+};
+
+class Engine {
+ public:
+  explicit Engine(const EngineShape& s, int device);
+  ~Engine();
+
+  // Allocate the arena: weights of every layer + `num_pages` KV pages.
+  void init_memory(int64_t num_pages);
+  int64_t num_pages() const { return num_pages_; }
+  int64_t page_bytes() const;
+  int64_t layer_slot_bytes() const;
+  int64_t layer_weight_bytes() const;
+  int64_t kv_base_ptr() const { return reinterpret_cast<int64_t>(arena_->kv_base()); }
+
+  // Weights.  Layer tensors use the Python layout (w_gate_up = [gate; up]);
+  // the engine interleaves gate/up per 128 rows and pads F to 128.
+  void load_layer(int l, const std::vector<torch::Tensor>& w);   // in_norm, w_qkv, w_o, post_norm, w_gate_up, w_down
+  void load_globals(torch::Tensor embed, torch::Tensor final_norm, torch::Tensor lm_head);
+  void random_init(int64_t seed, double std);
+  void random_init_layers(const std::vector<int64_t>& layers, int64_t seed, double std);
+  torch::Tensor layer_bytes_view(int l);   // raw bytes of a layer segment (uint8)
+
+  // One step.  `meta` is a pinned int32 tensor laid out by the Python runner
+  // (see native_runner.py); returns sampled ids on the last stage.
+  std::vector<int64_t> forward(torch::Tensor meta, int64_t T, int64_t B, int64_t max_pages, int64_t n_items,
+                               int64_t splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
+                               bool first_stage, bool last_stage, int64_t sample_mode, int64_t step);
+  torch::Tensor hidden();                   // [max_tokens, H] residual stream (PP transfer)
+  torch::Tensor logits();                   // [max_batch, V] fp32
+
+  // Parameter drop / restore (balloon).
+  int64_t drop_layers(const std::vector<int64_t>& layers);   // returns contiguous extend bytes
+  std::vector<int64_t> restore_layers();
+  std::vector<int64_t> dropped() const;
+
+  // KV / parameter movement with the chunk-copy kernel.  src_ptr may be a
+  // peer mapping (in-kernel P2P pull over NVLink).
+  void copy_chunks(int64_t dst_ptr, int64_t src_ptr, torch::Tensor dst_off, torch::Tensor src_off,
+                   int64_t chunk_bytes, int64_t max_blocks);
+  int64_t export_kv_fd() const { return arena_->export_kv_fd(); }
+  int64_t export_layer_fd(int64_t l) const { return arena_->export_layer_fd((int)l); }
+  int64_t kv_phys_bytes() const { return (int64_t)arena_->kv_phys_bytes(); }
+  int64_t layer_segment_bytes(int64_t l) const { return (int64_t)arena_->layer_bytes((int)l); }
+  int64_t layer_ptr(int64_t l) const { return reinterpret_cast<int64_t>(arena_->layer_ptr((int)l)); }
+
+  // NCCL (tensor-parallel all-reduce inside the layer loop).
+  void init_tp_comm(const std::vector<int64_t>& unique_id, int64_t rank, int64_t size);
+
+  int64_t launches() const { return launches_; }
+  void reset_launches() { launches_ = 0; }
+
+ private:
+  void build_layer_maps(int l);
+  void gemm(const CUtensorMap& mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
+            const __nv_bfloat16* res, cudaStream_t s);
+  void all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t s);
+
+  EngineShape s_;
+  int device_;
+  int f_pad_;
+  int qkv_n_;
+  int64_t num_pages_ = 0;
+  std::unique_ptr<Arena> arena_;
+  std::vector<LayerW> layers_;
+  torch::Tensor embed_, final_norm_, lm_head_;
+  CUtensorMap m_lm_head_;
+  // workspaces
+  torch::Tensor h_, y_, qkv_, attn_, act_, tmp_, ylast_, logits_, gemm_ws_, counters_, attn_o_, attn_ml_,
+      meta_dev_, tokens_dev_, tokens_host_, cos_sin_;
+  CUtensorMap m_y_, m_attn_, m_act_, m_ylast_;
+  int64_t attn_split_tokens_ = 0;
+  int attn_max_splits_ = 16;
+  ncclComm_t tp_comm_ = nullptr;
+  int64_t launches_ = 0;
+};
+
+std::vector<int64_t> nccl_unique_id();
+int64_t read_error_flag(bool reset);
+
+}  // namespace kus

@@ -1,0 +1,23 @@
+// Single translation unit for every device kernel of the library, so that
+// the device error flag is one symbol shared by all kernels without
+// relocatable device code.
+#include "../common.cuh"
+
+#include "gemm_tcgen05.cu"
+#include "elementwise.cu"
+#include "attention.cu"
+#include "init.cu"
+
+namespace kus {
+long long error_flag(bool reset) {
+  int code = 0, info = 0;
+  cudaMemcpyFromSymbol(&code, g_kus_error, sizeof(int));
+  cudaMemcpyFromSymbol(&info, g_kus_error_info, sizeof(int));
+  if (reset) {
+    int zero = 0;
+    cudaMemcpyToSymbol(g_kus_error, &zero, sizeof(int));
+    cudaMemcpyToSymbol(g_kus_error_info, &zero, sizeof(int));
+  }
+  return (long long)code | ((long long)info << 8);
+}
+}  // namespace kus

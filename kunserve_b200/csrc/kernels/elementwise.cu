@@ -1,0 +1,272 @@
+// Memory-bound kernels of the Llama step: embedding gather, RMSNorm (with
+// optional fused residual add), RoPE + paged KV append, token sampling and the
+// chunk-copy kernel that performs every KV / parameter movement.
+//
+// All rows are processed with 16-byte vector loads/stores; hidden sizes and
+// head dims must be multiples of 8 elements (checked by the host wrappers).
+#include "../common.cuh"
+#include "kernels.h"
+
+namespace kus {
+
+// ------------------------------------------------------------- embedding
+__global__ void embed_kernel(const int* __restrict__ tokens, const __nv_bfloat16* __restrict__ table,
+                             __nv_bfloat16* __restrict__ out, int T, int H, int V) {
+  const int t = blockIdx.x;
+  int tok = tokens[t];
+  if (tok < 0 || tok >= V) {
+    set_error(kErrBounds, tok);
+    tok = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)tok * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + (size_t)t * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+void embed(const int* tokens, const __nv_bfloat16* table, __nv_bfloat16* out, int T, int H, int V,
+           cudaStream_t s) {
+  if (T <= 0) return;
+  embed_kernel<<<T, 128, 0, s>>>(tokens, table, out, T, H, V);
+}
+
+// --------------------------------------------------------------- RMSNorm
+// y[r] = (x[r] (+ add[r])) * rsqrt(mean(.^2) + eps) * w; with `add`, the sum is
+// also written back to x (residual stream update).  `rows` (optional) selects
+// the source row of output row r (used for the final norm of last tokens).
+template <int VPT>
+__global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ add,
+                               const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
+                               const int* __restrict__ rows, int H, float eps) {
+  const int r = blockIdx.x;
+  const int src = rows ? rows[r] : r;
+  uint4* xr = reinterpret_cast<uint4*>(x + (size_t)src * H);
+  const uint4* ar = add ? reinterpret_cast<const uint4*>(add + (size_t)src * H) : nullptr;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)r * H);
+  const int nv = H / 8;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < nv) {
+      unpack_bf16x8(xr[i], v[j]);
+      if (ar) {
+        float a[8];
+        unpack_bf16x8(ar[i], a);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[j][k] += a[k];
+        // round the residual stream to bf16 exactly as stored
+        uint4 packed = pack_bf16x8(v[j]);
+        xr[i] = packed;
+        unpack_bf16x8(packed, v[j]);
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += v[j][k] * v[j][k];
+    }
+  }
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)H + eps);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < nv) {
+      float g[8], o[8];
+      unpack_bf16x8(wr[i], g);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = v[j][k] * inv * g[k];
+      yr[i] = pack_bf16x8(o);
+    }
+  }
+}
+
+void rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* add, const __nv_bfloat16* w, __nv_bfloat16* y,
+             const int* rows, int R, int H, float eps, cudaStream_t s) {
+  if (R <= 0) return;
+  const int nv = H / 8;
+  int threads = nv >= 256 ? 256 : ((nv + 31) / 32) * 32;
+  const int vpt = (nv + threads - 1) / threads;
+  if (vpt <= 1)
+    rmsnorm_kernel<1><<<R, threads, 0, s>>>(x, add, w, y, rows, H, eps);
+  else if (vpt <= 2)
+    rmsnorm_kernel<2><<<R, threads, 0, s>>>(x, add, w, y, rows, H, eps);
+  else if (vpt <= 4)
+    rmsnorm_kernel<4><<<R, threads, 0, s>>>(x, add, w, y, rows, H, eps);
+  else
+    rmsnorm_kernel<8><<<R, 1024 / 4, 0, s>>>(x, add, w, y, rows, H, eps);
+}
+
+// ----------------------------------------------------- RoPE + KV append
+// qkv: [T, (nq + 2*nkv) * hd] bf16.  q heads are rotated in place; k heads are
+// rotated and written, v heads copied, into the paged pool at (page, slot)
+// of each token.  cos_sin: [max_pos, hd] fp32, first hd/2 cos then hd/2 sin.
+__global__ void rope_append_kernel(__nv_bfloat16* __restrict__ qkv, const int* __restrict__ positions,
+                                   const int* __restrict__ pages, const int* __restrict__ slots,
+                                   const float* __restrict__ cos_sin, KVGeom g, int layer, int nq, int nkv,
+                                   int max_pos) {
+  const int t = blockIdx.x;
+  const int hd = g.hd;
+  const int half = hd / 2;
+  int pos = positions[t];
+  if (pos < 0 || pos >= max_pos) {
+    set_error(kErrBounds, pos);
+    pos = 0;
+  }
+  const float* cs = cos_sin + (size_t)pos * hd;
+  const int warps = blockDim.x / 32, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __nv_bfloat16* row = qkv + (size_t)t * (nq + 2 * nkv) * hd;
+  const int page = pages[t], slot = slots[t];
+  for (int h = warp; h < nq + 2 * nkv; h += warps) {
+    __nv_bfloat16* src = row + h * hd;
+    if (h < nq + nkv) {
+      __nv_bfloat16* dst = h < nq ? src : kv_ptr(g, page, layer, false) + ((size_t)slot * g.kvh + (h - nq)) * hd;
+      for (int i = lane; i < half; i += 32) {
+        const float c = cs[i], s = cs[half + i];
+        const float x1 = bf2f(src[i]), x2 = bf2f(src[i + half]);
+        dst[i] = f2bf(x1 * c - x2 * s);
+        dst[i + half] = f2bf(x2 * c + x1 * s);
+      }
+    } else {
+      __nv_bfloat16* dst = kv_ptr(g, page, layer, true) + ((size_t)slot * g.kvh + (h - nq - nkv)) * hd;
+      const uint4* s4 = reinterpret_cast<const uint4*>(src);
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      for (int i = lane; i < hd / 8; i += 32) d4[i] = s4[i];
+    }
+  }
+}
+
+void rope_append(__nv_bfloat16* qkv, const int* positions, const int* pages, const int* slots,
+                 const float* cos_sin, const KVGeom& g, int layer, int T, int nq, int nkv, int max_pos,
+                 cudaStream_t s) {
+  if (T <= 0) return;
+  rope_append_kernel<<<T, 256, 0, s>>>(qkv, positions, pages, slots, cos_sin, g, layer, nq, nkv, max_pos);
+}
+
+// -------------------------------------------------------------- sampling
+// Per-row argmax of fp32 logits; rows with temperature > 0 add Gumbel noise
+// (Gumbel-max trick: argmax(l/T + G) ~ softmax(l/T)).  The noise comes from a
+// SplitMix64 hash of (seed, step, index), so a request's sample stream does
+// not depend on batch composition.
+KUS_DEVICE uint64_t splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void sample_kernel(const float* __restrict__ logits, int V, int ld, const float* __restrict__ temp,
+                              const unsigned* __restrict__ seeds, unsigned long long step,
+                              int* __restrict__ out) {
+  const int r = blockIdx.x;
+  const float* row = logits + (size_t)r * ld;
+  const float t = temp ? temp[r] : 0.f;
+  const bool noisy = t > 1e-5f;
+  const float invt = noisy ? 1.f / t : 1.f;
+  const uint64_t base = noisy ? splitmix64((uint64_t)seeds[r] ^ splitmix64(step)) : 0;
+  float best = -INFINITY;
+  int arg = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    float v = row[i];
+    if (noisy) {
+      const uint64_t h = splitmix64(base + (uint64_t)i);
+      // uniform in (0, 1): 24 random bits, offset by half a step
+      const float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+      v = v * invt - logf(-logf(u));
+    }
+    if (v > best || (v == best && i < arg)) {
+      best = v;
+      arg = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oa = __shfl_xor_sync(0xffffffffu, arg, o);
+    if (ob > best || (ob == best && oa < arg)) {
+      best = ob;
+      arg = oa;
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int sa[32];
+  if ((threadIdx.x & 31) == 0) {
+    sb[threadIdx.x >> 5] = best;
+    sa[threadIdx.x >> 5] = arg;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (sb[w] > best || (sb[w] == best && sa[w] < arg)) {
+        best = sb[w];
+        arg = sa[w];
+      }
+    out[r] = arg;
+  }
+}
+
+void sample(const float* logits, int B, int V, int ld, const float* temp, const unsigned* seeds,
+            unsigned long long step, int* out, cudaStream_t s) {
+  if (B <= 0) return;
+  sample_kernel<<<B, 1024, 0, s>>>(logits, V, ld, temp, seeds, step, out);
+}
+
+// ------------------------------------------------------------ chunk copy
+// dst_base + dst_off[i] <- src_base + src_off[i], `chunk` bytes each (multiple
+// of 16).  src_base may be a peer GPU's buffer mapped into this context: the
+// kernel then pulls over NVLink with plain 16-byte loads.
+__global__ void copy_chunks_kernel(uint8_t* __restrict__ dst_base, const uint8_t* __restrict__ src_base,
+                                   const long long* __restrict__ dst_off, const long long* __restrict__ src_off,
+                                   int n, long long chunk) {
+  const long long vec_per_chunk = chunk / 16;
+  const long long total = vec_per_chunk * n;
+  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total;
+       v += (long long)gridDim.x * blockDim.x) {
+    const long long c = v / vec_per_chunk, k = v - c * vec_per_chunk;
+    const uint4* s = reinterpret_cast<const uint4*>(src_base + src_off[c]) + k;
+    uint4* d = reinterpret_cast<uint4*>(dst_base + dst_off[c]) + k;
+    *d = __ldcs(s);
+  }
+}
+
+void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off, const long long* src_off, int n,
+                 long long chunk, int max_blocks, cudaStream_t s) {
+  if (n <= 0) return;
+  const long long vecs = chunk / 16 * n;
+  long long blocks = (vecs + 255) / 256;
+  if (blocks > max_blocks) blocks = max_blocks;
+  copy_chunks_kernel<<<(int)blocks, 256, 0, s>>>(reinterpret_cast<uint8_t*>(dst_base),
+                                                 reinterpret_cast<const uint8_t*>(src_base), dst_off, src_off, n,
+                                                 chunk);
+}
+
+// -------------------------------------------------- residual add (TP path)
+__global__ void add_inplace_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y, long long n8) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {
+    float a[8], b[8];
+    uint4* xp = reinterpret_cast<uint4*>(x) + i;
+    unpack_bf16x8(*xp, a);
+    unpack_bf16x8(reinterpret_cast<const uint4*>(y)[i], b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] += b[k];
+    *xp = pack_bf16x8(a);
+  }
+}
+
+void add_inplace(__nv_bfloat16* x, const __nv_bfloat16* y, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  long long n8 = n / 8;
+  int blocks = (int)((n8 + 255) / 256);
+  if (blocks > 4 * 148) blocks = 4 * 148;
+  add_inplace_kernel<<<blocks, 256, 0, s>>>(x, y, n8);
+}
+
+}  // namespace kus

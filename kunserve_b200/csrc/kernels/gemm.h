@@ -1,0 +1,47 @@
+// Host interface of the tcgen05 GEMM (gemm_tcgen05.cu).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace kus {
+
+enum GemmEpilogue : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SILU = 2, EPI_ADD = 3 };
+
+struct GemmArgs {
+  int M, N, K;
+  int m_tiles, n_tiles, split_k;
+  int n_out;            // output columns (N, or N/2 for EPI_SILU)
+  void* out;
+  int ldc;
+  const __nv_bfloat16* residual;
+  int ld_res;
+  float* workspace;     // split-K partial tiles, fp32 [tiles][split][128][BN]
+  int* tile_counters;   // one int per tile, zero between GEMMs
+};
+
+struct GemmPlan {
+  CUtensorMap tmA;
+  CUtensorMap tmB;
+  GemmArgs args;
+  int bn;
+  int epi;
+  int grid;
+};
+
+int num_sms();
+bool make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                    uint32_t box_rows);
+int choose_bn(int M, int N, int epi);
+// Tile counts and split-K factor for an M x N x K problem (bn <= 0: choose).
+GemmPlan plan_gemm(int M, int N, int K, int epi, int bn = 0, int max_split = 16);
+size_t workspace_floats(int m_tiles, int n_tiles, int split_k, int bn);
+// Bind operands.  a_rows / b_rows override the rows declared to TMA (0: M / N).
+bool finalize_plan(GemmPlan& p, const void* A, int lda, const void* B, int ldb, void* out, int ldc,
+                   const __nv_bfloat16* residual, int ld_res, float* workspace, int* counters,
+                   uint64_t a_rows = 0, uint64_t b_rows = 0);
+void run_gemm(const GemmPlan& p, cudaStream_t s);
+int gemm_smem_bytes(int bn);
+
+}  // namespace kus

@@ -1,0 +1,466 @@
+// Dense GEMM on the sm_100a tensor cores: C[M,N] = A[M,K] * B[N,K]^T.
+//
+// A (activations) and B (weights, nn.Linear layout) are bf16 and K-major.
+// Tiles of 128 x BN x 64 move global->shared with TMA (128-byte swizzle),
+// one elected thread issues tcgen05.mma (kind::f16, fp32 accumulate) into a
+// double-buffered TMEM accumulator, and four epilogue warps read TMEM back
+// with tcgen05.ld and apply the fused epilogue:
+//
+//   EPI_BF16   store bf16
+//   EPI_F32    store fp32 (logits)
+//   EPI_SILU   B rows are interleaved per tile (BN/2 gate rows, then the
+//              BN/2 matching up rows); store silu(gate) * up, N/2 columns
+//   EPI_ADD    store bf16(acc + residual) (residual may alias the output)
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
+// owner, warps 2-5 epilogue.  The grid is persistent (<= one CTA per SM) and
+// walks (tile, k-split) units.  With split-K each unit writes an fp32
+// partial tile to a workspace and bumps a per-tile counter; the CTA that
+// arrives last sums the partials and runs the epilogue, so no CTA ever waits
+// for another.  All mbarrier waits are bounded (common.cuh).
+#include "../common.cuh"
+#include "gemm.h"
+#include <cudaTypedefs.h>
+
+namespace kus {
+
+namespace gemm_impl {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr int kSmemBudget = 200 * 1024;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+KUS_DEVICE float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int EPI>
+KUS_DEVICE void store16(const GemmArgs& a, int row, int col, const float (&v)[16]) {
+  // col is the first of 16 consecutive output columns of this row
+  if (row >= a.M) return;
+  if (EPI == EPI_F32) {
+    float* out = reinterpret_cast<float*>(a.out) + (size_t)row * a.ldc + col;
+    if (col + 16 <= a.n_out) {
+#pragma unroll
+      for (int i = 0; i < 16; i += 4)
+        *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+      for (int i = 0; i < 16 && col + i < a.n_out; ++i) out[i] = v[i];
+    }
+    return;
+  }
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)row * a.ldc + col;
+  float w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) w[i] = v[i];
+  if (EPI == EPI_ADD) {
+    const __nv_bfloat16* res = a.residual + (size_t)row * a.ld_res + col;
+    if (col + 16 <= a.n_out) {
+      float r[8];
+      uint4 u0 = *reinterpret_cast<const uint4*>(res);
+      uint4 u1 = *reinterpret_cast<const uint4*>(res + 8);
+      unpack_bf16x8(u0, r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] += r[i];
+      unpack_bf16x8(u1, r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[8 + i] += r[i];
+    } else {
+      for (int i = 0; i < 16 && col + i < a.n_out; ++i) w[i] += bf2f(res[i]);
+    }
+  }
+  if (col + 16 <= a.n_out) {
+    float lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      lo[i] = w[i];
+      hi[i] = w[8 + i];
+    }
+    *reinterpret_cast<uint4*>(out) = pack_bf16x8(lo);
+    *reinterpret_cast<uint4*>(out + 8) = pack_bf16x8(hi);
+  } else {
+    for (int i = 0; i < 16 && col + i < a.n_out; ++i) out[i] = f2bf(w[i]);
+  }
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + C::kStages * C::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* tfull = empty + C::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* flag_smem = reinterpret_cast<int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  const int num_kb = (args.K + BK - 1) / BK;
+  const int S = args.split_k;
+  const int kbs = (num_kb + S - 1) / S;
+  const int tiles = args.m_tiles * args.n_tiles;
+  const int units = tiles * S;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_sync()) {
+      prefetch_tmap(&tmA);
+      prefetch_tmap(&tmB);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int tile = u / S, split = u % S;
+        const int m = tile % args.m_tiles, n = tile / args.m_tiles;
+        const int kb0 = split * kbs, kb1 = min(kb0 + kbs, num_kb);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+          tma_load_2d(smem_a + stage * C::kABytes, &tmA, &full[stage], kb * BK, m * BM);
+          tma_load_2d(smem_b + stage * C::kBBytes, &tmB, &full[stage], kb * BK, n * BN);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // drain: wait until the consumer released every stage we filled, so no
+      // TMA write can land after the CTA exits
+      for (int i = 0; i < C::kStages && ok; ++i) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) break;
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int split = u % S;
+        const int kb0 = split * kbs, kb1 = min(kb0 + kbs, num_kb);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, kErrWaitTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128(smem_u32(smem_a + stage * C::kABytes));
+          const uint64_t db = umma_desc_sw128(smem_u32(smem_b + stage * C::kBBytes));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // advance 16 bf16 = 32 bytes along K inside the swizzle atom
+            umma_f16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int r_in_tile = quarter * 32 + lane;
+    const int et = threadIdx.x - 64;   // 0..127
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    constexpr int kOutCols = (EPI == EPI_SILU) ? BN / 2 : BN;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int tile = u / S, split = u % S;
+      const int m = tile % args.m_tiles, n = tile / args.m_tiles;
+      const int row = m * BM + r_in_tile;
+      // A failed (timed-out) wait skips the work but keeps every thread on the
+      // same barrier sequence; once the error flag is set later waits fail fast.
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, kErrWaitTmemFull));
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+      const int col0 = n * kOutCols;
+      if (S == 1) {
+        if (ok && EPI == EPI_SILU) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 2; c += 16) {
+            float g[16], up[16], o[16];
+            tmem_ld16(taddr + c, g);
+            tmem_ld16(taddr + BN / 2 + c, up);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = silu(g[i]) * up[i];
+            store16<EPI_BF16>(args, row, col0 + c, o);
+          }
+        } else if (ok) {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            float v[16];
+            tmem_ld16(taddr + c, v);
+            store16<EPI>(args, row, col0 + c, v);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      } else {
+        // split-K: park the partial, the last split of the tile reduces
+        float* ws = args.workspace + ((size_t)tile * S + split) * (BM * BN);
+        if (ok) {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            float v[16];
+            tmem_ld16(taddr + c, v);
+            if (row < args.M) {
+              float* dst = ws + (size_t)r_in_tile * BN + c;
+#pragma unroll
+              for (int i = 0; i < 16; i += 4)
+                __stcg(reinterpret_cast<float4*>(dst + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        __threadfence();
+        named_barrier(1, 128);
+        if (et == 0) {
+          int last = 0;
+          if (!error_set()) {
+            const int prev = atomicAdd(&args.tile_counters[tile], 1);
+            last = (prev == S - 1);
+            if (last) args.tile_counters[tile] = 0;   // ready for the next GEMM
+          }
+          *flag_smem = last;
+        }
+        named_barrier(1, 128);
+        const int last = *flag_smem;
+        named_barrier(1, 128);   // flag_smem is rewritten by the next unit
+        if (last && row < args.M) {
+          __threadfence();
+          const float* base = args.workspace + (size_t)tile * S * (BM * BN) + (size_t)r_in_tile * BN;
+          if (EPI == EPI_SILU) {
+#pragma unroll 1
+            for (int c = 0; c < BN / 2; c += 16) {
+              float g[16] = {}, up[16] = {}, o[16];
+              for (int s = 0; s < S; ++s) {
+                const float* p = base + (size_t)s * (BM * BN);
+#pragma unroll
+                for (int i = 0; i < 16; i += 4) {
+                  float4 x = __ldcg(reinterpret_cast<const float4*>(p + c + i));
+                  float4 y = __ldcg(reinterpret_cast<const float4*>(p + BN / 2 + c + i));
+                  g[i] += x.x; g[i + 1] += x.y; g[i + 2] += x.z; g[i + 3] += x.w;
+                  up[i] += y.x; up[i + 1] += y.y; up[i + 2] += y.z; up[i + 3] += y.w;
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = silu(g[i]) * up[i];
+              store16<EPI_BF16>(args, row, col0 + c, o);
+            }
+          } else {
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+              float v[16] = {};
+              for (int s = 0; s < S; ++s) {
+                const float* p = base + (size_t)s * (BM * BN) + c;
+#pragma unroll
+                for (int i = 0; i < 16; i += 4) {
+                  float4 x = __ldcg(reinterpret_cast<const float4*>(p + i));
+                  v[i] += x.x; v[i + 1] += x.y; v[i + 2] += x.z; v[i + 3] += x.w;
+                }
+              }
+              store16<EPI>(args, row, col0 + c, v);
+            }
+          }
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
+}
+
+// -------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+template <int BN, int EPI>
+void launch(const GemmPlan& p, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    attr_set = true;
+  }
+  gemm_kernel<BN, EPI><<<p.grid, kThreads, C::kSmemBytes, stream>>>(p.tmA, p.tmB, p.args);
+}
+
+template <int EPI>
+void launch_bn(const GemmPlan& p, cudaStream_t s) {
+  switch (p.bn) {
+    case 64: launch<64, EPI>(p, s); break;
+    case 128: launch<128, EPI>(p, s); break;
+    default: launch<256, EPI>(p, s); break;
+  }
+}
+
+}  // namespace gemm_impl
+
+using namespace gemm_impl;
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+bool make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                    uint32_t box_rows) {
+  auto fn = get_encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int choose_bn(int M, int N, int epi) {
+  if (epi == EPI_SILU) return 256;   // weights are interleaved in 128-row halves
+  if (N >= 256) return 256;
+  if (N >= 128) return 128;
+  return 64;
+}
+
+size_t workspace_floats(int m_tiles, int n_tiles, int split_k, int bn) {
+  return split_k > 1 ? (size_t)m_tiles * n_tiles * split_k * BM * bn : 0;
+}
+
+GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, int max_split) {
+  GemmPlan p{};
+  p.bn = bn > 0 ? bn : choose_bn(M, N, epi);
+  p.epi = epi;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = (N + p.bn - 1) / p.bn;
+  const int num_kb = (K + BK - 1) / BK;
+  const int sms = num_sms();
+  int split = 1;
+  const int tiles = m_tiles * n_tiles;
+  if (tiles < sms && max_split > 1) {
+    split = sms / tiles;
+    split = split > max_split ? max_split : split;
+    const int min_kb_per_split = 4;
+    while (split > 1 && num_kb / split < min_kb_per_split) --split;
+    // every split must own at least one k-block
+    while (split > 1 && ((num_kb + split - 1) / split) * (split - 1) >= num_kb) --split;
+  }
+  p.args.M = M;
+  p.args.N = N;
+  p.args.K = K;
+  p.args.m_tiles = m_tiles;
+  p.args.n_tiles = n_tiles;
+  p.args.split_k = split;
+  p.args.n_out = epi == EPI_SILU ? N / 2 : N;
+  const int units = tiles * split;
+  p.grid = units < sms ? units : sms;
+  return p;
+}
+
+bool finalize_plan(GemmPlan& p, const void* A, int lda, const void* B, int ldb, void* out, int ldc,
+                   const __nv_bfloat16* residual, int ld_res, float* workspace, int* counters, uint64_t a_rows,
+                   uint64_t b_rows) {
+  p.args.out = out;
+  p.args.ldc = ldc;
+  p.args.residual = residual;
+  p.args.ld_res = ld_res;
+  p.args.workspace = workspace;
+  p.args.tile_counters = counters;
+  if (!make_tmap_bf16(&p.tmA, A, a_rows ? a_rows : (uint64_t)p.args.M, p.args.K, lda, BM)) return false;
+  if (!make_tmap_bf16(&p.tmB, B, b_rows ? b_rows : (uint64_t)p.args.N, p.args.K, ldb, p.bn)) return false;
+  return true;
+}
+
+void run_gemm(const GemmPlan& p, cudaStream_t s) {
+  if (p.args.M <= 0) return;
+  switch (p.epi) {
+    case EPI_F32: launch_bn<EPI_F32>(p, s); break;
+    case EPI_SILU: launch<256, EPI_SILU>(p, s); break;
+    case EPI_ADD: launch_bn<EPI_ADD>(p, s); break;
+    default: launch_bn<EPI_BF16>(p, s); break;
+  }
+}
+
+int gemm_smem_bytes(int bn) {
+  switch (bn) {
+    case 64: return Cfg<64>::kSmemBytes;
+    case 128: return Cfg<128>::kSmemBytes;
+    default: return Cfg<256>::kSmemBytes;
+  }
+}
+
+}  // namespace kus

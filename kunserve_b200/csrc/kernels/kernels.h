@@ -1,0 +1,81 @@
+// Host interface of the non-GEMM kernels and the paged KV geometry.
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace kus {
+
+// Geometry of a paged KV pool (see kunserve_b200/kv/layout.py).  Page id f
+// below N*P is slice f/P of physical page f%P; ids from N*P on are extend
+// pages of Ls layer slots placed right after the P base pages.
+struct KVGeom {
+  char* base;
+  int P;                  // physical base pages
+  int N;                  // fusion size (1 = unfused)
+  int Ls;                 // layer slots per slice (= layers / N)
+  long long page_stride;  // bytes per physical page (all layers)
+  long long layer_stride; // bytes per (page, layer) slot: K then V
+  int block_size;
+  int kvh;
+  int hd;
+};
+
+__host__ __device__ __forceinline__ long long kv_offset(const KVGeom& g, int page, int layer, bool v) {
+  long long off;
+  const int np = g.N * g.P;
+  if (page < np) {
+    off = (long long)(page % g.P) * g.page_stride + ((long long)(page / g.P) * g.Ls + layer) * g.layer_stride;
+  } else {
+    off = (long long)g.P * g.page_stride + ((long long)(page - np) * g.Ls + layer) * g.layer_stride;
+  }
+  return v ? off + g.layer_stride / 2 : off;
+}
+
+__host__ __device__ __forceinline__ __nv_bfloat16* kv_ptr(const KVGeom& g, int page, int layer, bool v) {
+  return reinterpret_cast<__nv_bfloat16*>(g.base + kv_offset(g, page, layer, v));
+}
+
+void embed(const int* tokens, const __nv_bfloat16* table, __nv_bfloat16* out, int T, int H, int V, cudaStream_t s);
+void rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* add, const __nv_bfloat16* w, __nv_bfloat16* y,
+             const int* rows, int R, int H, float eps, cudaStream_t s);
+void rope_append(__nv_bfloat16* qkv, const int* positions, const int* pages, const int* slots,
+                 const float* cos_sin, const KVGeom& g, int layer, int T, int nq, int nkv, int max_pos,
+                 cudaStream_t s);
+void sample(const float* logits, int B, int V, int ld, const float* temp, const unsigned* seeds,
+            unsigned long long step, int* out, cudaStream_t s);
+void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off, const long long* src_off, int n,
+                 long long chunk, int max_blocks, cudaStream_t s);
+void add_inplace(__nv_bfloat16* x, const __nv_bfloat16* y, long long n, cudaStream_t s);
+
+// Paged attention over a ragged batch (prefill chunks and decodes mixed).
+struct AttnBatch {
+  const int* q_start;     // [B+1] token offsets of each request's queries
+  const int* ctx_len;     // [B] keys visible to the last query (start + n)
+  const int* page_table;  // [B, max_pages]
+  int max_pages;
+  const int2* items;      // [n_items] (request, first q row of the tile)
+  int n_items;
+  int splits;             // KV splits per item (>1: partials + combine)
+};
+
+struct AttnScratch {
+  float* o_part;          // [splits, T, nq, hd]
+  float* ml_part;         // [splits, T, nq, 2]
+};
+
+// q: [T, q_stride] bf16 (first nq*hd columns are the rotated queries);
+// out: [T, nq*hd] bf16.
+void paged_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
+                     const AttnBatch& b, const AttnScratch& sc, int T, int nq, float scale, cudaStream_t s);
+int attention_q_rows_per_tile();
+
+}  // namespace kus
+
+namespace kus {
+// Deterministic N(0, std) bf16 fill from a counter hash (random-init weights).
+void fill_normal_bf16(__nv_bfloat16* p, long long n, unsigned long long seed, float std, cudaStream_t s);
+void fill_value_bf16(__nv_bfloat16* p, long long n, float v, cudaStream_t s);
+// Read (and optionally clear) the device error flag: code | (info << 8).
+long long error_flag(bool reset);
+}  // namespace kus

@@ -1,0 +1,302 @@
+"""Drives the native engine (``kunserve_b200._C.Engine``) for one worker.
+
+Per step it packs the batch metadata into one pinned int32 buffer (a single
+host-to-device copy), decides the attention split, runs the C++ layer loop
+and returns the sampled ids (copied back to pinned memory by the engine).
+Pipeline activations travel over NCCL point-to-point from the engine's
+hidden buffer.
+"""
+import itertools
+import math
+from typing import List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from ..config.runtime import ModelConfig, ParallelConfig
+from ..kv.layout import KVLayout
+from ..models.torch_llama import sample_tokens
+from ..ops import native
+from .step import StepInput
+
+MAX_ENGINE_TOKENS = 16384
+ATTN_SPLIT_TOKENS = 512
+Q_TILE_ROWS = 64
+
+
+def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf: np.ndarray):
+    """Fill ``buf`` (int32) with the engine's step metadata; returns
+    ``(n_ints, T, B, n_items, max_ctx)``."""
+    B = step.num_requests
+    ql = np.fromiter((len(t) for t in step.input_tokens), dtype=np.int64, count=B)
+    T = int(ql.sum())
+    starts = np.asarray(step.start_positions, dtype=np.int64)
+    q_start = np.zeros(B + 1, dtype=np.int64)
+    np.cumsum(ql, out=q_start[1:])
+    rows = ql * group
+    tiles = (rows + Q_TILE_ROWS - 1) // Q_TILE_ROWS
+    n_items = int(tiles.sum())
+    item_req = np.repeat(np.arange(B), tiles)
+    item_first = np.arange(n_items) - np.repeat(np.cumsum(tiles) - tiles, tiles)
+    table = np.zeros((B, max_pages), dtype=np.int32)
+    for i, p in enumerate(step.page_tables):
+        if p:
+            table[i, :len(p)] = p
+    req_of_tok = np.repeat(np.arange(B), ql)
+    pos = np.arange(T) - q_start[req_of_tok] + starts[req_of_tok]
+    o = 0
+
+    def put(a):
+        nonlocal o
+        n = a.size
+        buf[o:o + n] = a.reshape(-1)
+        o += n
+
+    items = np.empty((n_items, 2), dtype=np.int32)
+    items[:, 0] = item_req
+    items[:, 1] = item_first * Q_TILE_ROWS
+    put(items)
+    put(np.fromiter(itertools.chain.from_iterable(step.input_tokens), dtype=np.int32, count=T))
+    put(pos.astype(np.int32))
+    put(table[req_of_tok, pos // block_size])
+    put((pos % block_size).astype(np.int32))
+    put(q_start.astype(np.int32))
+    ctx = (starts + ql).astype(np.int32)
+    put(ctx)
+    put((q_start[1:] - 1).astype(np.int32))
+    put(table)
+    temps = np.asarray(step.temperature if step.temperature is not None else [0.0] * B, dtype=np.float32)
+    put(temps.view(np.int32))
+    seeds = np.asarray(step.seeds if step.seeds is not None else [0] * B, dtype=np.int64) & 0xFFFFFFFF
+    put(seeds.astype(np.uint32).view(np.int32))
+    return o, T, B, n_items, int(ctx.max()) if B else 0
+
+
+class NativeRunner:
+    def __init__(self, mc: ModelConfig, pc: ParallelConfig, layout: KVLayout, device: torch.device,
+                 path: str = "", seed: int = 0, max_batch_tokens: int = 8192, max_batch_size: int = 256,
+                 comm=None, num_cpu_blocks: int = 0, weights=None):
+        C = native()
+        self.C = C
+        self.mc, self.pc, self.layout, self.comm = mc, pc, layout, comm
+        self.device = device
+        sh = C.EngineShape()
+        sh.layers = mc.get_num_layers(pc)
+        sh.nq = mc.get_q_heads(pc)
+        sh.nkv = mc.get_num_heads(pc)
+        sh.hd = mc.get_head_size()
+        sh.hidden = mc.get_hidden_size()
+        sh.ffn = mc.get_ffn_inter_dim() // pc.tensor_parallel_size
+        sh.vocab = mc.get_vocab_size()
+        sh.max_tokens = min(max_batch_tokens, MAX_ENGINE_TOKENS)
+        sh.max_batch = max_batch_size
+        sh.max_pos = mc.get_max_model_len()
+        sh.block_size = layout.block_size
+        sh.eps = mc.get_layernorm_eps()
+        sh.rope_theta = mc.arch.rope_theta
+        sh.tp = pc.tensor_parallel_size
+        self.shape = sh
+        self.group = sh.nq // sh.nkv
+        dev = device.index if device.index is not None else torch.cuda.current_device()
+        with torch.cuda.device(dev):
+            self.eng = C.Engine(sh, dev)
+            self.eng.init_memory(layout.num_pages)
+            assert self.eng.page_bytes() == layout.page_stride, (self.eng.page_bytes(), layout.page_stride)
+            if weights is not None:
+                self.load_weights(weights)
+            elif path:
+                from ..weights.loader import load_converted
+                self.load_weights(load_converted(path, mc, pc, torch.bfloat16))
+            else:
+                self.eng.random_init(seed + 1000 * pc.pipeline_parallel_rank, 0.02)
+            torch.cuda.synchronize()
+        self.max_pages = math.ceil(sh.max_pos / layout.block_size)
+        n = (2 * (sh.max_tokens * self.group // Q_TILE_ROWS + sh.max_batch + 1) + 4 * sh.max_tokens
+             + 5 * sh.max_batch + 1 + sh.max_batch * self.max_pages + 64)
+        self.meta = torch.empty(n, dtype=torch.int32, pin_memory=True)
+        self.meta_np = self.meta.numpy()
+        self.num_sms = C.num_sms()
+        self.ext_pages = 0
+        self.fusion_size = 1
+        self.peer_maps = {}
+
+    def load_weights(self, w) -> None:
+        for l, lw in enumerate(w.layers):
+            if lw is None:
+                continue
+            self.eng.load_layer(l, [lw["input_norm"], lw["w_qkv"], lw["w_o"], lw["post_norm"], lw["w_gate_up"],
+                                    lw["w_down"]])
+        g = w.globals
+        self.eng.load_globals(g["embed"], g["final_norm"], g["lm_head"])
+
+    def _splits(self, T: int, n_items: int, max_ctx: int) -> int:
+        if T > ATTN_SPLIT_TOKENS:
+            return 1
+        ctas = n_items * self.shape.nkv
+        want = math.ceil(2 * self.num_sms / max(ctas, 1))
+        return int(max(1, min(16, want, max_ctx // 128)))
+
+    def step(self, step: StepInput, recv_from: Optional[Tuple[str, int]] = None,
+             send_to: Optional[Tuple[str, int]] = None, last_stage: bool = True) -> Optional[List[int]]:
+        width = max([len(p) for p in step.page_tables] + [1])
+        n, T, B, n_items, max_ctx = pack_meta(step, self.layout.block_size, self.group, width, self.meta_np)
+        splits = self._splits(T, n_items, max_ctx)
+        first = recv_from is None
+        if not first:
+            buf = self.comm.recv((T, self.shape.hidden), torch.bfloat16, self.device, *recv_from)
+            self.eng.hidden()[:T].copy_(buf)
+        sample_mode = 0
+        if last_stage and step.top_k is not None and (any(k > 0 for k in step.top_k) or
+                                                      any(p < 1.0 for p in (step.top_p or []))):
+            sample_mode = 1
+        out = self.eng.forward(self.meta, T, B, width, n_items, splits, step.layer_start, step.layer_end,
+                               step.fusion_size, first, last_stage, sample_mode, step.step_id)
+        if send_to is not None:
+            self.comm.send(self.eng.hidden()[:T], *send_to)
+        if not last_stage:
+            return None
+        if sample_mode == 1:
+            logits = self.eng.logits()[:B]
+            return sample_tokens(logits, step.temperature, step.top_k, step.top_p, step.seeds,
+                                 step.step_id).tolist()
+        return list(out)
+
+    # ---------------------------------------------------------- balloon
+    def drop_layers(self, layers: List[int], fusion_size: int) -> int:
+        ext_bytes = self.eng.drop_layers(layers)
+        self.fusion_size = fusion_size
+        self.ext_pages = ext_bytes // self.layout.extend_page_bytes(fusion_size)
+        return int(self.ext_pages)
+
+    def restore_layers(self, dropped, keepers, my_rank, n) -> float:
+        """Remap the dropped layers and pull their bytes from the keepers."""
+        restored = self.eng.restore_layers()
+        moved = 0.0
+        if self.comm is not None and n > 1:
+            moved = self._pull_layers(restored, keepers, my_rank, n)
+        self.ext_pages = 0
+        self.fusion_size = 1
+        return moved
+
+    def _pull_layers(self, restored, keepers, my_rank, n) -> float:
+        # NCCL baseline path: every rank sends the layers it kept
+        L = self.shape.layers
+        kept = [l for l in range(L) if keepers[l] == my_rank]
+        sends = {}
+        for peer in range(n):
+            if peer == my_rank:
+                continue
+            need = [l for l in range(L) if keepers[l] == my_rank]
+            if need:
+                sends[self._kvex(peer)] = torch.cat([self.eng.layer_bytes_view(l) for l in kept])
+        recv = {}
+        for peer in range(n):
+            if peer == my_rank:
+                continue
+            mine = [l for l in restored if keepers[l] == peer]
+            nbytes = sum(self.eng.layer_segment_bytes(l) for l in mine)
+            recv[self._kvex(peer)] = ((nbytes,), torch.uint8)
+        got = self.comm.exchange("kvex", sends, recv, self.device)
+        moved = 0
+        for peer in range(n):
+            if peer == my_rank:
+                continue
+            buf = got[self._kvex(peer)]
+            off = 0
+            for l in sorted(l for l in restored if keepers[l] == peer):
+                nb = self.eng.layer_segment_bytes(l)
+                self.eng.layer_bytes_view(l).copy_(buf[off:off + nb])
+                off += nb
+            moved += off
+        return float(moved)
+
+    def _kvex(self, member: int) -> int:
+        return member * self.pc.pipeline_parallel_size + self.pc.pipeline_parallel_rank
+
+    # ------------------------------------------------------- KV movement
+    def pool_bytes(self, extend: bool = True) -> torch.Tensor:
+        n = self.layout.base_bytes + (self.ext_pages * self.layout.extend_page_bytes(self.fusion_size)
+                                      if extend else 0)
+        ptr = self.eng.kv_base_ptr()
+        return _u8_view(ptr, n, self.device)
+
+    def local_copy(self, src: List[int], dst: List[int], chunk: int) -> None:
+        d = torch.tensor(dst, dtype=torch.int64, device=self.device)
+        s = torch.tensor(src, dtype=torch.int64, device=self.device)
+        base = self.eng.kv_base_ptr()
+        self.eng.copy_chunks(base, base, d, s, chunk, 4 * self.num_sms)
+        torch.cuda.synchronize(self.device)
+
+    def kv_exchange(self, plan_send, plan_recv, chunk, my_rank, n) -> int:
+        pool = self.pool_bytes()
+        ar = torch.arange(chunk, device=self.device)
+        sends = {}
+        for k, offs in plan_send.items():
+            idx = (torch.tensor(offs, dtype=torch.int64, device=self.device)[:, None] + ar).reshape(-1)
+            sends[self._kvex(k)] = pool[idx]
+        shapes = {self._kvex(j): ((len(offs) * chunk,), torch.uint8) for j, offs in plan_recv.items()}
+        got = self.comm.exchange("kvex", sends, shapes, self.device)
+        total = 0
+        for j, offs in plan_recv.items():
+            if offs:
+                dst = torch.tensor(offs, dtype=torch.int64, device=self.device)
+                self._scatter(got[self._kvex(j)], dst, chunk)
+                total += len(offs) * chunk
+        torch.cuda.synchronize(self.device)
+        return total
+
+    def _scatter(self, buf: torch.Tensor, dst_offs: torch.Tensor, chunk: int) -> None:
+        src = torch.arange(dst_offs.numel(), dtype=torch.int64, device=self.device) * chunk
+        self.eng.copy_chunks(self.eng.kv_base_ptr(), buf.data_ptr(), dst_offs, src, chunk, 4 * self.num_sms)
+
+    def kv_restore(self, my_rank, n, home, fusion_pages, dp_pages, chunk) -> int:
+        from ..kv import copy_plan
+        pool = self.pool_bytes()
+        ar = torch.arange(chunk, device=self.device)
+        if my_rank != home:
+            src, _ = copy_plan.restore_plan(self.layout, n, my_rank, fusion_pages[my_rank], dp_pages)
+            idx = (torch.tensor(src, dtype=torch.int64, device=self.device)[:, None] + ar).reshape(-1)
+            self.comm.exchange("kvex", {self._kvex(home): pool[idx]}, {}, self.device)
+            return 0
+        recvs = {self._kvex(j): ((len(dp_pages) * chunk,), torch.uint8) for j in range(n) if j != home}
+        got = self.comm.exchange("kvex", {}, recvs, self.device)
+        for j in range(n):
+            src, dst = copy_plan.restore_plan(self.layout, n, j, fusion_pages[j], dp_pages)
+            d = torch.tensor(dst, dtype=torch.int64, device=self.device)
+            if j == home:
+                s = torch.tensor(src, dtype=torch.int64, device=self.device)
+                base = self.eng.kv_base_ptr()
+                self.eng.copy_chunks(base, base, d, s, chunk, 4 * self.num_sms)
+            else:
+                self._scatter(got[self._kvex(j)], d, chunk)
+        torch.cuda.synchronize(self.device)
+        return len(dp_pages) * chunk * n
+
+    def swap(self, pairs, is_swap_in: bool) -> None:
+        if not hasattr(self, "_host"):
+            self._host = {}
+        pool = self.pool_bytes(extend=False)
+        ps = self.layout.page_stride
+        for a, b in pairs:
+            if is_swap_in:
+                pool[b * ps:(b + 1) * ps].copy_(self._host.pop(a), non_blocking=True)
+            else:
+                h = torch.empty(ps, dtype=torch.uint8, pin_memory=True)
+                h.copy_(pool[a * ps:(a + 1) * ps])
+                self._host[b] = h
+        torch.cuda.synchronize(self.device)
+
+    def read_kv(self, page_id: int, local_layer: int, fusion_size: int) -> torch.Tensor:
+        off = self.layout.kv_offset(page_id, local_layer, fusion_size)
+        n = self.layout.layer_stride // 2
+        return self.pool_bytes()[off:off + n].view(torch.bfloat16).clone().cpu()
+
+
+def _u8_view(ptr: int, nbytes: int, device) -> torch.Tensor:
+    """A uint8 tensor over device memory owned by the engine (no copy)."""
+    import ctypes
+
+    class _Holder:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+    return torch.as_tensor(_Holder(), device=device)

@@ -16,7 +16,7 @@ from .weights import LlamaWeights
 
 
 def rope_cos_sin(positions: torch.Tensor, head_dim: int, theta: float):
-    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64, device=positions.device) / head_dim))
     ang = positions.to(torch.float64)[:, None] * inv[None, :]
     return torch.cos(ang).float(), torch.sin(ang).float()
 

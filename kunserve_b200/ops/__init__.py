@@ -1,0 +1,1 @@
+from ._native import native, available, check_error, NativeUnavailable

@@ -1,0 +1,87 @@
+"""The native engine end to end against the PyTorch paged Llama (fp32 math,
+identical bf16 weights), and through the instance engine."""
+import asyncio
+
+import pytest
+import torch
+
+from kunserve_b200.config import (BalloonConfig, BenchConfig, CacheConfig, ModelConfig, ParallelConfig,
+                                  SchedConfig)
+from kunserve_b200.engine.step import StepInput
+from kunserve_b200.kv.layout import KVLayout
+from kunserve_b200.models.torch_llama import PagedKVPool, TorchLlama
+from kunserve_b200.models.weights import LlamaWeights
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(P=64, bs=16, max_tokens=2048, model="tiny-llama-128"):
+    from kunserve_b200.engine.native_runner import NativeRunner
+    mc = ModelConfig(model, dtype="bf16")
+    pc = ParallelConfig()
+    w = LlamaWeights.random(mc, pc, seed=3, dtype=torch.bfloat16)
+    s = w.shapes
+    lay = KVLayout(P, s.num_layers, bs, s.kv_heads, s.head_dim, 2)
+    nat = NativeRunner(mc, pc, lay, torch.device("cuda:0"), weights=w, max_batch_tokens=max_tokens,
+                       max_batch_size=64)
+    wd = LlamaWeights(s, {k: v.cuda() for k, v in w.globals.items()},
+                      [{k: v.cuda() for k, v in lw.items()} for lw in w.layers])
+    ref = TorchLlama(wd, PagedKVPool(lay, torch.bfloat16, device="cuda"), compute_dtype=torch.float32)
+    return mc, nat, ref
+
+
+def test_engine_matches_torch_logits():
+    mc, nat, ref = _setup()
+    prompts = [[(7 * i + 3 * j) % 32000 for j in range(n)] for i, n in enumerate((20, 5, 33))]
+    tables = [[0, 1], [2], [3, 4, 5]]
+    step = StepInput([0, 1, 2], prompts, [0, 0, 0], tables, [1, 1, 1], 0, 2, top_k=[5, 5, 5],
+                     top_p=[1.0] * 3, temperature=[0.0] * 3, seeds=[0, 1, 2])
+    nat.step(step)   # sample_mode 1 leaves logits in the engine
+    lg_nat = nat.eng.logits()[:3].clone()
+    h = ref.forward_hidden(step)
+    lg_ref = ref.logits(h, step)
+    rel = ((lg_nat - lg_ref).norm() / lg_ref.norm()).item()
+    assert rel < 3e-2, rel
+    assert (lg_nat.argmax(-1) == lg_ref.argmax(-1)).float().mean() >= 2 / 3
+    # one decode step on top of the cached prefixes
+    nxt = lg_ref.argmax(-1).tolist()
+    step2 = StepInput([0, 1, 2], [[t] for t in nxt], [20, 5, 33], tables, [0, 0, 0], 0, 2, top_k=[5] * 3,
+                      top_p=[1.0] * 3, temperature=[0.0] * 3, seeds=[0, 1, 2], step_id=1)
+    nat.step(step2)
+    lg2 = nat.eng.logits()[:3].clone()
+    ref2 = ref.logits(ref.forward_hidden(step2), step2)
+    assert ((lg2 - ref2).norm() / ref2.norm()).item() < 3e-2
+    from kunserve_b200.ops import check_error
+    check_error()
+
+
+def test_engine_greedy_in_kernel_equals_argmax():
+    mc, nat, ref = _setup()
+    step = StepInput([0], [[1, 2, 3, 4]], [0], [[0]], [1], 0, 2, temperature=[0.0], seeds=[0])
+    toks = nat.step(step)
+    assert toks == [int(nat.eng.logits()[0].argmax())]
+
+
+def test_instance_engine_native_runs_requests():
+    from kunserve_b200.engine.instance import InstanceEngine
+    from kunserve_b200.engine.worker import Worker
+    from kunserve_b200.runtime import LocalActor
+    import sys, os
+    sys.path.insert(0, os.path.dirname(__file__))
+    from helpers import drive, make_requests
+    mc = ModelConfig("tiny-llama-128", dtype="bf16")
+    pc, cc = ParallelConfig(), CacheConfig(block_size=16)
+    w = Worker(0, mc, cc, pc, backend="native", device="cuda:0", seed=1)
+    sc = SchedConfig(policy="mixed", enable_chunked_prefill=True, chunked_prefill_budget=256, max_batch_size=64,
+                     max_tokens_per_batch=2048)
+    eng = InstanceEngine(0, 0, mc, pc, cc, sc, BalloonConfig(), BenchConfig(), [[LocalActor(w)]])
+    reqs = make_requests(24, seed=5, plen=(10, 300), olen=(5, 40))
+
+    async def run():
+        await eng.initialize(num_gpu_blocks=128)
+        return await drive(eng, reqs, timeout_s=300)
+
+    got = asyncio.run(run())
+    assert len(got) == 24
+    assert all(len(v) == r.sampling_params.max_tokens for v, r in zip([got[r.request_id] for r in reqs], reqs))
+    eng.block_managers[0].check_invariants()

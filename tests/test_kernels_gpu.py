@@ -1,0 +1,228 @@
+"""Numerics of every CUDA kernel against a plain PyTorch fp32 reference."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def C():
+    from kunserve_b200.ops import native
+    return native()
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-6)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 256), (7, 512, 1024), (128, 640, 512), (300, 1024, 4096),
+                                   (1000, 768, 2048), (64, 4096, 4096), (2, 32000, 512)])
+@pytest.mark.parametrize("max_split", [1, 16])
+def test_gemm_bf16(C, M, N, K, max_split):
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm(A, B, out, C.EPI_BF16, None, 0, max_split)
+    torch.cuda.synchronize()
+    ref = A.float() @ B.float().t()
+    assert _rel(out, ref) < 1e-2
+    from kunserve_b200.ops import check_error
+    check_error()
+
+
+def test_gemm_f32_add_silu(C):
+    torch.manual_seed(1)
+    M, K, F = 37, 512, 384
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    W = (torch.randn(512, K, device="cuda") * 0.05).bfloat16()
+    o32 = torch.empty(M, 512, device="cuda", dtype=torch.float32)
+    C.gemm(A, W, o32, C.EPI_F32, None, 0, 16)
+    ref = A.float() @ W.float().t()
+    assert _rel(o32, ref) < 5e-3
+    res = torch.randn(M, 512, device="cuda").bfloat16()
+    o = res.clone()
+    C.gemm(A, W, o, C.EPI_ADD, o, 0, 1)
+    assert _rel(o, ref + res.float()) < 1e-2
+    # SiLU*up with weights interleaved per 128 rows (gate block, up block)
+    gate = (torch.randn(F, K, device="cuda") * 0.05).bfloat16()
+    up = (torch.randn(F, K, device="cuda") * 0.05).bfloat16()
+    inter = torch.stack([gate.view(F // 128, 128, K), up.view(F // 128, 128, K)], 1).reshape(2 * F, K).contiguous()
+    act = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+    for ms in (1, 16):
+        C.gemm(A, inter, act, C.EPI_SILU, None, 256, ms)
+        g, u = A.float() @ gate.float().t(), A.float() @ up.float().t()
+        assert _rel(act, torch.nn.functional.silu(g) * u) < 1e-2
+    torch.cuda.synchronize()
+
+
+def test_rmsnorm(C):
+    torch.manual_seed(2)
+    for H in (512, 4096, 5120, 8192):
+        x = torch.randn(9, H, device="cuda").bfloat16()
+        a = torch.randn(9, H, device="cuda").bfloat16()
+        w = torch.rand(H, device="cuda").bfloat16()
+        y = torch.empty_like(x)
+        x2 = x.clone()
+        C.rmsnorm(x2, a, w, y, None, 1e-5)
+        s = (x.float() + a.float())
+        assert torch.allclose(x2.float(), s, atol=2e-2)
+        s = x2.float()
+        ref = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
+        assert _rel(y, ref) < 1e-2
+        rows = torch.tensor([3, 0], device="cuda", dtype=torch.int32)
+        y2 = torch.empty(2, H, device="cuda", dtype=torch.bfloat16)
+        C.rmsnorm(x2, None, w, y2, rows, 1e-5)
+        assert _rel(y2, ref[[3, 0]]) < 1e-2
+
+
+def _pool(P, L, bs, kvh, hd, ext_pages=0, N=1):
+    from kunserve_b200.kv.layout import KVLayout
+    lay = KVLayout(P, L, bs, kvh, hd, 2)
+    n = lay.base_bytes + ext_pages * lay.extend_page_bytes(N)
+    return lay, torch.zeros(n // 2, device="cuda", dtype=torch.bfloat16)
+
+
+def test_rope_append(C):
+    from kunserve_b200.models.torch_llama import apply_rope, rope_cos_sin
+    torch.manual_seed(3)
+    nq, nkv, hd, bs, L, P = 4, 2, 128, 16, 4, 8
+    for N, ext in ((1, 0), (2, 3)):
+        lay, pool = _pool(P, L, bs, nkv, hd, ext, N)
+        T = 5
+        qkv = torch.randn(T, (nq + 2 * nkv) * hd, device="cuda").bfloat16()
+        orig = qkv.clone()
+        pos = torch.tensor([0, 1, 17, 40, 3], device="cuda", dtype=torch.int32)
+        pages = torch.tensor([0, 0, 5 if N == 1 else 9, 2 if N == 1 else 2 * P + 1, 7], device="cuda",
+                             dtype=torch.int32)
+        slots = pos % bs
+        cos, sin = rope_cos_sin(torch.arange(4096), hd, 10000.0)
+        cs = torch.cat([cos, sin], 1).cuda().contiguous()
+        layer = 1
+        Ls = L // N
+        C.rope_append(qkv, pos, pages, slots, cs, pool, P, N, Ls, L, bs, nq, nkv, hd, layer)
+        torch.cuda.synchronize()
+        c, s = cos.cuda()[pos.long()], sin.cuda()[pos.long()]
+        q = orig[:, :nq * hd].float().view(T, nq, hd)
+        k = orig[:, nq * hd:(nq + nkv) * hd].float().view(T, nkv, hd)
+        v = orig[:, (nq + nkv) * hd:].float().view(T, nkv, hd)
+        assert _rel(qkv[:, :nq * hd].view(T, nq, hd), apply_rope(q, c, s)) < 1e-2
+        kr = apply_rope(k, c, s)
+        for t in range(T):
+            off = lay.kv_offset(int(pages[t]), layer, N) // 2 + int(slots[t]) * nkv * hd
+            voff = lay.kv_offset(int(pages[t]), layer, N, True) // 2 + int(slots[t]) * nkv * hd
+            assert _rel(pool[off:off + nkv * hd].view(nkv, hd), kr[t]) < 1e-2
+            assert torch.equal(pool[voff:voff + nkv * hd].view(nkv, hd), v[t].bfloat16())
+
+
+def _ref_attention(q, pool, lay, N, layer, tables, starts, qlens, nq, nkv, hd):
+    out = torch.empty(q.shape[0], nq, hd, device="cuda")
+    G = nq // nkv
+    t0 = 0
+    for i, n in enumerate(qlens):
+        ctx = starts[i] + n
+        ks, vs = [], []
+        for p in range(ctx):
+            page, slot = tables[i][p // lay.block_size], p % lay.block_size
+            ko = lay.kv_offset(page, layer, N) // 2 + slot * nkv * hd
+            vo = lay.kv_offset(page, layer, N, True) // 2 + slot * nkv * hd
+            ks.append(pool[ko:ko + nkv * hd].view(nkv, hd))
+            vs.append(pool[vo:vo + nkv * hd].view(nkv, hd))
+        K = torch.stack(ks).float().repeat_interleave(G, 1)
+        V = torch.stack(vs).float().repeat_interleave(G, 1)
+        qi = q[t0:t0 + n].float().view(n, nq, hd)
+        sc = torch.einsum("nhd,chd->hnc", qi, K) / math.sqrt(hd)
+        qpos = torch.arange(starts[i], ctx, device="cuda")
+        mask = torch.arange(ctx, device="cuda")[None] > qpos[:, None]
+        sc = sc.masked_fill(mask[None], float("-inf"))
+        out[t0:t0 + n] = torch.einsum("hnc,chd->nhd", torch.softmax(sc, -1), V)
+        t0 += n
+    return out
+
+
+@pytest.mark.parametrize("nq,nkv", [(4, 2), (8, 1), (4, 4)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_paged_attention(C, nq, nkv, splits):
+    import numpy as np
+    from kunserve_b200.engine.native_runner import pack_meta
+    from kunserve_b200.engine.step import StepInput
+    torch.manual_seed(4)
+    hd, bs, L, P, N = 128, 16, 2, 64, 1
+    lay, pool = _pool(P, L, bs, nkv, hd)
+    pool.copy_(torch.randn_like(pool.float()).bfloat16())
+    # mixed batch: a prefill chunk with a prefix, a fresh prefill, two decodes
+    starts = [40, 0, 100, 5] if splits == 1 else [0, 0, 300, 77]
+    qlens = [30, 17, 1, 1] if splits == 1 else [1, 1, 1, 1]
+    rng = np.random.default_rng(0)
+    perm = rng.permutation(P).tolist()
+    tables, k = [], 0
+    for s, n in zip(starts, qlens):
+        need = (s + n + bs - 1) // bs
+        tables.append(perm[k:k + need])
+        k += need
+    T = sum(qlens)
+    q = torch.randn(T, nq * hd, device="cuda").bfloat16()
+    step = StepInput(list(range(4)), [[0] * n for n in qlens], starts, tables, [1] * 4, 0, 1)
+    buf = np.zeros(4096, dtype=np.int32)
+    G = nq // nkv
+    width = max(len(t) for t in tables)
+    _, T2, B, n_items, _ = pack_meta(step, bs, G, width, buf)
+    items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
+    o = 2 * n_items + 4 * T
+    q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
+    ctx = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
+    tab = torch.zeros(B, width, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        tab[i, :len(t)] = torch.tensor(t)
+    out = torch.empty(T, nq * hd, device="cuda", dtype=torch.bfloat16)
+    o_part = torch.empty(splits * T * nq * hd, device="cuda")
+    ml = torch.empty(splits * T * nq * 2, device="cuda")
+    layer = 1
+    C.attention(q, nq * hd, out, pool, P, N, L, L, bs, nkv, layer, q_start, ctx, tab.cuda(), items, splits,
+                o_part, ml, nq, 1.0 / math.sqrt(hd))
+    torch.cuda.synchronize()
+    ref = _ref_attention(q, pool, lay, N, layer, tables, starts, qlens, nq, nkv, hd)
+    assert _rel(out.view(T, nq, hd), ref) < 2e-2
+
+
+def test_sample_greedy_and_temperature(C):
+    torch.manual_seed(5)
+    logits = torch.randn(6, 32000, device="cuda")
+    temps = torch.tensor([0, 0, 1.0, 0.5, 0, 2.0], device="cuda")
+    seeds = torch.arange(6, device="cuda", dtype=torch.int32)
+    out = torch.empty(6, device="cuda", dtype=torch.int32)
+    C.sample(logits, temps, seeds, 3, out)
+    am = logits.argmax(-1)
+    for r in (0, 1, 4):
+        assert int(out[r]) == int(am[r])
+    # temperature sampling follows softmax(l/T): check frequencies on a small vocab
+    lg = torch.tensor([[0.0, 1.0, 2.0, 3.0]], device="cuda").repeat(4000, 1)
+    t = torch.ones(4000, device="cuda")
+    sd = torch.arange(4000, device="cuda", dtype=torch.int32)
+    o = torch.empty(4000, device="cuda", dtype=torch.int32)
+    C.sample(lg, t, sd, 0, o)
+    freq = torch.bincount(o.long(), minlength=4).float() / 4000
+    p = torch.softmax(lg[0], 0)
+    assert (freq - p).abs().max() < 0.04
+
+
+def test_copy_chunks(C):
+    src = torch.randint(0, 255, (1 << 20,), device="cuda", dtype=torch.uint8)
+    dst = torch.zeros_like(src)
+    so = torch.tensor([0, 4096, 65536], device="cuda", dtype=torch.int64)
+    do = torch.tensor([8192, 0, 131072], device="cuda", dtype=torch.int64)
+    C.copy_chunks(dst.data_ptr(), src.data_ptr(), do, so, 4096, 64)
+    torch.cuda.synchronize()
+    for s, d in zip(so.tolist(), do.tolist()):
+        assert torch.equal(dst[d:d + 4096], src[s:s + 4096])
+
+
+def test_embed(C):
+    tab = torch.randn(100, 512, device="cuda").bfloat16()
+    tok = torch.tensor([3, 99, 0], device="cuda", dtype=torch.int32)
+    out = torch.empty(3, 512, device="cuda", dtype=torch.bfloat16)
+    C.embed(tok, tab, out)
+    assert torch.equal(out, tab[tok.long()])
