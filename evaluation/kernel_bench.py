@@ -1,0 +1,161 @@
+"""Kernel microbenchmarks on one GPU, timed with CUDA events.
+
+    python evaluation/kernel_bench.py gemm --m 1 16 256 4096 --n 6144 --k 4096
+    python evaluation/kernel_bench.py gemm-cublas --m 16 --n 4096 --k 4096
+    python evaluation/kernel_bench.py attention --batch 64 --ctx 1024
+    python evaluation/kernel_bench.py decode-step --batch 1 32 128
+
+Each case runs ``--warmup`` untimed iterations, then ``--iters`` timed ones
+with a synchronize on both sides; inputs rotate over several buffers whose
+total exceeds the 126 MB L2 (weights of one GEMM are larger than L2 on their
+own for the decode shapes), so every iteration reads from HBM.  Results are
+printed as JSON lines with the achieved bandwidth / FLOP rate and their
+fraction of the measured peaks in ``MEASURED_PEAKS.json`` (fallback: 6.65
+TB/s and 1.59 PFLOP/s).
+"""
+import argparse
+import json
+import math
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"] * 1e9, d["bf16_tflops"] * 1e12, "measured"
+    return 6.65e12, 1.59e15, "fallback"
+
+
+def timeit(fn, warmup, iters):
+    for _ in range(warmup):
+        fn(0)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(iters):
+        fn(i)
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters * 1e-3
+
+
+def bench_gemm(args, cublas=False):
+    from kunserve_b200.ops import check_error, native
+    C = native()
+    bw, fl, src = peaks()
+    for M in args.m:
+        for N in args.n:
+            for K in args.k:
+                nbuf = max(2, math.ceil(256e6 / (N * K * 2)))
+                Ws = [(torch.randn(N, K, device="cuda") * 0.02).bfloat16() for _ in range(min(nbuf, 8))]
+                A = torch.randn(M, K, device="cuda").bfloat16()
+                out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+                if cublas:
+                    fn = lambda i: torch.matmul(A, Ws[i % len(Ws)].t(), out=out)
+                else:
+                    fn = lambda i: C.gemm(A, Ws[i % len(Ws)], out, C.EPI_BF16, None, args.bn, args.max_split)
+                t = timeit(fn, args.warmup, args.iters)
+                check_error()
+                bytes_ = (M * K + N * K + M * N) * 2
+                flops = 2.0 * M * N * K
+                print(json.dumps({"kernel": "gemm_cublas" if cublas else "gemm_tcgen05", "M": M, "N": N, "K": K,
+                                  "us": round(t * 1e6, 2), "TB_s": round(bytes_ / t / 1e12, 3),
+                                  "bw_frac": round(bytes_ / t / bw, 3), "TFLOP_s": round(flops / t / 1e12, 1),
+                                  "flop_frac": round(flops / t / fl, 3), "peaks": src}), flush=True)
+
+
+def bench_attention(args):
+    from kunserve_b200.engine.native_runner import pack_meta
+    from kunserve_b200.engine.step import StepInput
+    from kunserve_b200.ops import native
+    import numpy as np
+    C = native()
+    bw, fl, src = peaks()
+    nq, nkv, hd, bs, L = args.nq, args.nkv, 128, 16, 1
+    for B in args.batch:
+        for ctx in args.ctx:
+            pages_per = math.ceil(ctx / bs)
+            P = B * pages_per
+            from kunserve_b200.kv.layout import KVLayout
+            lay = KVLayout(P, L, bs, nkv, hd, 2)
+            pool = torch.randn(lay.base_bytes // 2, device="cuda").bfloat16()
+            tables = [list(range(i * pages_per, (i + 1) * pages_per)) for i in range(B)]
+            q = torch.randn(B, nq * hd, device="cuda").bfloat16()
+            step = StepInput(list(range(B)), [[0]] * B, [ctx - 1] * B, tables, [0] * B, 0, 1)
+            buf = np.zeros(4 * B + 2 * B + 64 + B * pages_per + 16 * B, dtype=np.int32)
+            _, T, _, n_items, _ = pack_meta(step, bs, nq // nkv, pages_per, buf)
+            items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
+            o = 2 * n_items + 4 * T
+            q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
+            ctxl = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
+            tab = torch.tensor(tables, dtype=torch.int32, device="cuda")
+            splits = int(max(1, min(16, math.ceil(2 * 148 / (n_items * nkv)), ctx // 128))) if args.splits < 0 \
+                else args.splits
+            out = torch.empty(B, nq * hd, device="cuda", dtype=torch.bfloat16)
+            op = torch.empty(splits * B * nq * hd, device="cuda")
+            ml = torch.empty(splits * B * nq * 2, device="cuda")
+            fn = lambda i: C.attention(q, nq * hd, out, pool, P, 1, L, L, bs, nkv, 0, q_start, ctxl, tab, items,
+                                       splits, op, ml, nq, 1 / math.sqrt(hd))
+            t = timeit(fn, args.warmup, args.iters)
+            kv_bytes = B * ctx * nkv * hd * 2 * 2
+            print(json.dumps({"kernel": "paged_attention_decode", "B": B, "ctx": ctx, "nq": nq, "nkv": nkv,
+                              "splits": splits, "us": round(t * 1e6, 2), "TB_s": round(kv_bytes / t / 1e12, 3),
+                              "bw_frac": round(kv_bytes / t / bw, 3), "peaks": src}), flush=True)
+
+
+def bench_copy(args):
+    from kunserve_b200.ops import native
+    C = native()
+    bw, _, src = peaks()
+    for n in args.chunks:
+        chunk = args.chunk_bytes
+        srcb = torch.empty(n * chunk, device="cuda", dtype=torch.uint8)
+        dst = torch.empty_like(srcb)
+        perm = torch.randperm(n, device="cuda")
+        so = torch.arange(n, device="cuda", dtype=torch.int64) * chunk
+        do = perm.to(torch.int64) * chunk
+        fn = lambda i: C.copy_chunks(dst.data_ptr(), srcb.data_ptr(), do, so, chunk, 4 * 148)
+        t = timeit(fn, args.warmup, args.iters)
+        by = 2 * n * chunk
+        print(json.dumps({"kernel": "copy_chunks_local", "chunks": n, "chunk_bytes": chunk, "us": round(t * 1e6, 2),
+                          "TB_s": round(by / t / 1e12, 3), "bw_frac": round(by / t / bw, 3), "peaks": src}),
+              flush=True)
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("what", choices=["gemm", "gemm-cublas", "attention", "copy"])
+    p.add_argument("--m", type=int, nargs="+", default=[1, 16, 64, 256])
+    p.add_argument("--n", type=int, nargs="+", default=[6144, 4096, 28672])
+    p.add_argument("--k", type=int, nargs="+", default=[4096])
+    p.add_argument("--bn", type=int, default=0)
+    p.add_argument("--max-split", type=int, default=16)
+    p.add_argument("--batch", type=int, nargs="+", default=[1, 16, 64, 256])
+    p.add_argument("--ctx", type=int, nargs="+", default=[512, 2048])
+    p.add_argument("--nq", type=int, default=32)
+    p.add_argument("--nkv", type=int, default=8)
+    p.add_argument("--splits", type=int, default=-1)
+    p.add_argument("--chunks", type=int, nargs="+", default=[1024, 16384])
+    p.add_argument("--chunk-bytes", type=int, default=65536)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--iters", type=int, default=20)
+    a = p.parse_args()
+    if a.what == "gemm":
+        bench_gemm(a)
+    elif a.what == "gemm-cublas":
+        bench_gemm(a, cublas=True)
+    elif a.what == "attention":
+        bench_attention(a)
+    else:
+        bench_copy(a)
+
+
+if __name__ == "__main__":
+    main()

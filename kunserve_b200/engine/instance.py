@@ -182,6 +182,26 @@ class InstanceEngine(AdmissionMixin):
         self._terminate = True
         self.stopped = True
 
+    def reset(self) -> None:
+        """Drop every request and its pages and clear the counters, so the
+        instance can serve a fresh workload (the loop must not be running)."""
+        for s in self.scheduler:
+            for r in s.all_requests():
+                self._free_blocks(r)
+            s.unaccepted_queue.clear()
+            s.long_unaccepted_queue.clear()
+            s.waiting_queue.clear()
+            s.swapped_queue.clear()
+            s.running_queue.requests.clear()
+            s.num_preemption = 0
+        self.unaccepted_queue.clear()
+        for bm in self.block_managers:
+            assert not bm.block_table, "pages still held after reset"
+        self._terminate = False
+        self.stopped = False
+        self.ttfts, self.tbts, self.step_log = [], [], []
+        self.finished_tokens = self.finished_requests = 0
+
     async def stop_and_wait(self) -> None:
         self.stopped = True
         while any(self.scheduler_running):

@@ -119,6 +119,9 @@ class NativeRunner:
         self.ext_pages = 0
         self.fusion_size = 1
         self.peer_maps = {}
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.num_steps = 0
 
     def load_weights(self, w) -> None:
         for l, lw in enumerate(w.layers):
@@ -151,6 +154,10 @@ class NativeRunner:
             sample_mode = 1
         out = self.eng.forward(self.meta, T, B, width, n_items, splits, step.layer_start, step.layer_end,
                                step.fusion_size, first, last_stage, sample_mode, step.step_id)
+        self.num_steps += 1
+        self.h2d_bytes += 4 * n
+        if last_stage and sample_mode == 0:
+            self.d2h_bytes += 4 * B
         if send_to is not None:
             self.comm.send(self.eng.hidden()[:T], *send_to)
         if not last_stage:

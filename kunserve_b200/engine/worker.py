@@ -102,8 +102,10 @@ class Worker:
             self.runner = TorchLlama(weights, pool, self.comm, compute_dtype=cdt)
         else:
             from .native_runner import NativeRunner
+            # chunked prefill may overshoot the token budget by one token per
+            # partly-prefilled request, so leave room for a full batch of them
             self.runner = NativeRunner(self.mc, self.pc, self.layout, self.device, path=path,
-                                       seed=self.seed, max_batch_tokens=max_batch_tokens,
+                                       seed=self.seed, max_batch_tokens=max_batch_tokens + max_batch_size,
                                        max_batch_size=max_batch_size, comm=self.comm,
                                        num_cpu_blocks=num_cpu_blocks)
         logger.info(f"worker {self.worker_id}: {self.backend} runner, {num_gpu_blocks} KV pages "

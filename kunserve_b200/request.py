@@ -225,7 +225,8 @@ class Request:
 
     # -- chunked prefill -----------------------------------------------------
     def have_follow_up_chunk(self) -> bool:
-        return self.is_context_stage() and self.prefill_end_index < self.get_input_len()
+        return self.is_context_stage() and (self.prefill_end_index < self.get_input_len()
+                                            or self.prefill_begin_index >= self.prefill_end_index)
 
     def set_chunk(self, chunk_size: int) -> int:
         """Set the current chunk to start at ``prefill_begin_index``; returns the
@@ -373,9 +374,9 @@ class BatchedRequests:
             r.last_step_time = end_time
             r.add_process_time(end_time - self.start_time)
             if r.have_follow_up_chunk():
-                # the chunk only filled KV; move the window on
+                # the chunk only filled KV: the next window starts where this
+                # one ended and stays empty until the scheduler sizes it
                 r.prefill_begin_index = r.prefill_end_index
-                r.prefill_end_index = r.get_input_len()
             else:
                 r.add_generated_token(tok, tid, end_time)
         self.start_time = None

@@ -107,7 +107,7 @@ class ColocatedScheduler:
         with ``prefill_only_chunk=False``) runs prefill chunks and decodes
         together; otherwise prefills run first and decodes wait."""
         prefills, decodes = self.running_queue.split_requests()
-        prefills = [r for r in prefills if r.kvcache_ready]
+        prefills = [r for r in prefills if r.kvcache_ready and r.get_num_input_tokens() > 0]
         decodes = [r for r in decodes if r.kvcache_ready]
         mixed = self.sched_config.policy == "mixed" or (
             self.sched_config.enable_chunked_prefill and not prefill_only_chunk)

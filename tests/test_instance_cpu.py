@@ -58,3 +58,26 @@ def test_preemption_under_small_pool():
     bm = eng.block_managers[0]
     bm.check_invariants()
     assert bm.num_free_whole() == bm.P
+
+
+def test_chunked_prefill_respects_token_budget():
+    budget = 40
+    eng, w, mc = _engine(chunked=True, budget=budget, policy="mixed")
+    seen = []
+    orig = w.step
+
+    def spy(step, *a, **k):
+        seen.append(step.num_tokens)
+        return orig(step, *a, **k)
+    w.step = spy
+    reqs = make_requests(8, seed=9, plen=(30, 130), olen=(3, 8))
+
+    async def run():
+        await eng.initialize(num_gpu_blocks=64)
+        return await drive(eng, reqs)
+
+    got = asyncio.run(run())
+    assert len(got) == 8
+    # a step may exceed the budget by one token per partly-prefilled request
+    assert max(seen) <= budget + len(reqs), seen
+    assert sum(1 for t in seen if t > budget) <= 2
