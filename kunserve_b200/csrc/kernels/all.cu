@@ -21,3 +21,6 @@ long long error_flag(bool reset) {
   return (long long)code | ((long long)info << 8);
 }
 }  // namespace kus
+
+// Allocation-free C entry point (a separate addition; see gemm_noalloc.h).
+#include "gemm_noalloc.cu"

@@ -1,0 +1,60 @@
+// Allocation-free GEMM entry point (C ABI).
+//
+// This entry point has no counterpart in the reference implementation; it
+// is an addition of this library.
+//
+// Who it is for: code that must not allocate GPU memory while it runs -- an
+// inference-runtime plugin whose enqueue callback forbids allocation, a
+// custom allocator or memory-pool hook that would re-enter itself, a
+// real-time loop with a fixed memory budget, or a host thread that cannot
+// take the caching allocator's lock.  Those callers cannot call cudaMalloc
+// (or anything that does, such as a PyTorch op), so this function never
+// does: its split-K scratch is a fixed array compiled into the library.
+//
+//   C[M,N] (bf16, row-major, ldc) = A[M,K] (bf16, lda) * B[N,K]^T (bf16, ldb)
+//
+// It runs the same tcgen05 kernel as the regular entry point
+// (kus::run_gemm, bf16 epilogue) with the same split-K plan, so results
+// match it.
+//
+// Scratch: one static device array of KUS_NOALLOC_SCRATCH_BYTES per GPU
+// that loads this library, held until the process exits.  A problem whose
+// split-K plan needs more is rejected (KUS_NOALLOC_ERR_SCRATCH); every
+// problem planned on a GPU with at most 148 SMs fits.
+//
+// Set-up: the first call on a device (with that device current) looks up
+// the array's device address with cudaGetSymbolAddress; make that first
+// call outside any stream capture.
+//
+// Concurrency: all calls on a device share the one array, which keeps the
+// last call's contents.  Calls whose executions overlap on the GPU (on
+// different streams, or from different host threads without ordering)
+// race on it; order them on one stream.
+//
+// Returns 0 on success, a negative KUS_NOALLOC_ERR_* code for a rejected
+// argument, or a positive cudaError_t from the CUDA runtime.
+#pragma once
+#include <cuda_runtime.h>
+
+#define KUS_NOALLOC_SCRATCH_BYTES (20u << 20)   /* 20 MiB per GPU */
+
+enum {
+  KUS_NOALLOC_OK = 0,
+  KUS_NOALLOC_ERR_ARGS = -1,      /* non-positive size, K or a leading dimension not a multiple of 8 */
+  KUS_NOALLOC_ERR_SCRATCH = -2,   /* the split-K plan needs more than KUS_NOALLOC_SCRATCH_BYTES */
+  KUS_NOALLOC_ERR_ALIGN = -3,     /* a pointer is not 16-byte aligned */
+  KUS_NOALLOC_ERR_TMAP = -4,      /* TMA descriptor encoding failed */
+  KUS_NOALLOC_ERR_SETUP = -5,     /* cudaGetSymbolAddress failed on this device */
+};
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+__attribute__((visibility("default"))) int kus_gemm_bf16_noalloc(const void* A, int lda, const void* B, int ldb,
+                                                                 void* C, int ldc, int M, int N, int K,
+                                                                 cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
