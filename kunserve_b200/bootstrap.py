@@ -80,11 +80,15 @@ def build_instances(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: S
             handles[rank] = LocalActor(Worker(rank, mc, cc, pc, backend=backend, device=devices[rank], seed=seed))
         elif actor_kind == "process":
             env = {"KUNSERVE_WORKER_RANK": str(rank)}
+            # every rank must be spawned before any can finish joining the job
             handles[rank] = ProcessActor(make_worker_process, rank, world, port, topo, mc, cc, pc, backend,
-                                         devices[rank], seed, env=env)
+                                         devices[rank], seed, env=env, wait_ready=False)
         else:
             handles[rank] = make_actor("ray", make_worker_process, rank, world, port, topo, mc, cc, pc, backend,
                                        devices[rank], seed, num_gpus=1 if devices[rank] != "cpu" else 0)
+    if actor_kind == "process":
+        for h in handles.values():
+            h.wait_ready()
     groups = []
     for g in range(ec.ngroups):
         insts = []

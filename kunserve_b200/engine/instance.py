@@ -108,6 +108,8 @@ class InstanceEngine(AdmissionMixin):
         self.step_log: List[Tuple[float, int, int]] = []   # (seconds, tokens, requests)
         self.event_log: List[Tuple[float, str, float]] = []  # (time, event, seconds)
         self._loop_task: Optional[asyncio.Task] = None
+        # per VE scheduler: was its next batch prepared after its last step?
+        self._prepared: Dict[int, bool] = {}
 
     # ------------------------------------------------------------ set-up
     def _new_scheduler(self) -> ColocatedScheduler:
@@ -224,11 +226,18 @@ class InstanceEngine(AdmissionMixin):
         ls = stage_layers // n
         lstart = inst * ls if fusion_exec and n > 1 else 0
         sp = [r.sampling_params for r in requests]
+        tables = bm.get_block_table(requests)
+        for r, t in zip(requests, tables):
+            if len(t) * self.block_size < r.context_len_after_step():
+                raise AssertionError(
+                    f"instance {self.instance_id} (state {self.state}, member {inst}): request {r.request_id} "
+                    f"needs {r.context_len_after_step()} KV slots but holds {len(t)} pages ({r!r}, "
+                    f"kind={bm._kind.get(r.request_id)})")
         return StepInput(
             request_ids=[r.request_id for r in requests],
             input_tokens=[r.get_input_tokens_ids() for r in requests],
             start_positions=[r.start_position() for r in requests],
-            page_tables=bm.get_block_table(requests),
+            page_tables=tables,
             is_prefill=[int(r.is_context_stage()) for r in requests],
             layer_start=lstart, layer_end=lstart + ls,
             fusion_size=bm.fusion_size if fusion_exec else 1,
@@ -269,6 +278,12 @@ class InstanceEngine(AdmissionMixin):
             resharding: List[Request] = []
             if ve < len(self.is_resharding) and self.is_resharding[ve]:
                 resharding = await self._live_reshard_prepare(ve)
+            if not self._prepared.get(id(self.scheduler[ve]), False):
+                # a transition stopped the previous step before it prepared
+                # this VE's next batch (page growth, admission): do it now
+                async with self.allocate_lock:
+                    await self._get_next_batch(ve)
+            self._prepared[id(self.scheduler[ve])] = False
             batch, _ = self.scheduler[ve].schedule(prefill_only_chunk=True)
             batch.set_sched_time()
             pipe, replica = batch.get_fusion_requests()
@@ -350,6 +365,7 @@ class InstanceEngine(AdmissionMixin):
         if self.stopped:
             return
         s = self.scheduler[ve]
+        self._prepared[id(s)] = True
         for r in s.pop_finished_requests():
             self._free_blocks(r)
         # 1. grow the running requests; preempt on shortage
@@ -706,8 +722,9 @@ class InstanceEngine(AdmissionMixin):
             r.kvcache_ready = True
 
     async def reshard_blocks(self, requests: Sequence[Request]) -> None:
-        """Bulk reshard in batches of ``exchange_batch_size`` requests; what
-        cannot be placed is recomputed instead."""
+        """Bulk reshard in batches of ``exchange_batch_size`` requests.  The
+        requests keep their place in their VE's running queue; what cannot be
+        placed on the other members is recomputed instead."""
         remaining = list(requests)
         cap = self.balloon_config.exchange_batch_size or len(remaining) or 1
         while remaining:
@@ -715,20 +732,17 @@ class InstanceEngine(AdmissionMixin):
             ok, fail = self.prepare_reshard_blocks(head)
             if ok:
                 await self._reshard_blocks_batched(ok)
-                for r in ok:
-                    self._place_in_ve(r)
             if fail and not ok:
                 for r in fail + remaining:
+                    for s in self.scheduler:
+                        if r in s.running_queue.requests:
+                            s.running_queue.requests.remove(r)
                     self._free_blocks(r)
                     r.prepare_for_recompute()
                     r.fusion_exec = True
                     self.unaccepted_queue.appendleft(r)
                 break
             remaining = fail + remaining
-
-    def _place_in_ve(self, r: Request) -> None:
-        s = min(self.scheduler, key=lambda s: len(s.running_queue))
-        s.running_queue.add_request(r)
 
     async def _live_reshard_prepare(self, ve: int) -> List[Request]:
         s = self.scheduler[ve]

@@ -130,7 +130,7 @@ class ProcessActor(ActorHandle):
     kind = "process"
 
     def __init__(self, factory: Callable, *args, env: Optional[Dict[str, str]] = None,
-                 ready_timeout: float = 600.0, **kwargs):
+                 ready_timeout: float = 600.0, wait_ready: bool = True, **kwargs):
         ctx = mp.get_context("spawn")
         parent, child = ctx.Pipe()
         proc = ctx.Process(target=_process_main, args=(child, factory, args, kwargs, env), daemon=True)
@@ -146,7 +146,12 @@ class ProcessActor(ActorHandle):
         t = threading.Thread(target=self._reader, daemon=True)
         d["_reader_thread"] = t
         t.start()
-        self._ready.result(timeout=ready_timeout)
+        if wait_ready:
+            self._ready.result(timeout=ready_timeout)
+
+    def wait_ready(self, timeout: float = 600.0) -> None:
+        """Block until the object was built in the child (raises its error)."""
+        self._ready.result(timeout=timeout)
 
     def _reader(self):
         while True:
