@@ -89,10 +89,13 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   embed_ = torch::empty({s.vocab, s.hidden}, bf);
   final_norm_ = torch::ones({s.hidden}, bf);
   lm_head_ = torch::empty({s.vocab, s.hidden}, bf);
-  KUS_CHECK(make_tmap_bf16(&m_y_, y_.data_ptr(), T, s.hidden, s.hidden, 128), "tmap y");
-  KUS_CHECK(make_tmap_bf16(&m_attn_, attn_.data_ptr(), T, s.nq * s.hd, s.nq * s.hd, 128), "tmap attn");
-  KUS_CHECK(make_tmap_bf16(&m_act_, act_.data_ptr(), T, f_pad_, f_pad_, 128), "tmap act");
-  KUS_CHECK(make_tmap_bf16(&m_ylast_, ylast_.data_ptr(), ylast_.size(0), s.hidden, s.hidden, 128), "tmap ylast");
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t box = 16u << i;
+    KUS_CHECK(make_tmap_bf16(&m_y_[i], y_.data_ptr(), T, s.hidden, s.hidden, box), "tmap y");
+    KUS_CHECK(make_tmap_bf16(&m_attn_[i], attn_.data_ptr(), T, s.nq * s.hd, s.nq * s.hd, box), "tmap attn");
+    KUS_CHECK(make_tmap_bf16(&m_act_[i], act_.data_ptr(), T, f_pad_, f_pad_, box), "tmap act");
+    KUS_CHECK(make_tmap_bf16(&m_ylast_[i], ylast_.data_ptr(), ylast_.size(0), s.hidden, s.hidden, box), "tmap ylast");
+  }
   KUS_CHECK(make_tmap_bf16(&m_lm_head_, lm_head_.data_ptr(), s.vocab, s.hidden, s.hidden, 256), "tmap lm_head");
 }
 
@@ -204,7 +207,7 @@ torch::Tensor Engine::layer_bytes_view(int l) {
 torch::Tensor Engine::hidden() { return h_; }
 torch::Tensor Engine::logits() { return logits_; }
 
-void Engine::gemm(const CUtensorMap& mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
+void Engine::gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
                   const __nv_bfloat16* res, cudaStream_t st) {
   GemmPlan p = plan_gemm(M, N, K, epi, 256, 16);
   const size_t need = workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn);
@@ -212,7 +215,8 @@ void Engine::gemm(const CUtensorMap& mA, const CUtensorMap& mB, int M, int N, in
     p = plan_gemm(M, N, K, epi, 256, p.args.split_k - 1);
     if (workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn) <= (size_t)gemm_ws_.numel()) break;
   }
-  p.tmA = mA;
+  const int box = a_box_rows(p);
+  p.tmA = mA[box == 16 ? 0 : box == 32 ? 1 : box == 64 ? 2 : 3];
   p.tmB = mB;
   p.args.out = out;
   p.args.ldc = ldc;

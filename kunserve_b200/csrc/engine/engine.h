@@ -90,7 +90,7 @@ class Engine {
 
  private:
   void build_layer_maps(int l);
-  void gemm(const CUtensorMap& mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
+  void gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
             const __nv_bfloat16* res, cudaStream_t s);
   void all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t s);
 
@@ -106,7 +106,8 @@ class Engine {
   // workspaces
   torch::Tensor h_, y_, qkv_, attn_, act_, tmp_, ylast_, logits_, gemm_ws_, counters_, attn_o_, attn_ml_,
       meta_dev_, tokens_dev_, tokens_host_, cos_sin_;
-  CUtensorMap m_y_, m_attn_, m_act_, m_ylast_;
+  // activation TMA descriptors per token-box height (16, 32, 64, 128 rows)
+  CUtensorMap m_y_[4], m_attn_[4], m_act_[4], m_ylast_[4];
   int64_t attn_split_tokens_ = 0;
   int attn_max_splits_ = 16;
   ncclComm_t tp_comm_ = nullptr;

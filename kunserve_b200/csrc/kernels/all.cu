@@ -4,6 +4,7 @@
 #include "../common.cuh"
 
 #include "gemm_tcgen05.cu"
+#include "gemm_swap.cu"
 #include "elementwise.cu"
 #include "attention.cu"
 #include "init.cu"

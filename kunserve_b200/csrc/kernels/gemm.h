@@ -28,7 +28,13 @@ struct GemmPlan {
   int bn;
   int epi;
   int grid;
+  int swap;   // 1: decode-shaped, operands swapped (gemm_swap.cu), token tile of `bnt` rows
+  int bnt;
 };
+
+// Rows of the A (token) TMA box a plan needs: 128, or bnt when swapped.
+inline int a_box_rows(const GemmPlan& p) { return p.swap ? p.bnt : 128; }
+void run_gemm_swap(const GemmPlan& p, cudaStream_t s);
 
 int num_sms();
 bool make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,

@@ -1,0 +1,306 @@
+// Decode-shaped GEMM (few tokens, many output features) on tcgen05 with the
+// operands swapped: D^T[N, M] = B[N, K] * A[M, K]^T.
+//
+// With M <= 64 tokens the regular 128-row token tile would be mostly
+// padding.  Here the weight tile (256 rows, the same TMA box the regular
+// kernel uses) is the MMA's A operand, split into two 128-row halves, and
+// the token tile (BNT = 16..64 rows) is the narrow N operand.  Stages are
+// dominated by weight bytes, so more of them fit in shared memory and more
+// HBM traffic is in flight per SM.  The epilogue writes the transpose back
+// to C[M, N]; with EPI_SILU the two halves of a tile are the gate and up
+// rows of the same 128 features (the interleave of the weight layout), so a
+// thread holds both and stores silu(gate) * up directly.
+// Split-K and its last-arriver reduction work as in gemm_tcgen05.cu.
+#include "../common.cuh"
+#include "gemm.h"
+
+namespace kus {
+namespace gemm_swap_impl {
+
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr int kWRows = 256;
+constexpr int kSmemBudget = 212 * 1024;
+
+template <int BNT>
+struct SCfg {
+  static constexpr int kWBytes = kWRows * BK * 2;    // 32 KB
+  static constexpr int kXBytes = BNT * BK * 2;
+  static constexpr int kStageBytes = kWBytes + kXBytes;
+  static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
+  static constexpr int kTmemCols = (4 * BNT) < 32 ? 32 : 4 * BNT;   // 2 halves x 2 buffers
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+KUS_DEVICE float silu_s(float x) { return x / (1.0f + __expf(-x)); }
+
+// v[i] = D^T[f, tok0 + i]; store C[tok0 + i, f] for the 16 tokens.
+template <int EPI>
+KUS_DEVICE void store_col16(const GemmArgs& a, int f, int tok0, const float (&v)[16]) {
+  if (f >= a.n_out) return;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int tok = tok0 + i;
+    if (tok >= a.M) break;
+    if (EPI == EPI_F32) {
+      reinterpret_cast<float*>(a.out)[(size_t)tok * a.ldc + f] = v[i];
+    } else {
+      float x = v[i];
+      if (EPI == EPI_ADD) x += bf2f(a.residual[(size_t)tok * a.ld_res + f]);
+      reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)tok * a.ldc + f] = f2bf(x);
+    }
+  }
+}
+
+template <int BNT, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_swap_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     GemmArgs args) {
+  using C = SCfg<BNT>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_w = smem;
+  uint8_t* smem_x = smem + C::kStages * C::kWBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* tfull = empty + C::kStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  int* flag_smem = reinterpret_cast<int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int num_kb = (args.K + BK - 1) / BK;
+  const int S = args.split_k;
+  const int kbs = (num_kb + S - 1) / S;
+  const int tiles = args.n_tiles;          // one token tile
+  const int units = tiles * S;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_holder, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (elect_one_sync()) {
+      prefetch_tmap(&tmX);
+      prefetch_tmap(&tmW);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int n = u / S, split = u % S;
+        const int kb0 = split * kbs, kb1 = min(kb0 + kbs, num_kb);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
+          tma_load_2d(smem_w + stage * C::kWBytes, &tmW, &full[stage], kb * BK, n * kWRows);
+          tma_load_2d(smem_x + stage * C::kXBytes, &tmX, &full[stage], kb * BK, 0);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      for (int i = 0; i < C::kStages && ok; ++i) {
+        if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) break;
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, BNT);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int split = u % S;
+        const int kb0 = split * kbs, kb1 = min(kb0 + kbs, num_kb);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, kErrWaitTmemEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * 2 * BNT;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t w_addr = smem_u32(smem_w + stage * C::kWBytes);
+          const uint64_t dx = umma_desc_sw128(smem_u32(smem_x + stage * C::kXBytes));
+          const uint64_t dw0 = umma_desc_sw128(w_addr);
+          const uint64_t dw1 = umma_desc_sw128(w_addr + 128 * 128);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
+            umma_f16(d, dw0 + (uint64_t)(2 * k), dx + (uint64_t)(2 * k), idesc, accum);
+            umma_f16(d + BNT, dw1 + (uint64_t)(2 * k), dx + (uint64_t)(2 * k), idesc, accum);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;     // row within a 128-row half
+    const int et = threadIdx.x - 64;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int n = u / S, split = u % S;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, kErrWaitTmemFull));
+      tc_fence_after();
+      const uint32_t t0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 2 * BNT);
+      if (S == 1) {
+        if (ok) {
+#pragma unroll 1
+          for (int c = 0; c < BNT; c += 16) {
+            float v0[16], v1[16];
+            tmem_ld16(t0 + c, v0);
+            tmem_ld16(t0 + BNT + c, v1);
+            if (EPI == EPI_SILU) {
+              float o[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = silu_s(v0[i]) * v1[i];
+              store_col16<EPI_BF16>(args, n * 128 + r, c, o);
+            } else {
+              store_col16<EPI>(args, n * kWRows + r, c, v0);
+              store_col16<EPI>(args, n * kWRows + 128 + r, c, v1);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      } else {
+        float* ws = args.workspace + ((size_t)n * S + split) * (kWRows * BNT);
+        if (ok) {
+#pragma unroll 1
+          for (int c = 0; c < BNT; c += 16) {
+            float v0[16], v1[16];
+            tmem_ld16(t0 + c, v0);
+            tmem_ld16(t0 + BNT + c, v1);
+            float* d0 = ws + (size_t)r * BNT + c;
+            float* d1 = ws + (size_t)(128 + r) * BNT + c;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+              __stcg(reinterpret_cast<float4*>(d0 + i), make_float4(v0[i], v0[i + 1], v0[i + 2], v0[i + 3]));
+              __stcg(reinterpret_cast<float4*>(d1 + i), make_float4(v1[i], v1[i + 1], v1[i + 2], v1[i + 3]));
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        __threadfence();
+        named_barrier(1, 128);
+        if (et == 0) {
+          int last = 0;
+          if (!error_set()) {
+            const int prev = atomicAdd(&args.tile_counters[n], 1);
+            last = (prev == S - 1);
+            if (last) args.tile_counters[n] = 0;
+          }
+          *flag_smem = last;
+        }
+        named_barrier(1, 128);
+        const int last = *flag_smem;
+        named_barrier(1, 128);
+        if (last) {
+          __threadfence();
+          const float* base = args.workspace + (size_t)n * S * (kWRows * BNT);
+#pragma unroll 1
+          for (int c = 0; c < BNT; c += 16) {
+            float v0[16] = {}, v1[16] = {};
+            for (int s = 0; s < S; ++s) {
+              const float* p0 = base + (size_t)s * (kWRows * BNT) + (size_t)r * BNT + c;
+              const float* p1 = p0 + (size_t)128 * BNT;
+#pragma unroll
+              for (int i = 0; i < 16; i += 4) {
+                const float4 x = __ldcg(reinterpret_cast<const float4*>(p0 + i));
+                const float4 y = __ldcg(reinterpret_cast<const float4*>(p1 + i));
+                v0[i] += x.x; v0[i + 1] += x.y; v0[i + 2] += x.z; v0[i + 3] += x.w;
+                v1[i] += y.x; v1[i + 1] += y.y; v1[i + 2] += y.z; v1[i + 3] += y.w;
+              }
+            }
+            if (EPI == EPI_SILU) {
+              float o[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = silu_s(v0[i]) * v1[i];
+              store_col16<EPI_BF16>(args, n * 128 + r, c, o);
+            } else {
+              store_col16<EPI>(args, n * kWRows + r, c, v0);
+              store_col16<EPI>(args, n * kWRows + 128 + r, c, v1);
+            }
+          }
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
+}
+
+template <int BNT, int EPI>
+void launch_swap(const GemmPlan& p, cudaStream_t s) {
+  using C = SCfg<BNT>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gemm_swap_kernel<BNT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    attr = true;
+  }
+  gemm_swap_kernel<BNT, EPI><<<p.grid, kThreads, C::kSmemBytes, s>>>(p.tmA, p.tmB, p.args);
+}
+
+template <int EPI>
+void launch_swap_bnt(const GemmPlan& p, cudaStream_t s) {
+  switch (p.bnt) {
+    case 16: launch_swap<16, EPI>(p, s); break;
+    case 32: launch_swap<32, EPI>(p, s); break;
+    default: launch_swap<64, EPI>(p, s); break;
+  }
+}
+
+}  // namespace gemm_swap_impl
+
+void run_gemm_swap(const GemmPlan& p, cudaStream_t s) {
+  using namespace gemm_swap_impl;
+  switch (p.epi) {
+    case EPI_F32: launch_swap_bnt<EPI_F32>(p, s); break;
+    case EPI_SILU: launch_swap_bnt<EPI_SILU>(p, s); break;
+    case EPI_ADD: launch_swap_bnt<EPI_ADD>(p, s); break;
+    default: launch_swap_bnt<EPI_BF16>(p, s); break;
+  }
+}
+
+}  // namespace kus

@@ -403,9 +403,16 @@ size_t workspace_floats(int m_tiles, int n_tiles, int split_k, int bn) {
 
 GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, int max_split) {
   GemmPlan p{};
-  p.bn = bn > 0 ? bn : choose_bn(M, N, epi);
   p.epi = epi;
-  const int m_tiles = (M + BM - 1) / BM;
+  // few tokens: swap operands so the weight tile fills the 128-row MMA side
+  if ((bn == 0 || bn == 256) && M <= 32 && N >= 256) {
+    p.swap = 1;
+    p.bnt = M <= 16 ? 16 : 32;
+    p.bn = 256;
+  } else {
+    p.bn = bn > 0 ? bn : choose_bn(M, N, epi);
+  }
+  const int m_tiles = p.swap ? 1 : (M + BM - 1) / BM;
   const int n_tiles = (N + p.bn - 1) / p.bn;
   const int num_kb = (K + BK - 1) / BK;
   const int sms = num_sms();
@@ -440,13 +447,17 @@ bool finalize_plan(GemmPlan& p, const void* A, int lda, const void* B, int ldb, 
   p.args.ld_res = ld_res;
   p.args.workspace = workspace;
   p.args.tile_counters = counters;
-  if (!make_tmap_bf16(&p.tmA, A, a_rows ? a_rows : (uint64_t)p.args.M, p.args.K, lda, BM)) return false;
+  if (!make_tmap_bf16(&p.tmA, A, a_rows ? a_rows : (uint64_t)p.args.M, p.args.K, lda, a_box_rows(p))) return false;
   if (!make_tmap_bf16(&p.tmB, B, b_rows ? b_rows : (uint64_t)p.args.N, p.args.K, ldb, p.bn)) return false;
   return true;
 }
 
 void run_gemm(const GemmPlan& p, cudaStream_t s) {
   if (p.args.M <= 0) return;
+  if (p.swap) {
+    run_gemm_swap(p, s);
+    return;
+  }
   switch (p.epi) {
     case EPI_F32: launch_bn<EPI_F32>(p, s); break;
     case EPI_SILU: launch<256, EPI_SILU>(p, s); break;

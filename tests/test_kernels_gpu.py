@@ -18,7 +18,7 @@ def _rel(a, b):
     return ((a - b).norm() / (b.norm() + 1e-6)).item()
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 256, 256), (7, 512, 1024), (128, 640, 512), (300, 1024, 4096),
+@pytest.mark.parametrize("M,N,K", [(1, 256, 256), (7, 512, 1024), (33, 2816, 1024), (65, 1024, 512), (128, 640, 512), (300, 1024, 4096),
                                    (1000, 768, 2048), (64, 4096, 4096), (2, 32000, 512)])
 @pytest.mark.parametrize("max_split", [1, 16])
 def test_gemm_bf16(C, M, N, K, max_split):
