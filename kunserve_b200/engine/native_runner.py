@@ -100,6 +100,8 @@ class NativeRunner:
         dev = device.index if device.index is not None else torch.cuda.current_device()
         with torch.cuda.device(dev):
             self.eng = C.Engine(sh, dev)
+            if pc.tensor_parallel_size > 1:
+                self._init_tp_comm(dev)
             self.eng.init_memory(layout.num_pages)
             assert self.eng.page_bytes() == layout.page_stride, (self.eng.page_bytes(), layout.page_stride)
             if weights is not None:
@@ -122,6 +124,16 @@ class NativeRunner:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.num_steps = 0
+
+    def _init_tp_comm(self, dev: int) -> None:
+        """NCCL communicator of the engine's in-layer all-reduce: TP rank 0
+        creates the unique id, the ``tp`` group broadcasts it."""
+        import torch.distributed as dist
+        assert self.comm is not None, "tensor parallelism needs a communicator"
+        uid = [self.C.nccl_unique_id() if self.pc.tensor_parallel_rank == 0 else None]
+        dist.broadcast_object_list(uid, src=self.comm.peer("tp", 0), group=self.comm.groups["tp"],
+                                   device=torch.device("cuda", dev))
+        self.eng.init_tp_comm(uid[0], self.pc.tensor_parallel_rank, self.pc.tensor_parallel_size)
 
     def load_weights(self, w) -> None:
         for l, lw in enumerate(w.layers):

@@ -328,6 +328,19 @@ class Worker:
         idx = pool.block_view_index(torch.tensor([page_id]), local_layer, fusion_size, False)
         return pool.data[idx].clone()
 
+    def last_logits(self, n: int) -> torch.Tensor:
+        """fp32 logits of the last step's ``n`` rows (left by sample mode 1)."""
+        return self.runner.eng.logits()[:n].float().cpu()
+
+    def layer_checksums(self) -> List[float]:
+        """Per-layer checksum of this rank's weight bytes (restore tests)."""
+        if self.backend == "native":
+            return [float(self.runner.eng.layer_bytes_view(l).to(torch.float64).sum())
+                    if l not in self.runner.eng.dropped() else float("nan")
+                    for l in range(self.shapes.num_layers)]
+        return [float(sum(t.double().sum() for t in lw.values())) if lw is not None else float("nan")
+                for lw in self.runner.w.layers]
+
     def pop_step_times(self) -> List[float]:
         out, self.step_times = self.step_times, []
         return out

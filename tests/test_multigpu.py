@@ -1,0 +1,137 @@
+"""Two-GPU paths of the native engine: tensor parallelism (in-engine NCCL
+all-reduce) and the balloon cycle (parameter drop into extend pages, KV
+reshard between GPUs, parameter restore from the peer, live KV restore).
+Workers are separate processes, one per GPU."""
+import asyncio
+import math
+
+import pytest
+import torch
+
+from kunserve_b200.config import KunServeConfig, ModelConfig, ParallelConfig
+from kunserve_b200.request import SamplingParams
+from kunserve_b200.utils.misc import EngineState
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _need2():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+
+
+@pytest.fixture(scope="module")
+def ckpt(tmp_path_factory):
+    from helpers import hf_from_weights
+    from kunserve_b200.models.weights import LlamaWeights
+    from kunserve_b200.weights import convert_weights
+    mc = ModelConfig("tiny-llama-128", dtype="bf16")
+    w = LlamaWeights.random(mc, ParallelConfig(), seed=9, dtype=torch.float32, full_model=True)
+    src = tmp_path_factory.mktemp("hf")
+    hf_from_weights(mc, w).save_pretrained(src)
+    out = str(tmp_path_factory.mktemp("conv"))
+    convert_weights(str(src), out, torch.bfloat16)
+    return mc, out
+
+
+def test_tp2_logits_match_oracle(ckpt):
+    _need2()
+    from kunserve_b200.bootstrap import build_instances
+    from kunserve_b200.config import CacheConfig, SchedConfig
+    from kunserve_b200.engine.step import StepInput
+    from kunserve_b200.kv.layout import KVLayout
+    from kunserve_b200.models.torch_llama import PagedKVPool, TorchLlama
+    from kunserve_b200.runtime import get
+    from kunserve_b200.weights import load_converted
+    mc, path = ckpt
+    cfg = KunServeConfig()
+    cfg.engine_config.tp = 2
+    cc = CacheConfig(block_size=16)
+    groups = build_instances(cfg, mc, cc, SchedConfig(), actor_kind="process", devices=["cuda:0", "cuda:1"])
+    workers = groups[0][0].workers[0]
+    try:
+        get([w.init_model.remote(16, path, 256, 8) for w in workers], timeout=600)
+        prompts = [[(11 * i + 5 * j) % 32000 for j in range(n)] for i, n in enumerate((17, 40))]
+        step = StepInput([0, 1], prompts, [0, 0], [[0, 1], [2, 3, 4]], [1, 1], 0, 2, temperature=[0.0, 0.0],
+                         top_k=[3, 3], top_p=[1.0, 1.0], seeds=[0, 1])
+        get([w.step.remote(step) for w in workers], timeout=600)
+        got = get(workers[0].last_logits.remote(2), timeout=60)
+        full = load_converted(path, mc, ParallelConfig(), torch.bfloat16, device="cuda:0")
+        s = full.shapes
+        ref = TorchLlama(full, PagedKVPool(KVLayout(16, 2, 16, s.kv_heads, s.head_dim, 2), torch.bfloat16, "cuda:0"),
+                         compute_dtype=torch.float32)
+        want = ref.logits(ref.forward_hidden(step), step).cpu()
+        rel = ((got - want).norm() / want.norm()).item()
+        assert rel < 3e-2, rel
+    finally:
+        for w in workers:
+            w.kill()
+
+
+async def _balloon_native():
+    from kunserve_b200.llm import AsyncLLM
+    from kunserve_b200.runtime import aw
+    cfg = KunServeConfig()
+    e = cfg.engine_config
+    e.ngroups, e.group_size, e.block_size = 1, 2, 16
+    e.enable_chunked_prefill, e.chunked_prefill_budget = True, 512
+    e.max_batch_tokens = 1024
+    cfg.balloon_config.balloon_mode = "reshard"
+    cfg.bench_config.enable_restore = True
+    mc = ModelConfig("tiny-llama-128", dtype="bf16")
+    llm = await AsyncLLM.create(cfg, model_config=mc, backend="native", actor_kind="process",
+                                devices=["cuda:0", "cuda:1"], num_gpu_blocks=96, seed=3)
+    g = llm.groups[0]
+    leader = g.leader
+    w0, w1 = leader.workers[0][0], g.instances[1].workers[0][0]
+    try:
+        before = [await aw(w.layer_checksums.remote()) for w in (w0, w1)]
+        sp = lambda n: SamplingParams(temperature=0.0, max_tokens=n, ignore_eos=True)
+        tasks = [asyncio.create_task(llm.generate(prompt_token_ids=list(range(3 + i, 40 + 7 * i)),
+                                                  sampling_params=sp(60), request_id=i)) for i in range(10)]
+        loop = asyncio.get_running_loop()
+        t0 = loop.time()
+        while sum(len(s.running_queue.get_decode_requests()) for i in g.instances for s in i.scheduler) < 6:
+            assert loop.time() - t0 < 120
+            await asyncio.sleep(0.01)
+        await g.stop_all_engines()
+        # KV of one stale request on instance 1, all layers, before the reshard
+        stale = next(r for s in g.instances[1].scheduler for r in s.running_queue.requests)
+        pages1 = list(g.instances[1].block_managers[0].get_single_block_table(stale.request_id))
+        kv_before = [await aw(w1.read_kv.remote(p, l, 1)) for p in pages1 for l in range(2)]
+        ctx = stale.get_input_len() + stale.get_output_len() - 1     # positions whose KV exists now
+        per_tok = kv_before[0].numel() // 16
+        await g.trigger_balloon()     # engines stay stopped until the balloon restarts them
+        assert g.state == EngineState.BALLOON
+        # layer 0 of the stale request now lives on instance 0 (slice 0), layer 1 stays on instance 1
+        bm0, bm1 = leader.block_managers[0], leader.block_managers[1]
+        f0 = bm0.get_single_block_table(stale.request_id)[:len(pages1)]
+        f1 = bm1.get_single_block_table(stale.request_id)[:len(pages1)]
+        assert f1 == [1 * bm1.P + p for p in pages1]
+        for k, p in enumerate(pages1):
+            n = max(0, min(16, ctx - 16 * k)) * per_tok     # decoding resumed: later slots may be new
+            assert torch.equal((await aw(w0.read_kv.remote(f0[k], 0, 2)))[:n], kv_before[2 * k][:n])
+            assert torch.equal((await aw(w1.read_kv.remote(f1[k], 0, 2)))[:n], kv_before[2 * k + 1][:n])
+        tasks += [asyncio.create_task(llm.generate(prompt_token_ids=list(range(5, 50)), sampling_params=sp(20),
+                                                   request_id=100 + i)) for i in range(4)]
+        await asyncio.sleep(2.0)
+        await g.trigger_restore()
+        after = [await aw(w.layer_checksums.remote()) for w in (w0, w1)]
+        for a, b in zip(after, before):
+            assert all(math.isclose(x, y, rel_tol=0, abs_tol=1e-6) for x, y in zip(a, b)), (a, b)
+        t0 = loop.time()
+        while leader.get_num_fusion_requests() and loop.time() - t0 < 120:
+            await asyncio.sleep(0.05)
+        await g.trigger_init()
+        res = await asyncio.wait_for(asyncio.gather(*tasks), 300)
+        return res
+    finally:
+        await llm.terminate()
+
+
+def test_balloon_cycle_two_gpus():
+    _need2()
+    res = asyncio.run(_balloon_native())
+    by = {r["request_id"]: r for r in res}
+    assert all(len(by[i]["outputs"]) == 60 for i in range(10))
+    assert all(len(by[100 + i]["outputs"]) == 20 for i in range(4))
