@@ -34,6 +34,7 @@ class GroupEngine:
         self.tasks: Dict[int, asyncio.Task] = {}
         self.transitions: List[Tuple[float, str, float]] = []
         self.failed: Optional[BaseException] = None
+        self.p2p = False
         for inst in instances:
             inst.peers = instances
 
@@ -74,6 +75,27 @@ class GroupEngine:
     def terminate(self) -> None:
         for inst in self.instances:
             inst.terminate()
+
+    async def setup_peer_memory(self) -> bool:
+        """Map every member's KV pool and weight segments into its peers
+        (same pipeline stage and TP rank), so reshard, live restore and
+        parameter restore pull over NVLink inside the copy kernel.  Returns
+        False when the workers have no native engine."""
+        from ..runtime.actors import aw
+        if len(self.instances) < 2:
+            return False
+        pp, tp = self.leader.pp_size, self.leader.tp_size
+        for st in range(pp):
+            for t in range(tp):
+                members = [inst.workers[st][t] for inst in self.instances]
+                infos = [await aw(w.export_memory.remote()) for w in members]
+                if not all(infos):
+                    return False
+                await asyncio.gather(*[aw(w.import_peers.remote({j: infos[j] for j in range(len(members))
+                                                                 if j != i}))
+                                       for i, w in enumerate(members)])
+        self.p2p = True
+        return True
 
     # ------------------------------------------------------------ votes
     async def make_decision_for(self, engines: List[InstanceEngine], event: Event) -> bool:

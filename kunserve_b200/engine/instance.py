@@ -702,9 +702,11 @@ class InstanceEngine(AdmissionMixin):
                         home_len = len(self.block_managers[j].get_single_block_table(r.request_id))
                         lst.extend(bm.get_single_block_table(r.request_id)[:home_len])
                     pages.append(lst)
+                home = [[p for r in by_home[j] for p in self.block_managers[j].get_single_block_table(r.request_id)]
+                        for j in range(n)]
                 for st in range(self.pp_size):
                     for w in self.workers[i * self.pp_size + st]:
-                        futs.append(w.kv_exchange.remote(pages, i, n))
+                        futs.append(w.kv_exchange.remote(pages, i, n, home))
             try:
                 moved = await asyncio.gather(*[aw(f) for f in futs])
             except Exception:

@@ -180,6 +180,39 @@ class NativeRunner:
                                  step.step_id).tolist()
         return list(out)
 
+    # -------------------------------------------------------- peer memory
+    def export_memory(self) -> dict:
+        from ..parallel.peer import FdServer
+        L = self.shape.layers
+        fds = [self.eng.export_kv_fd()] + [self.eng.export_layer_fd(l) for l in range(L)]
+        sizes = [self.eng.kv_phys_bytes()] + [self.eng.layer_segment_bytes(l) for l in range(L)]
+        if getattr(self, "_fd_server", None) is not None:
+            self._fd_server.close()
+        self._fd_server = FdServer(fds)
+        return {"sock": self._fd_server.path, "sizes": sizes}
+
+    def import_peers(self, infos: dict) -> int:
+        """Map every group member's memory (``infos[member]`` from its
+        ``export_memory``); afterwards KV and weight movement pulls over NVLink."""
+        from ..parallel.peer import PeerMemory, fetch_fds
+        dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        for member, info in infos.items():
+            self.peer_maps[int(member)] = PeerMemory(self.C, dev, fetch_fds(info["sock"]), info["sizes"])
+        return len(self.peer_maps)
+
+    def close_peer_memory(self) -> None:
+        self.peer_maps.clear()
+        if getattr(self, "_fd_server", None) is not None:
+            self._fd_server.close()
+            self._fd_server = None
+
+    def _pull(self, dst_base: int, member: int, src_base: int, dst: List[int], src: List[int], chunk: int) -> None:
+        if not dst:
+            return
+        d = torch.tensor(dst, dtype=torch.int64, device=self.device)
+        s = torch.tensor(src, dtype=torch.int64, device=self.device)
+        self.eng.copy_chunks(dst_base, src_base, d, s, chunk, 4 * self.num_sms)
+
     # ---------------------------------------------------------- balloon
     def drop_layers(self, layers: List[int], fusion_size: int) -> int:
         ext_bytes = self.eng.drop_layers(layers)
@@ -191,7 +224,16 @@ class NativeRunner:
         """Remap the dropped layers and pull their bytes from the keepers."""
         restored = self.eng.restore_layers()
         moved = 0.0
-        if self.comm is not None and n > 1:
+        if n > 1 and self.peer_maps:
+            chunk = 1 << 20
+            for l in restored:
+                nb = self.eng.layer_segment_bytes(l)
+                offs = list(range(0, nb, chunk))
+                src = self.peer_maps[keepers[l]].layers[l]
+                self._pull(self.eng.layer_ptr(l), keepers[l], src, offs, offs, chunk)
+                moved += nb
+            torch.cuda.synchronize(self.device)
+        elif self.comm is not None and n > 1:
             moved = self._pull_layers(restored, keepers, my_rank, n)
         self.ext_pages = 0
         self.fusion_size = 1
@@ -246,7 +288,15 @@ class NativeRunner:
         self.eng.copy_chunks(base, base, d, s, chunk, 4 * self.num_sms)
         torch.cuda.synchronize(self.device)
 
-    def kv_exchange(self, plan_send, plan_recv, chunk, my_rank, n) -> int:
+    def kv_exchange(self, plan_send, plan_recv, chunk, my_rank, n, peer_src=None) -> int:
+        if self.peer_maps and peer_src is not None:
+            total = 0
+            base = self.eng.kv_base_ptr()
+            for j, dst in plan_recv.items():
+                self._pull(base, j, self.peer_maps[j].kv, dst, peer_src[j], chunk)
+                total += len(dst) * chunk
+            torch.cuda.synchronize(self.device)
+            return total
         pool = self.pool_bytes()
         ar = torch.arange(chunk, device=self.device)
         sends = {}
@@ -270,6 +320,15 @@ class NativeRunner:
 
     def kv_restore(self, my_rank, n, home, fusion_pages, dp_pages, chunk) -> int:
         from ..kv import copy_plan
+        if self.peer_maps:
+            if my_rank != home:
+                return 0          # the home instance pulls
+            base = self.eng.kv_base_ptr()
+            for j in range(n):
+                src, dst = copy_plan.restore_plan(self.layout, n, j, fusion_pages[j], dp_pages)
+                self._pull(base, j, base if j == home else self.peer_maps[j].kv, dst, src, chunk)
+            torch.cuda.synchronize(self.device)
+            return len(dp_pages) * chunk * n
         pool = self.pool_bytes()
         ar = torch.arange(chunk, device=self.device)
         if my_rank != home:

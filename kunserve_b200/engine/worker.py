@@ -130,6 +130,13 @@ class Worker:
         self.step_times.append(time.perf_counter() - t0)
         return out
 
+    def export_memory(self) -> dict:
+        """Share this worker's KV pool and weight segments with group peers."""
+        return self.runner.export_memory() if self.backend == "native" else {}
+
+    def import_peers(self, infos: dict) -> int:
+        return self.runner.import_peers(infos) if self.backend == "native" else 0
+
     def clear_request_resource_batched(self, requests) -> None:
         """The engine keeps no per-request state outside the KV pool."""
 
@@ -212,12 +219,19 @@ class Worker:
         return self.runner.pool.data.view(torch.uint8)
 
     def kv_exchange(self, pages_of_instances: Sequence[Sequence[int]], group_rank: int,
-                    group_size: int) -> int:
-        """Balloon-time reshard (reference N7).  Returns bytes received."""
+                    group_size: int, home_pages: Optional[Sequence[Sequence[int]]] = None) -> int:
+        """Balloon-time reshard (reference N7).  ``home_pages[j]`` (optional)
+        are member j's own whole pages in the order of
+        ``pages_of_instances[j]``; with peer memory mapped, each worker pulls
+        its slices straight from the members' pools.  Returns bytes received."""
         plan_send, plan_recv = copy_plan.reshard_plan(self.layout, group_size, group_rank, pages_of_instances)
         cb = copy_plan.chunk_bytes(self.layout, group_size)
         if self.backend == "native":
-            return self.runner.kv_exchange(plan_send, plan_recv, cb, group_rank, group_size)
+            peer_src = None
+            if home_pages is not None:
+                peer_src = {j: [copy_plan.whole_page_slice_offset(self.layout, b, group_rank, group_size)
+                                for b in home_pages[j]] for j in plan_recv}
+            return self.runner.kv_exchange(plan_send, plan_recv, cb, group_rank, group_size, peer_src)
         pool = self._pool_bytes()
         ar = torch.arange(cb, device=pool.device)
         sends = {}

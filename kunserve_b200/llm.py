@@ -9,6 +9,7 @@ reference's no-op, stops every loop and worker).
 """
 import asyncio
 import itertools
+import os
 import time
 from typing import Dict, List, Optional, Sequence
 
@@ -71,6 +72,8 @@ class AsyncLLM:
                   for gi, insts in enumerate(inst_groups)]
         for g in groups:
             await asyncio.gather(*[i.initialize(num_gpu_blocks=num_gpu_blocks) for i in g.instances])
+            if os.environ.get("KUNSERVE_P2P", "1") != "0":
+                await g.setup_peer_memory()
         llm = cls(cfg, mc, groups, router, server_id, tokenizer)
         llm.start()
         return llm

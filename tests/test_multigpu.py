@@ -68,8 +68,10 @@ def test_tp2_logits_match_oracle(ckpt):
             w.kill()
 
 
-async def _balloon_native():
+async def _balloon_native(p2p: bool):
+    import os
     from kunserve_b200.llm import AsyncLLM
+    os.environ["KUNSERVE_P2P"] = "1" if p2p else "0"
     from kunserve_b200.runtime import aw
     cfg = KunServeConfig()
     e = cfg.engine_config
@@ -82,6 +84,7 @@ async def _balloon_native():
     llm = await AsyncLLM.create(cfg, model_config=mc, backend="native", actor_kind="process",
                                 devices=["cuda:0", "cuda:1"], num_gpu_blocks=96, seed=3)
     g = llm.groups[0]
+    assert g.p2p == p2p
     leader = g.leader
     w0, w1 = leader.workers[0][0], g.instances[1].workers[0][0]
     try:
@@ -129,9 +132,10 @@ async def _balloon_native():
         await llm.terminate()
 
 
-def test_balloon_cycle_two_gpus():
+@pytest.mark.parametrize("p2p", [True, False], ids=["p2p-copy-kernel", "nccl"])
+def test_balloon_cycle_two_gpus(p2p):
     _need2()
-    res = asyncio.run(_balloon_native())
+    res = asyncio.run(_balloon_native(p2p))
     by = {r["request_id"]: r for r in res}
     assert all(len(by[i]["outputs"]) == 60 for i in range(10))
     assert all(len(by[100 + i]["outputs"]) == 20 for i in range(4))
