@@ -190,8 +190,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("layer_segment_bytes", &Engine::layer_segment_bytes)
       .def("layer_ptr", &Engine::layer_ptr)
       .def("init_tp_comm", &Engine::init_tp_comm)
+      .def("init_tp_fused", &Engine::init_tp_fused)
+      .def("tp_rb_ptr", &Engine::tp_rb_ptr)
+      .def("tp_rb_bytes", &Engine::tp_rb_bytes)
+      .def("set_tp_peers", &Engine::set_tp_peers)
+      .def("tp_fused", &Engine::tp_fused)
+      .def("set_tp_fused", &Engine::set_tp_fused)
       .def("launches", &Engine::launches)
       .def("reset_launches", &Engine::reset_launches);
+  py::class_<SharedBuffer>(m, "SharedBuffer")
+      .def(py::init<int, size_t>())
+      .def("ptr", [](const SharedBuffer& b) { return reinterpret_cast<int64_t>(b.ptr()); })
+      .def("bytes", &SharedBuffer::bytes)
+      .def("export_fd", &SharedBuffer::export_fd);
   py::class_<PeerMapping>(m, "PeerMapping")
       .def(py::init<int, int, size_t>())
       .def("ptr", [](const PeerMapping& p) { return reinterpret_cast<int64_t>(p.ptr()); })

@@ -150,6 +150,39 @@ int Arena::export_kv_fd() const {
   return fd;
 }
 
+SharedBuffer::SharedBuffer(int device, size_t bytes) {
+  const auto& d = DriverApi::get();
+  CUmemAllocationProp prop = make_prop(device, true);
+  size_t gran = 0;
+  check_cu(d.memGetAllocationGranularity(&gran, &prop, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED), "granularity");
+  bytes_ = round_up(bytes ? bytes : 1, gran);
+  check_cu(d.memCreate(&h_, bytes_, &prop, 0), "cuMemCreate shared");
+  check_cu(d.memAddressReserve(&va_, bytes_, gran, 0, 0), "reserve shared");
+  check_cu(d.memMap(va_, bytes_, 0, h_, 0), "map shared");
+  CUmemAccessDesc acc{};
+  acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  acc.location.id = device;
+  acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+  check_cu(d.memSetAccess(va_, bytes_, &acc, 1), "access shared");
+}
+
+SharedBuffer::~SharedBuffer() {
+  const auto& d = DriverApi::get();
+  cudaDeviceSynchronize();
+  if (va_) {
+    d.memUnmap(va_, bytes_);
+    d.memAddressFree(va_, bytes_);
+  }
+  if (h_) d.memRelease(h_);
+}
+
+int SharedBuffer::export_fd() const {
+  int fd = -1;
+  check_cu(DriverApi::get().memExportToShareableHandle(&fd, h_, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0),
+           "export shared");
+  return fd;
+}
+
 PeerMapping::PeerMapping(int device, int fd, size_t bytes) : bytes_(bytes) {
   const auto& d = DriverApi::get();
   check_cu(d.memImportFromShareableHandle(&h_, reinterpret_cast<void*>((uintptr_t)fd),

@@ -87,6 +87,22 @@ class Arena {
   bool exportable_ = false;
 };
 
+// A standalone device buffer whose memory can be exported to peer processes
+// (symmetric receive buffers of the fused TP kernels, P2P benchmarks).
+class SharedBuffer {
+ public:
+  SharedBuffer(int device, size_t bytes);
+  ~SharedBuffer();
+  char* ptr() const { return reinterpret_cast<char*>(va_); }
+  size_t bytes() const { return bytes_; }
+  int export_fd() const;
+
+ private:
+  CUmemGenericAllocationHandle h_ = 0;
+  CUdeviceptr va_ = 0;
+  size_t bytes_ = 0;
+};
+
 // Map another process's exported physical memory (fd) into this context.
 class PeerMapping {
  public:

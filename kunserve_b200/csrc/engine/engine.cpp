@@ -297,17 +297,23 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     ++launches_;
   }
   bool pending = false;   // tmp holds an all-reduced partial still to be added to h
+  bool y_ready = false;   // the fused all-reduce already produced this layer's normed input
+  const bool fused = tp && fused_;
   for (int64_t l = layer_start; l < layer_end; ++l) {
     for (int d : dropped) KUS_CHECK(d != l, "step touches a dropped layer");
     const LayerW& W = layers_[l];
     const int ll = (int)(l - layer_start);
-    rmsnorm(h, pending ? tmp : nullptr, W.in_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+    if (!y_ready) rmsnorm(h, pending ? tmp : nullptr, W.in_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+    y_ready = false;
     gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
     rope_append(qkv, positions, kv_page, kv_slot, cos_sin_.data_ptr<float>(), geo, ll, (int)T, s_.nq, s_.nkv,
                 s_.max_pos, st);
     paged_attention(qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
     launches_ += 3 + (splits > 1 ? 1 : 0);
-    if (tp) {
+    if (fused) {
+      tp_push_gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, st);
+      tp_reduce(h, W.post_norm, y, (int)T, st);
+    } else if (tp) {
       gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_BF16, tmp, H, nullptr, st);
       all_reduce(tmp, T * H, st);
       rmsnorm(h, tmp, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
@@ -317,7 +323,13 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     }
     ++launches_;
     gemm(m_y_, W.m_gu, (int)T, 2 * f_pad_, H, EPI_SILU, act, f_pad_, nullptr, st);
-    if (tp) {
+    if (fused) {
+      tp_push_gemm(m_act_, W.m_down, (int)T, H, f_pad_, st);
+      const bool next = l + 1 < layer_end;
+      tp_reduce(h, next ? layers_[l + 1].in_norm : nullptr, y, (int)T, st);
+      y_ready = next;
+      pending = false;
+    } else if (tp) {
       gemm(m_act_, W.m_down, (int)T, H, f_pad_, EPI_BF16, tmp, H, nullptr, st);
       all_reduce(tmp, T * H, st);
       pending = true;
@@ -384,6 +396,60 @@ void Engine::init_tp_comm(const std::vector<int64_t>& uid, int64_t rank, int64_t
   KUS_CHECK(uid.size() == sizeof(id.internal), "nccl unique id size");
   for (size_t i = 0; i < uid.size(); ++i) id.internal[i] = (char)uid[i];
   check_nccl(ncclCommInitRank(&tp_comm_, (int)size, id, (int)rank), "ncclCommInitRank");
+}
+
+// Receive buffer layout: [flags: one u32 per source rank, 4 KB]
+// [parity 0: R slots of max_tokens x H bf16][parity 1: same].
+static constexpr int64_t kRbFlagBytes = 4096;
+
+int64_t Engine::init_tp_fused(int64_t rank) {
+  c10::cuda::CUDAGuard g(device_);
+  tp_rank_ = (int)rank;
+  KUS_CHECK(s_.tp <= kMaxTpPeers, "fused all-reduce supports up to 8 ranks");
+  const int64_t slot = (int64_t)s_.max_tokens * s_.hidden * 2;
+  rb_ = std::make_unique<SharedBuffer>(device_, kRbFlagBytes + 2 * (int64_t)s_.tp * slot);
+  check_cuda(cudaMemset(rb_->ptr(), 0, rb_->bytes()), "zero rb");
+  check_cuda(cudaDeviceSynchronize(), "rb sync");
+  return rb_->export_fd();
+}
+
+void Engine::set_tp_peers(const std::vector<int64_t>& bases) {
+  KUS_CHECK((int)bases.size() == s_.tp, "one receive buffer per TP rank");
+  rb_peers_ = bases;
+  fused_ = true;
+}
+
+void Engine::tp_push_gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, cudaStream_t st) {
+  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, 256, 16);
+  const int box = a_box_rows(p);
+  p.tmA = mA[box == 16 ? 0 : box == 32 ? 1 : box == 64 ? 2 : 3];
+  p.tmB = mB;
+  ++epoch_;
+  const int64_t slot = (int64_t)s_.max_tokens * s_.hidden * 2;
+  const int64_t data = kRbFlagBytes + (int64_t)(epoch_ & 1) * s_.tp * slot + (int64_t)tp_rank_ * slot;
+  for (int q = 0; q < s_.tp; ++q) {
+    p.args.peer_out[q] = reinterpret_cast<void*>(rb_peers_[q] + data);
+    p.args.flag_remote[q] = reinterpret_cast<unsigned*>(rb_peers_[q] + 4 * tp_rank_);
+  }
+  p.args.npeers = s_.tp;
+  p.args.epoch = epoch_;
+  p.args.done_counter = counters_.data_ptr<int>() + (counters_.numel() - 1);
+  p.args.out = nullptr;
+  p.args.ldc = s_.hidden;
+  p.args.workspace = gemm_ws_.data_ptr<float>();
+  p.args.tile_counters = counters_.data_ptr<int>();
+  run_gemm(p, st);
+  ++launches_;
+}
+
+void Engine::tp_reduce(__nv_bfloat16* h, const __nv_bfloat16* w, __nv_bfloat16* y, int T, cudaStream_t st) {
+  const int64_t slot_elems = (int64_t)s_.max_tokens * s_.hidden;
+  const char* base = rb_->ptr();
+  const auto* rb = reinterpret_cast<const __nv_bfloat16*>(base + kRbFlagBytes + (int64_t)(epoch_ & 1) * s_.tp *
+                                                                                  slot_elems * 2);
+  tp_reduce_rmsnorm(rb, s_.tp, slot_elems, h, w, y, T, s_.hidden, (float)s_.eps,
+                    reinterpret_cast<const unsigned*>(base), epoch_, st);
+  ++launches_;
 }
 
 std::vector<int64_t> nccl_unique_id() {

@@ -84,6 +84,14 @@ class Engine {
 
   // NCCL (tensor-parallel all-reduce inside the layer loop).
   void init_tp_comm(const std::vector<int64_t>& unique_id, int64_t rank, int64_t size);
+  // Fused TP all-reduce over peer memory: allocate this rank's receive
+  // buffer (returns an fd to share), then give every rank's mapped base.
+  int64_t init_tp_fused(int64_t rank);
+  int64_t tp_rb_ptr() const { return reinterpret_cast<int64_t>(rb_ ? rb_->ptr() : nullptr); }
+  int64_t tp_rb_bytes() const { return rb_ ? (int64_t)rb_->bytes() : 0; }
+  void set_tp_peers(const std::vector<int64_t>& bases);
+  bool tp_fused() const { return fused_; }
+  void set_tp_fused(bool on) { fused_ = on && rb_ && (int)rb_peers_.size() == s_.tp; }
 
   int64_t launches() const { return launches_; }
   void reset_launches() { launches_ = 0; }
@@ -111,6 +119,13 @@ class Engine {
   int64_t attn_split_tokens_ = 0;
   int attn_max_splits_ = 16;
   ncclComm_t tp_comm_ = nullptr;
+  std::unique_ptr<SharedBuffer> rb_;
+  std::vector<int64_t> rb_peers_;
+  int tp_rank_ = 0;
+  bool fused_ = false;
+  unsigned epoch_ = 0;
+  void tp_push_gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, cudaStream_t s);
+  void tp_reduce(__nv_bfloat16* h, const __nv_bfloat16* w, __nv_bfloat16* y, int T, cudaStream_t s);
   int64_t launches_ = 0;
 };
 

@@ -248,6 +248,82 @@ void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off,
                                                  chunk);
 }
 
+// ------------------------------------- fused TP all-reduce: the reduce side
+// Waits (bounded) until every tensor-parallel rank published `epoch` for the
+// partial it pushed into this rank's receive slots, then
+//   h[row] += sum_p rb[p][row]        (fp32 sum of the bf16 partials)
+//   y[row]  = rmsnorm(h[row]) * w      (when w is given)
+__global__ void tp_reduce_rmsnorm_kernel(const __nv_bfloat16* __restrict__ rb, int R, long long slot_elems,
+                                         __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
+                                         __nv_bfloat16* __restrict__ y, int H, float eps,
+                                         const unsigned* __restrict__ flags, unsigned epoch) {
+  __shared__ float red[32];
+  __shared__ int ok_s;
+  const int row = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int p = 0; p < R && ok; ++p) {
+      for (uint32_t i = 0;; ++i) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + p) : "memory");
+        if ((int)(v - epoch) >= 0) break;
+        if (i >= (kSpinLimit >> 6) || ((i & 255u) == 255u && error_set())) {
+          set_error(kErrPeerFlag, p);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    ok_s = ok;
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const int nv = H / 8;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    float acc[8], t[8];
+    uint4* hp = reinterpret_cast<uint4*>(h + (size_t)row * H) + i;
+    unpack_bf16x8(*hp, acc);
+    for (int p = 0; p < R; ++p) {
+      unpack_bf16x8(__ldcg(reinterpret_cast<const uint4*>(rb + p * slot_elems + (size_t)row * H) + i), t);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += t[k];
+    }
+    const uint4 packed = pack_bf16x8(acc);
+    *hp = packed;
+    unpack_bf16x8(packed, acc);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += acc[k] * acc[k];
+  }
+  if (w == nullptr) return;
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)H + eps);
+  for (int i = threadIdx.x; i < nv; i += blockDim.x) {
+    float a[8], g[8], o[8];
+    unpack_bf16x8(reinterpret_cast<const uint4*>(h + (size_t)row * H)[i], a);
+    unpack_bf16x8(reinterpret_cast<const uint4*>(w)[i], g);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = a[k] * inv * g[k];
+    reinterpret_cast<uint4*>(y + (size_t)row * H)[i] = pack_bf16x8(o);
+  }
+}
+
+void tp_reduce_rmsnorm(const __nv_bfloat16* rb, int R, long long slot_elems, __nv_bfloat16* h,
+                       const __nv_bfloat16* w, __nv_bfloat16* y, int T, int H, float eps, const unsigned* flags,
+                       unsigned epoch, cudaStream_t s) {
+  if (T <= 0) return;
+  tp_reduce_rmsnorm_kernel<<<T, 256, 0, s>>>(rb, R, slot_elems, h, w, y, H, eps, flags, epoch);
+}
+
 // -------------------------------------------------- residual add (TP path)
 __global__ void add_inplace_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y, long long n8) {
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long long)gridDim.x * blockDim.x) {

@@ -7,7 +7,9 @@
 
 namespace kus {
 
-enum GemmEpilogue : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SILU = 2, EPI_ADD = 3 };
+enum GemmEpilogue : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SILU = 2, EPI_ADD = 3, EPI_PUSH = 4 };
+
+constexpr int kMaxTpPeers = 8;
 
 struct GemmArgs {
   int M, N, K;
@@ -19,6 +21,14 @@ struct GemmArgs {
   int ld_res;
   float* workspace;     // split-K partial tiles, fp32 [tiles][split][128][BN]
   int* tile_counters;   // one int per tile, zero between GEMMs
+  // EPI_PUSH (fused tensor-parallel all-reduce): bf16 tiles go to every
+  // rank's receive slot (peer_out[p], row stride ldc); the last CTA then
+  // writes `epoch` to each rank's flag for this sender (flag_remote[p]).
+  void* peer_out[kMaxTpPeers];
+  unsigned* flag_remote[kMaxTpPeers];
+  int npeers;
+  unsigned epoch;
+  int* done_counter;    // CTA completion count, zero between GEMMs
 };
 
 struct GemmPlan {

@@ -44,6 +44,10 @@ KUS_DEVICE void store_col16(const GemmArgs& a, int f, int tok0, const float (&v)
     if (tok >= a.M) break;
     if (EPI == EPI_F32) {
       reinterpret_cast<float*>(a.out)[(size_t)tok * a.ldc + f] = v[i];
+    } else if (EPI == EPI_PUSH) {
+      const __nv_bfloat16 b = f2bf(v[i]);
+      for (int p = 0; p < a.npeers; ++p)
+        reinterpret_cast<__nv_bfloat16*>(a.peer_out[p])[(size_t)tok * a.ldc + f] = b;
     } else {
       float x = v[i];
       if (EPI == EPI_ADD) x += bf2f(a.residual[(size_t)tok * a.ld_res + f]);
@@ -266,6 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if (EPI == EPI_PUSH && warp >= 2) signal_push_done(args, threadIdx.x - 64);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
@@ -297,6 +302,7 @@ void run_gemm_swap(const GemmPlan& p, cudaStream_t s) {
   using namespace gemm_swap_impl;
   switch (p.epi) {
     case EPI_F32: launch_swap_bnt<EPI_F32>(p, s); break;
+    case EPI_PUSH: launch_swap_bnt<EPI_PUSH>(p, s); break;
     case EPI_SILU: launch_swap_bnt<EPI_SILU>(p, s); break;
     case EPI_ADD: launch_swap_bnt<EPI_ADD>(p, s); break;
     default: launch_swap_bnt<EPI_BF16>(p, s); break;

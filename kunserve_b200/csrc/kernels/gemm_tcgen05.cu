@@ -58,6 +58,25 @@ KUS_DEVICE void store16(const GemmArgs& a, int row, int col, const float (&v)[16
     }
     return;
   }
+  if (EPI == EPI_PUSH) {
+    float lo[8], hi[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      lo[i] = v[i];
+      hi[i] = v[8 + i];
+    }
+    const uint4 u0 = pack_bf16x8(lo), u1 = pack_bf16x8(hi);
+    for (int p = 0; p < a.npeers; ++p) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]) + (size_t)row * a.ldc + col;
+      if (col + 16 <= a.n_out) {
+        *reinterpret_cast<uint4*>(dst) = u0;
+        *reinterpret_cast<uint4*>(dst + 8) = u1;
+      } else {
+        for (int i = 0; i < 16 && col + i < a.n_out; ++i) dst[i] = f2bf(v[i]);
+      }
+    }
+    return;
+  }
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)row * a.ldc + col;
   float w[16];
 #pragma unroll
@@ -91,6 +110,27 @@ KUS_DEVICE void store16(const GemmArgs& a, int row, int col, const float (&v)[16
     for (int i = 0; i < 16 && col + i < a.n_out; ++i) out[i] = f2bf(w[i]);
   }
 }
+
+}  // namespace gemm_impl
+
+// Every epilogue thread of a CTA calls this once its pushes are issued: the
+// CTA's stores are fenced system-wide, the CTA is counted, and the last CTA
+// of the grid publishes `epoch` to every rank's flag slot for this sender.
+KUS_DEVICE void signal_push_done(const GemmArgs& a, int et) {
+  __threadfence_system();
+  named_barrier(1, 128);
+  if (et == 0) {
+    const int prev = atomicAdd(a.done_counter, 1);
+    if (prev == (int)(gridDim.x - 1)) {
+      *a.done_counter = 0;
+      __threadfence_system();
+      for (int p = 0; p < a.npeers; ++p)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.flag_remote[p]), "r"(a.epoch) : "memory");
+    }
+  }
+}
+
+namespace gemm_impl {
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -325,6 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+  if (EPI == EPI_PUSH && warp >= 2) signal_push_done(args, threadIdx.x - 64);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
@@ -460,6 +501,7 @@ void run_gemm(const GemmPlan& p, cudaStream_t s) {
   }
   switch (p.epi) {
     case EPI_F32: launch_bn<EPI_F32>(p, s); break;
+    case EPI_PUSH: launch_bn<EPI_PUSH>(p, s); break;
     case EPI_SILU: launch<256, EPI_SILU>(p, s); break;
     case EPI_ADD: launch_bn<EPI_ADD>(p, s); break;
     default: launch_bn<EPI_BF16>(p, s); break;

@@ -47,6 +47,10 @@ void sample(const float* logits, int B, int V, int ld, const float* temp, const 
 void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off, const long long* src_off, int n,
                  long long chunk, int max_blocks, cudaStream_t s);
 void add_inplace(__nv_bfloat16* x, const __nv_bfloat16* y, long long n, cudaStream_t s);
+// Reduce side of the fused tensor-parallel all-reduce (see elementwise.cu).
+void tp_reduce_rmsnorm(const __nv_bfloat16* rb, int R, long long slot_elems, __nv_bfloat16* h,
+                       const __nv_bfloat16* w, __nv_bfloat16* y, int T, int H, float eps, const unsigned* flags,
+                       unsigned epoch, cudaStream_t s);
 
 // Paged attention over a ragged batch (prefill chunks and decodes mixed).
 struct AttnBatch {
