@@ -8,6 +8,7 @@ hidden buffer.
 """
 import itertools
 import math
+import os
 from typing import List, Optional, Tuple
 
 import numpy as np
@@ -102,6 +103,8 @@ class NativeRunner:
             self.eng = C.Engine(sh, dev)
             if pc.tensor_parallel_size > 1:
                 self._init_tp_comm(dev)
+                if os.environ.get("KUNSERVE_TP_FUSED", "1") != "0":
+                    self._init_tp_fused(dev)
             self.eng.init_memory(layout.num_pages)
             assert self.eng.page_bytes() == layout.page_stride, (self.eng.page_bytes(), layout.page_stride)
             if weights is not None:
@@ -134,6 +137,34 @@ class NativeRunner:
         dist.broadcast_object_list(uid, src=self.comm.peer("tp", 0), group=self.comm.groups["tp"],
                                    device=torch.device("cuda", dev))
         self.eng.init_tp_comm(uid[0], self.pc.tensor_parallel_rank, self.pc.tensor_parallel_size)
+
+    def _init_tp_fused(self, dev: int) -> None:
+        """Receive buffers of the fused GEMM + all-reduce: every TP rank
+        exports its buffer, maps all the others, and gives the engine the
+        bases indexed by rank."""
+        import torch.distributed as dist
+        from ..parallel.peer import FdServer, fetch_fds
+        rank, size = self.pc.tensor_parallel_rank, self.pc.tensor_parallel_size
+        server = FdServer([self.eng.init_tp_fused(rank)])
+        infos = [None] * size
+        group = self.comm.groups["tp"]
+        dist.all_gather_object(infos, {"sock": server.path, "bytes": self.eng.tp_rb_bytes()}, group=group)
+        bases = []
+        self._rb_maps = []
+        for r, info in enumerate(infos):
+            if r == rank:
+                bases.append(self.eng.tp_rb_ptr())
+                continue
+            fd = fetch_fds(info["sock"])[0]
+            try:
+                m = self.C.PeerMapping(dev, fd, info["bytes"])
+            finally:
+                os.close(fd)
+            self._rb_maps.append(m)
+            bases.append(m.ptr())
+        dist.barrier(group=group, device_ids=[dev])
+        server.close()
+        self.eng.set_tp_peers(bases)
 
     def load_weights(self, w) -> None:
         for l, lw in enumerate(w.layers):

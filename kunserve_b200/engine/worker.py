@@ -342,6 +342,16 @@ class Worker:
         idx = pool.block_view_index(torch.tensor([page_id]), local_layer, fusion_size, False)
         return pool.data[idx].clone()
 
+    def tp_fused(self) -> bool:
+        return self.backend == "native" and bool(self.runner.eng.tp_fused())
+
+    def device_error(self) -> int:
+        """Device error flag of this worker's kernels (0 = none); clears it."""
+        if self.backend != "native":
+            return 0
+        from ..ops import native
+        return int(native().error_flag(True))
+
     def last_logits(self, n: int) -> torch.Tensor:
         """fp32 logits of the last step's ``n`` rows (left by sample mode 1)."""
         return self.runner.eng.logits()[:n].float().cpu()

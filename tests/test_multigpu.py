@@ -34,8 +34,11 @@ def ckpt(tmp_path_factory):
     return mc, out
 
 
-def test_tp2_logits_match_oracle(ckpt):
+@pytest.mark.parametrize("fused", [True, False], ids=["fused-p2p-allreduce", "nccl-allreduce"])
+def test_tp2_logits_match_oracle(ckpt, fused):
     _need2()
+    import os
+    os.environ["KUNSERVE_TP_FUSED"] = "1" if fused else "0"
     from kunserve_b200.bootstrap import build_instances
     from kunserve_b200.config import CacheConfig, SchedConfig
     from kunserve_b200.engine.step import StepInput
@@ -55,7 +58,13 @@ def test_tp2_logits_match_oracle(ckpt):
         step = StepInput([0, 1], prompts, [0, 0], [[0, 1], [2, 3, 4]], [1, 1], 0, 2, temperature=[0.0, 0.0],
                          top_k=[3, 3], top_p=[1.0, 1.0], seeds=[0, 1])
         get([w.step.remote(step) for w in workers], timeout=600)
+        assert get(workers[0].tp_fused.remote(), timeout=60) == fused
         got = get(workers[0].last_logits.remote(2), timeout=60)
+        # a decode step on top (small M: the swapped kernel pushes)
+        step2 = StepInput([0, 1], [[7], [9]], [17, 40], [[0, 1], [2, 3, 4]], [0, 0], 0, 2, temperature=[0.0, 0.0],
+                          top_k=[3, 3], top_p=[1.0, 1.0], seeds=[0, 1], step_id=1)
+        get([w.step.remote(step2) for w in workers], timeout=600)
+        got2 = get(workers[0].last_logits.remote(2), timeout=60)
         full = load_converted(path, mc, ParallelConfig(), torch.bfloat16, device="cuda:0")
         s = full.shapes
         ref = TorchLlama(full, PagedKVPool(KVLayout(16, 2, 16, s.kv_heads, s.head_dim, 2), torch.bfloat16, "cuda:0"),
@@ -63,6 +72,10 @@ def test_tp2_logits_match_oracle(ckpt):
         want = ref.logits(ref.forward_hidden(step), step).cpu()
         rel = ((got - want).norm() / want.norm()).item()
         assert rel < 3e-2, rel
+        want2 = ref.logits(ref.forward_hidden(step2), step2).cpu()
+        rel2 = ((got2 - want2).norm() / want2.norm()).item()
+        assert rel2 < 3e-2, rel2
+        assert get([w.device_error.remote() for w in workers], timeout=60) == [0, 0]
     finally:
         for w in workers:
             w.kill()
