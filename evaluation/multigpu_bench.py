@@ -1,0 +1,179 @@
+"""Multi-GPU kernel sweep (the benchmark configuration's kernel sweep):
+
+* fused tensor-parallel GEMM + all-reduce (push epilogue over NVLink +
+  reduce) against cuBLAS GEMM + NCCL all-reduce, for the row-parallel
+  projections (o_proj: K = H/tp; down_proj: K = F/tp) at M tokens;
+* paged KV-block migration (blocks of 16 tokens x 8 KV heads x 128 dim, K and
+  V) and parameter restore (contiguous bytes) pulled by the copy kernel from
+  a peer's mapped memory, against NCCL send/recv of the same bytes.
+
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
+        evaluation/multigpu_bench.py --what tp --tokens 1 16 256 4096 --hidden 4096
+
+Times are CUDA-event times on each rank, reported as the max over ranks.
+Fractions are of the roofline max(FLOPs / measured bf16 peak, bytes that
+must cross NVLink / 770 GB/s per direction).
+"""
+import argparse
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+LINK = 770e9     # measured peer copy, bytes/s per direction
+
+
+def peak_flops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p))["bf16_tflops"] * 1e12, "measured"
+    return 1.59e15, "fallback"
+
+
+def tmax(ms, dev):
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_ms(fn, warmup, iters, dev):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize(dev)
+    return tmax(s.elapsed_time(e) / iters, dev)
+
+
+def share(C, dev, nbytes, rank, world):
+    """An exportable buffer per rank; returns (own buffer, [base per rank], keep-alive)."""
+    from kunserve_b200.parallel.peer import FdServer, fetch_fds
+    buf = C.SharedBuffer(dev, nbytes)
+    srv = FdServer([buf.export_fd()])
+    infos = [None] * world
+    dist.all_gather_object(infos, {"sock": srv.path, "bytes": buf.bytes()})
+    bases, keep = [], [buf]
+    for r, info in enumerate(infos):
+        if r == rank:
+            bases.append(buf.ptr())
+            continue
+        fd = fetch_fds(info["sock"])[0]
+        m = C.PeerMapping(dev, fd, info["bytes"])
+        os.close(fd)
+        keep.append(m)
+        bases.append(m.ptr())
+    dist.barrier()
+    srv.close()
+    return bases, keep
+
+
+def bench_tp(args, C, dev, rank, world):
+    peak, src = peak_flops()
+    for H in args.hidden:
+        for kind, K_full in (("o_proj", H), ("down_proj", args.ffn.get(H, 4 * H))):
+            K = K_full // world
+            max_m = max(args.tokens)
+            bases, keep = share(C, dev, 4096 + 2 * world * max_m * H * 2, rank, world)
+            W = (torch.randn(H, K, device=dev) * 0.02).bfloat16()
+            ws = torch.empty(148 * 16 * 128 * 256, device=dev)
+            counters = torch.zeros(1 << 16, device=dev, dtype=torch.int32)
+            epoch = [0]
+            for M in args.tokens:
+                A = torch.randn(M, K, device=dev).bfloat16()
+                h = torch.zeros(M, H, device=dev, dtype=torch.bfloat16)
+                y = torch.empty_like(h)
+
+                def fused():
+                    epoch[0] += 1
+                    C.tp_gemm_allreduce(A, W, h, None, y, bases, rank, max_m, epoch[0], counters, ws)
+
+                def baseline():
+                    out = torch.matmul(A, W.t())
+                    dist.all_reduce(out)
+                    h.add_(out)
+
+                tf = time_ms(fused, args.warmup, args.iters, dev)
+                tb = time_ms(baseline, args.warmup, args.iters, dev)
+                flops = 2.0 * M * H * K
+                link_bytes = 2.0 * (world - 1) / world * M * H * 2
+                roof = max(flops / peak, link_bytes / LINK) * 1e3
+                if rank == 0:
+                    print(json.dumps({"kernel": f"fused_gemm_allreduce_{kind}", "tp": world, "M": M, "H": H,
+                                      "K": K, "fused_us": round(tf * 1e3, 2), "cublas_nccl_us": round(tb * 1e3, 2),
+                                      "speedup": round(tb / tf, 3), "roofline_us": round(roof * 1e3, 2),
+                                      "roofline_frac": round(roof / tf, 3), "peaks": src}), flush=True)
+            del keep
+
+
+def bench_copy(args, C, dev, rank, world):
+    block = 16 * 8 * 128 * 2 * 2            # K and V of one layer
+    for nblocks in args.blocks:
+        nbytes = nblocks * block
+        bases, keep = share(C, dev, nbytes, rank, world)
+        local = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+        peer = (rank + 1) % world
+        perm = torch.randperm(nblocks, device=dev).to(torch.int64) * block
+        seq = torch.arange(nblocks, device=dev, dtype=torch.int64) * block
+
+        def pull():
+            C.copy_chunks(local.data_ptr(), bases[peer], seq, perm, block, 4 * 148)
+
+        recv = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+        send = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+
+        def nccl():
+            ops = [dist.P2POp(dist.isend, send, peer), dist.P2POp(dist.irecv, recv, (rank - 1) % world)]
+            for r in dist.batch_isend_irecv(ops):
+                r.wait()
+
+        tp_ = time_ms(pull, args.warmup, args.iters, dev)
+        tn = time_ms(nccl, args.warmup, args.iters, dev)
+        if rank == 0:
+            print(json.dumps({"kernel": "p2p_kv_block_migration", "blocks": nblocks, "block_bytes": block,
+                              "GB": round(nbytes / 1e9, 3), "p2p_us": round(tp_ * 1e3, 1),
+                              "nccl_us": round(tn * 1e3, 1), "p2p_GB_s": round(nbytes / tp_ / 1e6, 1),
+                              "nccl_GB_s": round(nbytes / tn / 1e6, 1), "link_frac": round(nbytes / tp_ / 1e6 / 770, 3)}),
+                  flush=True)
+        del keep
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--what", choices=["tp", "copy", "all"], default="all")
+    p.add_argument("--tokens", type=int, nargs="+", default=[1, 16, 256, 4096])
+    p.add_argument("--hidden", type=int, nargs="+", default=[4096, 5120, 8192])
+    p.add_argument("--blocks", type=int, nargs="+", default=[1024, 16384, 65536])
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--iters", type=int, default=10)
+    a = p.parse_args()
+    a.ffn = {4096: 14336, 5120: 13824, 8192: 28672}
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from datetime import timedelta
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from kunserve_b200.ops import check_error, native
+    C = native()
+    try:
+        if a.what in ("tp", "all"):
+            bench_tp(a, C, local, rank, world)
+        if a.what in ("copy", "all"):
+            bench_copy(a, C, local, rank, world)
+        check_error()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -138,6 +138,39 @@ void copy_chunks_op(int64_t dst_ptr, int64_t src_ptr, torch::Tensor dst_off, tor
               reinterpret_cast<const long long*>(src_off.data_ptr<int64_t>()), dst_off.numel(), chunk, (int)max_blocks, at::cuda::getCurrentCUDAStream());
 }
 
+// One fused tensor-parallel GEMM + all-reduce for benchmarks and tests:
+// pushes A @ B^T into every rank's receive buffer (bases[r], slot `rank`,
+// parity `epoch & 1`), then reduces into h (and RMSNorm into y if w given).
+void tp_gemm_allreduce_op(torch::Tensor A, torch::Tensor B, torch::Tensor h, c10::optional<torch::Tensor> w,
+                          torch::Tensor y, std::vector<int64_t> bases, int64_t rank, int64_t max_tokens,
+                          int64_t epoch, torch::Tensor counters, torch::Tensor ws) {
+  CHECK_CUDA_BF16(A);
+  CHECK_CUDA_BF16(B);
+  c10::cuda::CUDAGuard g(A.device());
+  const int M = A.size(0), K = A.size(1), N = B.size(0), R = (int)bases.size();
+  TORCH_CHECK(R <= kMaxTpPeers && M <= max_tokens, "tp_gemm_allreduce sizes");
+  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, 256, 16);
+  TORCH_CHECK(workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn) <= (size_t)ws.numel(), "ws");
+  const int64_t slot = max_tokens * N * 2, flags = 4096;
+  const int64_t data = flags + (epoch & 1) * R * slot + rank * slot;
+  for (int q = 0; q < R; ++q) {
+    p.args.peer_out[q] = reinterpret_cast<void*>(bases[q] + data);
+    p.args.flag_remote[q] = reinterpret_cast<unsigned*>(bases[q] + 4 * rank);
+  }
+  p.args.npeers = R;
+  p.args.epoch = (unsigned)epoch;
+  p.args.done_counter = counters.data_ptr<int>() + (counters.numel() - 1);
+  TORCH_CHECK(finalize_plan(p, A.data_ptr(), K, B.data_ptr(), K, nullptr, N, nullptr, N, ws.data_ptr<float>(),
+                            counters.data_ptr<int>()),
+              "tensor map encoding failed");
+  auto st = at::cuda::getCurrentCUDAStream();
+  run_gemm(p, st);
+  const char* base = reinterpret_cast<const char*>(bases[rank]);
+  tp_reduce_rmsnorm(reinterpret_cast<const __nv_bfloat16*>(base + flags + (epoch & 1) * R * slot), R,
+                    max_tokens * N, bp(h), w.has_value() ? bp(*w) : nullptr, bp(y), M, N, 1e-5f,
+                    reinterpret_cast<const unsigned*>(base), (unsigned)epoch, st);
+}
+
 void fill_normal_op(torch::Tensor t, int64_t seed, double std) {
   CHECK_CUDA_BF16(t);
   c10::cuda::CUDAGuard g(t.device());
@@ -196,6 +229,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("set_tp_peers", &Engine::set_tp_peers)
       .def("tp_fused", &Engine::tp_fused)
       .def("set_tp_fused", &Engine::set_tp_fused)
+      .def("set_tp_fused_max_tokens", &Engine::set_tp_fused_max_tokens)
       .def("launches", &Engine::launches)
       .def("reset_launches", &Engine::reset_launches);
   py::class_<SharedBuffer>(m, "SharedBuffer")
@@ -215,6 +249,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample_op);
   m.def("embed", &embed_op);
   m.def("copy_chunks", &copy_chunks_op);
+  m.def("tp_gemm_allreduce", &tp_gemm_allreduce_op);
   m.def("fill_normal", &fill_normal_op);
   m.def("nccl_unique_id", &nccl_unique_id);
   m.def("error_flag", &read_error_flag, py::arg("reset") = true);

@@ -298,7 +298,8 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   }
   bool pending = false;   // tmp holds an all-reduced partial still to be added to h
   bool y_ready = false;   // the fused all-reduce already produced this layer's normed input
-  const bool fused = tp && fused_;
+  // the push epilogue wins at decode sizes; NCCL's ring wins for large steps
+  const bool fused = tp && fused_ && T <= fused_max_tokens_;
   for (int64_t l = layer_start; l < layer_end; ++l) {
     for (int d : dropped) KUS_CHECK(d != l, "step touches a dropped layer");
     const LayerW& W = layers_[l];

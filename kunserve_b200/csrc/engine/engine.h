@@ -92,6 +92,7 @@ class Engine {
   void set_tp_peers(const std::vector<int64_t>& bases);
   bool tp_fused() const { return fused_; }
   void set_tp_fused(bool on) { fused_ = on && rb_ && (int)rb_peers_.size() == s_.tp; }
+  void set_tp_fused_max_tokens(int64_t t) { fused_max_tokens_ = t; }
 
   int64_t launches() const { return launches_; }
   void reset_launches() { launches_ = 0; }
@@ -123,6 +124,7 @@ class Engine {
   std::vector<int64_t> rb_peers_;
   int tp_rank_ = 0;
   bool fused_ = false;
+  int64_t fused_max_tokens_ = 32;
   unsigned epoch_ = 0;
   void tp_push_gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, cudaStream_t s);
   void tp_reduce(__nv_bfloat16* h, const __nv_bfloat16* w, __nv_bfloat16* y, int T, cudaStream_t s);

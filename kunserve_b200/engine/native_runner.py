@@ -165,6 +165,7 @@ class NativeRunner:
         dist.barrier(group=group, device_ids=[dev])
         server.close()
         self.eng.set_tp_peers(bases)
+        self.eng.set_tp_fused_max_tokens(int(os.environ.get("KUNSERVE_TP_FUSED_MAX_TOKENS", "32")))
 
     def load_weights(self, w) -> None:
         for l, lw in enumerate(w.layers):

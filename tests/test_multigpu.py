@@ -39,6 +39,7 @@ def test_tp2_logits_match_oracle(ckpt, fused):
     _need2()
     import os
     os.environ["KUNSERVE_TP_FUSED"] = "1" if fused else "0"
+    os.environ["KUNSERVE_TP_FUSED_MAX_TOKENS"] = "4096"     # exercise the fused path on the prefill step too
     from kunserve_b200.bootstrap import build_instances
     from kunserve_b200.config import CacheConfig, SchedConfig
     from kunserve_b200.engine.step import StepInput
