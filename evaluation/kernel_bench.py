@@ -87,27 +87,39 @@ def bench_attention(args):
             lay = KVLayout(P, L, bs, nkv, hd, 2)
             pool = torch.randn(lay.base_bytes // 2, device="cuda").bfloat16()
             tables = [list(range(i * pages_per, (i + 1) * pages_per)) for i in range(B)]
-            q = torch.randn(B, nq * hd, device="cuda").bfloat16()
-            step = StepInput(list(range(B)), [[0]] * B, [ctx - 1] * B, tables, [0] * B, 0, 1)
-            buf = np.zeros(4 * B + 2 * B + 64 + B * pages_per + 16 * B, dtype=np.int32)
-            _, T, _, n_items, _ = pack_meta(step, bs, nq // nkv, pages_per, buf)
+            ql = args.qlen
+            T = B * ql
+            q = torch.randn(T, nq * hd, device="cuda").bfloat16()
+            step = StepInput(list(range(B)), [[0] * ql] * B, [ctx - ql] * B, tables, [int(ql > 1)] * B, 0, 1)
+            buf = np.zeros(2 * (T * (nq // nkv) // 64 + B + 1) + 4 * T + 6 * B + 64 + B * pages_per, dtype=np.int32)
+            n_int, T, _, n_items, _, n_dec = pack_meta(step, bs, nq // nkv, pages_per, buf)
+            dec = torch.from_numpy(buf[n_int - n_dec:n_int].copy()).cuda()
             items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
             o = 2 * n_items + 4 * T
             q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
             ctxl = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
             tab = torch.tensor(tables, dtype=torch.int32, device="cuda")
-            splits = int(max(1, min(16, math.ceil(2 * 148 / (n_items * nkv)), ctx // 128))) if args.splits < 0 \
-                else args.splits
-            out = torch.empty(B, nq * hd, device="cuda", dtype=torch.bfloat16)
-            op = torch.empty(splits * B * nq * hd, device="cuda")
-            ml = torch.empty(splits * B * nq * 2, device="cuda")
+            if n_dec:
+                splits = int(max(1, min(32, math.ceil(4 * 148 / (n_dec * nkv)), ctx // 256, 1024 // n_dec)))
+            else:
+                splits = 1
+            if args.splits > 0:
+                splits = args.splits
+            out = torch.empty(T, nq * hd, device="cuda", dtype=torch.bfloat16)
+            op = torch.empty(max(splits, 1) * T * nq * hd, device="cuda")
+            ml = torch.empty(max(splits, 1) * T * nq * 2, device="cuda")
             fn = lambda i: C.attention(q, nq * hd, out, pool, P, 1, L, L, bs, nkv, 0, q_start, ctxl, tab, items,
-                                       splits, op, ml, nq, 1 / math.sqrt(hd))
+                                       1, op, ml, nq, 1 / math.sqrt(hd), dec, splits, op, ml)
             t = timeit(fn, args.warmup, args.iters)
             kv_bytes = B * ctx * nkv * hd * 2 * 2
-            print(json.dumps({"kernel": "paged_attention_decode", "B": B, "ctx": ctx, "nq": nq, "nkv": nkv,
-                              "splits": splits, "us": round(t * 1e6, 2), "TB_s": round(kv_bytes / t / 1e12, 3),
-                              "bw_frac": round(kv_bytes / t / bw, 3), "peaks": src}), flush=True)
+            # causal FLOPs: query i of a request sees (ctx - ql + i + 1) keys; QK^T and PV, 2 FLOP per MAC
+            keys = sum(ctx - ql + i + 1 for i in range(ql))
+            flops = 4.0 * B * keys * nq * hd
+            print(json.dumps({"kernel": "paged_attention_" + ("decode" if ql == 1 else "prefill"), "B": B,
+                              "ctx": ctx, "qlen": ql, "nq": nq, "nkv": nkv, "splits": splits,
+                              "us": round(t * 1e6, 2), "TB_s": round(kv_bytes / t / 1e12, 3),
+                              "bw_frac": round(kv_bytes / t / bw, 3), "TFLOP_s": round(flops / t / 1e12, 1),
+                              "flop_frac": round(flops / t / fl, 3), "peaks": src}), flush=True)
 
 
 def bench_copy(args):
@@ -142,6 +154,7 @@ def main():
     p.add_argument("--nq", type=int, default=32)
     p.add_argument("--nkv", type=int, default=8)
     p.add_argument("--splits", type=int, default=-1)
+    p.add_argument("--qlen", type=int, default=1, help="query tokens per request (1 = decode)")
     p.add_argument("--chunks", type=int, nargs="+", default=[1024, 16384])
     p.add_argument("--chunk-bytes", type=int, default=65536)
     p.add_argument("--warmup", type=int, default=5)

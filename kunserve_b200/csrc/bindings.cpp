@@ -102,7 +102,8 @@ void rope_append_op(torch::Tensor qkv, torch::Tensor positions, torch::Tensor pa
 void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::Tensor pool, int64_t P, int64_t N,
                   int64_t Ls, int64_t L, int64_t block_size, int64_t nkv, int64_t layer, torch::Tensor q_start,
                   torch::Tensor ctx_len, torch::Tensor page_table, torch::Tensor items, int64_t splits,
-                  torch::Tensor o_part, torch::Tensor ml_part, int64_t nq, double scale) {
+                  torch::Tensor o_part, torch::Tensor ml_part, int64_t nq, double scale, torch::Tensor dec_reqs,
+                  int64_t dec_splits, torch::Tensor dec_o, torch::Tensor dec_ml) {
   c10::cuda::CUDAGuard g(q.device());
   KVGeom geo = make_geom(pool, P, N, Ls, L, block_size, nkv, 128);
   AttnBatch b;
@@ -113,7 +114,11 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
   b.items = reinterpret_cast<const int2*>(items.data_ptr<int>());
   b.n_items = items.size(0);
   b.splits = (int)splits;
-  AttnScratch sc{o_part.data_ptr<float>(), ml_part.data_ptr<float>()};
+  b.dec_reqs = dec_reqs.data_ptr<int>();
+  b.n_dec = dec_reqs.numel();
+  b.dec_splits = (int)dec_splits;
+  AttnScratch sc{o_part.data_ptr<float>(), ml_part.data_ptr<float>(), dec_o.data_ptr<float>(),
+                 dec_ml.data_ptr<float>()};
   paged_attention(bp(q), (int)q_stride, bp(out), geo, (int)layer, b, sc, q.size(0), (int)nq, (float)scale,
                   at::cuda::getCurrentCUDAStream());
 }

@@ -22,6 +22,9 @@ static void check_nccl(ncclResult_t r, const char* what) {
 
 static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
+// decode attention splits x decode requests per step (partials scratch)
+static constexpr int64_t kDecSplitSlots = 1024;
+
 // Byte layout of one layer segment: in_norm, post_norm, qkv, o, gu (interleaved), down.
 struct LayerLayout {
   size_t in_norm, post_norm, qkv, o, gu, down, total;
@@ -68,6 +71,8 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   attn_split_tokens_ = std::min<int64_t>(T, 512);
   attn_o_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * s.hd}, f32);
   attn_ml_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * 2}, f32);
+  dec_o_ = torch::empty({kDecSplitSlots * s.nq * s.hd}, f32);
+  dec_ml_ = torch::empty({kDecSplitSlots * s.nq * 2}, f32);
   const int64_t max_items = T * std::max(1, s.nq / s.nkv) / 64 + B + 1;
   const int64_t meta_ints = 2 * max_items + 4 * T + 5 * B + 1 +
                             B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + 64;
@@ -233,7 +238,7 @@ void Engine::all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t st) {
 }
 
 std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, int64_t max_pages, int64_t n_items,
-                                     int64_t splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
+                                     int64_t splits, int64_t n_dec, int64_t dec_splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
                                      bool first_stage, bool last_stage, int64_t sample_mode, int64_t step) {
   c10::cuda::CUDAGuard g(device_);
   KUS_CHECK(T > 0 && T <= s_.max_tokens, "step tokens exceed max_tokens");
@@ -242,7 +247,9 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   KUS_CHECK(splits >= 1 && splits <= attn_max_splits_, "bad attention split");
   KUS_CHECK(splits == 1 || T <= attn_split_tokens_, "split attention only for small steps");
   cudaStream_t st = at::cuda::getCurrentCUDAStream(device_);
-  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 2 * B;
+  KUS_CHECK(n_dec >= 0 && n_dec <= B && dec_splits >= 1 && dec_splits * n_dec <= kDecSplitSlots,
+            "bad decode attention split");
+  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 2 * B + n_dec;
   KUS_CHECK(meta.numel() >= n_meta && n_meta <= meta_dev_.numel(), "meta buffer too small");
   check_cuda(cudaMemcpyAsync(meta_dev_.data_ptr(), meta.data_ptr(), n_meta * 4, cudaMemcpyHostToDevice, st), "meta H2D");
   // meta layout (int32): items[2n] | tokens[T] | positions[T] | kv_page[T] | kv_slot[T] |
@@ -259,6 +266,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   const int* table = last_idx + B;
   const float* temps = reinterpret_cast<const float*>(table + B * max_pages);
   const unsigned* seeds = reinterpret_cast<const unsigned*>(temps + B);
+  const int* dec_reqs = reinterpret_cast<const int*>(seeds + B);
 
   KVGeom geo;
   geo.base = arena_->kv_base();
@@ -279,7 +287,11 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   ab.items = items;
   ab.n_items = (int)n_items;
   ab.splits = (int)splits;
-  AttnScratch sc{attn_o_.data_ptr<float>(), attn_ml_.data_ptr<float>()};
+  ab.dec_reqs = dec_reqs;
+  ab.n_dec = (int)n_dec;
+  ab.dec_splits = (int)dec_splits;
+  AttnScratch sc{attn_o_.data_ptr<float>(), attn_ml_.data_ptr<float>(), dec_o_.data_ptr<float>(),
+                 dec_ml_.data_ptr<float>()};
 
   const int H = s_.hidden;
   auto* h = reinterpret_cast<__nv_bfloat16*>(h_.data_ptr());

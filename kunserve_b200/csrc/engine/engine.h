@@ -62,7 +62,7 @@ class Engine {
   // One step.  `meta` is a pinned int32 tensor laid out by the Python runner
   // (see native_runner.py); returns sampled ids on the last stage.
   std::vector<int64_t> forward(torch::Tensor meta, int64_t T, int64_t B, int64_t max_pages, int64_t n_items,
-                               int64_t splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
+                               int64_t splits, int64_t n_dec, int64_t dec_splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
                                bool first_stage, bool last_stage, int64_t sample_mode, int64_t step);
   torch::Tensor hidden();                   // [max_tokens, H] residual stream (PP transfer)
   torch::Tensor logits();                   // [max_batch, V] fp32
@@ -114,7 +114,7 @@ class Engine {
   CUtensorMap m_lm_head_;
   // workspaces
   torch::Tensor h_, y_, qkv_, attn_, act_, tmp_, ylast_, logits_, gemm_ws_, counters_, attn_o_, attn_ml_,
-      meta_dev_, tokens_dev_, tokens_host_, cos_sin_;
+      meta_dev_, tokens_dev_, tokens_host_, cos_sin_, dec_o_, dec_ml_;
   // activation TMA descriptors per token-box height (16, 32, 64, 128 rows)
   CUtensorMap m_y_[4], m_attn_[4], m_act_[4], m_ylast_[4];
   int64_t attn_split_tokens_ = 0;

@@ -7,6 +7,7 @@
 #include "gemm_swap.cu"
 #include "elementwise.cu"
 #include "attention.cu"
+#include "attention_decode.cu"
 #include "init.cu"
 
 namespace kus {

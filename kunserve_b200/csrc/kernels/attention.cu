@@ -288,6 +288,7 @@ int attention_q_rows_per_tile() { return attn::TQ; }
 
 void paged_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
                      const AttnBatch& b, const AttnScratch& sc, int T, int nq, float scale, cudaStream_t s) {
+  paged_decode_attention(q, q_stride, out, g, layer, b, sc, nq, scale, s);
   if (b.n_items <= 0) return;
   constexpr int smem = 5 * attn::kTileBytes;
   static bool attr = false;

@@ -58,14 +58,19 @@ struct AttnBatch {
   const int* ctx_len;     // [B] keys visible to the last query (start + n)
   const int* page_table;  // [B, max_pages]
   int max_pages;
-  const int2* items;      // [n_items] (request, first q row of the tile)
+  const int2* items;      // [n_items] (request, first q row of the tile): prefill chunks, mma kernel
   int n_items;
   int splits;             // KV splits per item (>1: partials + combine)
+  const int* dec_reqs;    // [n_dec] requests with one query token: decode kernel
+  int n_dec;
+  int dec_splits;         // KV splits per decode request
 };
 
 struct AttnScratch {
   float* o_part;          // [splits, T, nq, hd]
   float* ml_part;         // [splits, T, nq, 2]
+  float* dec_o;           // [dec_splits, n_dec, nq, hd]
+  float* dec_ml;          // [dec_splits, n_dec, nq, 2]
 };
 
 // q: [T, q_stride] bf16 (first nq*hd columns are the rotated queries);
@@ -73,6 +78,10 @@ struct AttnScratch {
 void paged_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
                      const AttnBatch& b, const AttnScratch& sc, int T, int nq, float scale, cudaStream_t s);
 int attention_q_rows_per_tile();
+// Decode requests of the batch only (attention_decode.cu); paged_attention
+// calls it after the prefill items.
+void paged_decode_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
+                            const AttnBatch& b, const AttnScratch& sc, int nq, float scale, cudaStream_t s);
 
 }  // namespace kus
 

@@ -22,12 +22,15 @@ from .step import StepInput
 
 MAX_ENGINE_TOKENS = 16384
 ATTN_SPLIT_TOKENS = 512
+DEC_SPLIT_SLOTS = 1024          # dec_splits * n_dec bound (engine scratch)
 Q_TILE_ROWS = 64
 
 
 def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf: np.ndarray):
     """Fill ``buf`` (int32) with the engine's step metadata; returns
-    ``(n_ints, T, B, n_items, max_ctx)``."""
+    ``(n_ints, T, B, n_items, max_ctx, n_dec)``.  Requests with one query
+    token go to the decode kernel (list at the end); the others become
+    64-row query tiles (``items``) of the prefill kernel."""
     B = step.num_requests
     ql = np.fromiter((len(t) for t in step.input_tokens), dtype=np.int64, count=B)
     T = int(ql.sum())
@@ -35,7 +38,8 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     q_start = np.zeros(B + 1, dtype=np.int64)
     np.cumsum(ql, out=q_start[1:])
     rows = ql * group
-    tiles = (rows + Q_TILE_ROWS - 1) // Q_TILE_ROWS
+    is_dec = ql == 1
+    tiles = np.where(is_dec, 0, (rows + Q_TILE_ROWS - 1) // Q_TILE_ROWS)
     n_items = int(tiles.sum())
     item_req = np.repeat(np.arange(B), tiles)
     item_first = np.arange(n_items) - np.repeat(np.cumsum(tiles) - tiles, tiles)
@@ -70,7 +74,9 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     put(temps.view(np.int32))
     seeds = np.asarray(step.seeds if step.seeds is not None else [0] * B, dtype=np.int64) & 0xFFFFFFFF
     put(seeds.astype(np.uint32).view(np.int32))
-    return o, T, B, n_items, int(ctx.max()) if B else 0
+    dec = np.nonzero(is_dec)[0].astype(np.int32)
+    put(dec)
+    return o, T, B, n_items, int(ctx.max()) if B else 0, int(dec.size)
 
 
 class NativeRunner:
@@ -117,7 +123,7 @@ class NativeRunner:
             torch.cuda.synchronize()
         self.max_pages = math.ceil(sh.max_pos / layout.block_size)
         n = (2 * (sh.max_tokens * self.group // Q_TILE_ROWS + sh.max_batch + 1) + 4 * sh.max_tokens
-             + 5 * sh.max_batch + 1 + sh.max_batch * self.max_pages + 64)
+             + 6 * sh.max_batch + 1 + sh.max_batch * self.max_pages + 64)
         self.meta = torch.empty(n, dtype=torch.int32, pin_memory=True)
         self.meta_np = self.meta.numpy()
         self.num_sms = C.num_sms()
@@ -176,6 +182,14 @@ class NativeRunner:
         g = w.globals
         self.eng.load_globals(g["embed"], g["final_norm"], g["lm_head"])
 
+    def _dec_splits(self, n_dec: int, max_ctx: int) -> int:
+        """Key splits per decode request: enough CTAs to fill the GPU a few
+        times over, at least 256 keys per split, within the scratch."""
+        if n_dec == 0:
+            return 1
+        want = math.ceil(4 * self.num_sms / (n_dec * self.shape.nkv))
+        return int(max(1, min(32, want, max_ctx // 256, DEC_SPLIT_SLOTS // n_dec)))
+
     def _splits(self, T: int, n_items: int, max_ctx: int) -> int:
         if T > ATTN_SPLIT_TOKENS:
             return 1
@@ -186,8 +200,9 @@ class NativeRunner:
     def step(self, step: StepInput, recv_from: Optional[Tuple[str, int]] = None,
              send_to: Optional[Tuple[str, int]] = None, last_stage: bool = True) -> Optional[List[int]]:
         width = max([len(p) for p in step.page_tables] + [1])
-        n, T, B, n_items, max_ctx = pack_meta(step, self.layout.block_size, self.group, width, self.meta_np)
-        splits = self._splits(T, n_items, max_ctx)
+        n, T, B, n_items, max_ctx, n_dec = pack_meta(step, self.layout.block_size, self.group, width, self.meta_np)
+        splits = self._splits(T, n_items, max_ctx) if n_items else 1
+        dec_splits = self._dec_splits(n_dec, max_ctx)
         first = recv_from is None
         if not first:
             buf = self.comm.recv((T, self.shape.hidden), torch.bfloat16, self.device, *recv_from)
@@ -196,8 +211,8 @@ class NativeRunner:
         if last_stage and step.top_k is not None and (any(k > 0 for k in step.top_k) or
                                                       any(p < 1.0 for p in (step.top_p or []))):
             sample_mode = 1
-        out = self.eng.forward(self.meta, T, B, width, n_items, splits, step.layer_start, step.layer_end,
-                               step.fusion_size, first, last_stage, sample_mode, step.step_id)
+        out = self.eng.forward(self.meta, T, B, width, n_items, splits, n_dec, dec_splits, step.layer_start,
+                               step.layer_end, step.fusion_size, first, last_stage, sample_mode, step.step_id)
         self.num_steps += 1
         self.h2d_bytes += 4 * n
         if last_stage and sample_mode == 0:

@@ -150,11 +150,11 @@ def test_paged_attention(C, nq, nkv, splits):
     from kunserve_b200.engine.native_runner import pack_meta
     from kunserve_b200.engine.step import StepInput
     torch.manual_seed(4)
-    hd, bs, L, P, N = 128, 16, 2, 64, 1
+    hd, bs, L, P, N = 128, 16, 2, 128, 1
     lay, pool = _pool(P, L, bs, nkv, hd)
     pool.copy_(torch.randn_like(pool.float()).bfloat16())
     # mixed batch: a prefill chunk with a prefix, a fresh prefill, two decodes
-    starts = [40, 0, 100, 5] if splits == 1 else [0, 0, 300, 77]
+    starts = [40, 0, 100, 5] if splits == 1 else [0, 700, 300, 77]
     qlens = [30, 17, 1, 1] if splits == 1 else [1, 1, 1, 1]
     rng = np.random.default_rng(0)
     perm = rng.permutation(P).tolist()
@@ -169,8 +169,9 @@ def test_paged_attention(C, nq, nkv, splits):
     buf = np.zeros(4096, dtype=np.int32)
     G = nq // nkv
     width = max(len(t) for t in tables)
-    _, T2, B, n_items, _ = pack_meta(step, bs, G, width, buf)
+    n_int, T2, B, n_items, _, n_dec = pack_meta(step, bs, G, width, buf)
     items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
+    dec = torch.from_numpy(buf[n_int - n_dec:n_int].copy()).cuda()
     o = 2 * n_items + 4 * T
     q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
     ctx = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
@@ -181,8 +182,10 @@ def test_paged_attention(C, nq, nkv, splits):
     o_part = torch.empty(splits * T * nq * hd, device="cuda")
     ml = torch.empty(splits * T * nq * 2, device="cuda")
     layer = 1
-    C.attention(q, nq * hd, out, pool, P, N, L, L, bs, nkv, layer, q_start, ctx, tab.cuda(), items, splits,
-                o_part, ml, nq, 1.0 / math.sqrt(hd))
+    dec_o = torch.empty(splits * 4 * nq * hd, device="cuda")
+    dec_ml = torch.empty(splits * 4 * nq * 2, device="cuda")
+    C.attention(q, nq * hd, out, pool, P, N, L, L, bs, nkv, layer, q_start, ctx, tab.cuda(), items, 1,
+                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, splits, dec_o, dec_ml)
     torch.cuda.synchronize()
     ref = _ref_attention(q, pool, lay, N, layer, tables, starts, qlens, nq, nkv, hd)
     assert _rel(out.view(T, nq, hd), ref) < 2e-2
