@@ -85,7 +85,7 @@ def bench_tp(args, C, dev, rank, world):
             max_m = max(args.tokens)
             bases, keep = share(C, dev, 4096 + 2 * world * max_m * H * 2, rank, world)
             W = (torch.randn(H, K, device=dev) * 0.02).bfloat16()
-            ws = torch.empty(148 * 16 * 128 * 256, device=dev)
+            ws = torch.zeros(2 * 148 * 128 * 256, device=dev)   # stream-K tiles start (and stay) zero
             counters = torch.zeros(1 << 16, device=dev, dtype=torch.int32)
             epoch = [0]
             for M in args.tokens:

@@ -28,13 +28,14 @@ Scratch& scratch(int device) {
   Scratch& s = all.at(device);
   if (!s.ws.defined()) {
     auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA, device);
-    s.ws = torch::empty({(int64_t)148 * 16 * 128 * 256}, f32);
+    s.ws = torch::zeros({(int64_t)2 * 148 * 128 * 256}, f32);   // stream-K tiles, zero between GEMMs
     s.counters = torch::zeros({1 << 16}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, device));
   }
   return s;
 }
 
-// out = A @ B^T with the chosen epilogue; returns the split-K factor used.
+// out = A @ B^T with the chosen epilogue; returns how many tiles were split
+// along K (stream-K) across the grid (max_split <= 1 disables the split).
 int64_t gemm_op(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi, c10::optional<torch::Tensor> residual,
                 int64_t bn, int64_t max_split) {
   CHECK_CUDA_BF16(A);
@@ -43,10 +44,10 @@ int64_t gemm_op(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi
   TORCH_CHECK(A.size(1) % 8 == 0, "K must be a multiple of 8");
   c10::cuda::CUDAGuard g(A.device());
   const int M = A.size(0), K = A.size(1), N = B.size(0);
-  GemmPlan p = plan_gemm(M, N, K, (int)epi, (int)bn, (int)max_split);
+  GemmPlan p = plan_gemm(M, N, K, (int)epi, (int)bn, max_split > 1);
   Scratch& sc = scratch(A.get_device());
-  TORCH_CHECK(workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn) <= (size_t)sc.ws.numel(),
-              "split-K workspace too small");
+  TORCH_CHECK(plan_workspace_floats(p) <= (size_t)sc.ws.numel() && plan_counters(p) < sc.counters.numel(),
+              "stream-K workspace too small");
   const __nv_bfloat16* res = nullptr;
   if (epi == EPI_ADD) {
     TORCH_CHECK(residual.has_value(), "EPI_ADD needs a residual");
@@ -58,7 +59,7 @@ int64_t gemm_op(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi
                             (int)out.size(1), sc.ws.data_ptr<float>(), sc.counters.data_ptr<int>()),
               "tensor map encoding failed");
   run_gemm(p, at::cuda::getCurrentCUDAStream());
-  return p.args.split_k;
+  return p.args.sk_tiles;
 }
 
 void rmsnorm_op(torch::Tensor x, c10::optional<torch::Tensor> add, torch::Tensor w, torch::Tensor y,
@@ -154,8 +155,9 @@ void tp_gemm_allreduce_op(torch::Tensor A, torch::Tensor B, torch::Tensor h, c10
   c10::cuda::CUDAGuard g(A.device());
   const int M = A.size(0), K = A.size(1), N = B.size(0), R = (int)bases.size();
   TORCH_CHECK(R <= kMaxTpPeers && M <= max_tokens, "tp_gemm_allreduce sizes");
-  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, 256, 16);
-  TORCH_CHECK(workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn) <= (size_t)ws.numel(), "ws");
+  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, 256, true);
+  TORCH_CHECK(plan_workspace_floats(p) <= (size_t)ws.numel() && plan_counters(p) < counters.numel() - 1,
+              "ws (zero-filled fp32) too small");
   const int64_t slot = max_tokens * N * 2, flags = 4096;
   const int64_t data = flags + (epoch & 1) * R * slot + rank * slot;
   for (int q = 0; q < R; ++q) {

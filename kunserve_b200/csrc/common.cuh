@@ -1,10 +1,12 @@
 // Shared device helpers for the sm_100a kernels: bf16 vectors, bounded
 // mbarrier waits, TMA/tcgen05 inline PTX wrappers and the device error flag.
 //
-// Every spin-wait in this library is bounded.  A wait that runs out of
-// iterations records an error code in `g_kus_error` (read by the host after a
-// synchronize) and returns false; the kernel then drains what it issued and
-// returns, so a bug shows up as an error status instead of a hung GPU.
+// Every spin-wait in this library is bounded in wall-clock time (the
+// %globaltimer nanosecond clock, kWaitNs) and, as a backstop, in polls.  A
+// wait that runs out records an error code in `g_kus_error` (read by the host
+// after a synchronize) and returns false; the kernel then drains what it
+// issued and returns, so a bug shows up as an error status instead of a hung
+// GPU.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -38,8 +40,49 @@ KUS_DEVICE void set_error(int code, int info = 0) {
 
 KUS_DEVICE bool error_set() { return *(volatile int*)&g_kus_error != 0; }
 
-// ~2^27 polls is several seconds: far beyond any legitimate wait.
-constexpr uint32_t kSpinLimit = 1u << 27;
+// A legitimate wait in this library lasts microseconds (a pipeline stage) to
+// milliseconds (a peer rank's kernel); two seconds means a lost arrival.
+constexpr unsigned long long kWaitNs = 2000000000ull;
+// Poll backstop in case the clock does not advance.
+constexpr uint32_t kSpinLimit = 1u << 30;
+
+KUS_DEVICE unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ------------------------------------------------ programmatic dependent launch
+// Kernels of the forward pass are launched with programmatic stream
+// serialization (launch_k below): the next kernel's CTAs may start while
+// this one drains.  Every kernel calls pdl_wait() before it touches memory
+// that an earlier kernel writes or reads (it returns once every earlier
+// grid has completed and its writes are visible), then pdl_trigger() to
+// let the following kernel launch.  Without the launch attribute both are
+// no-ops.
+KUS_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+KUS_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host side: whether launches from this thread carry the attribute.
+inline bool& pdl_flag() {
+  static thread_local bool on = false;
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_flag() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 KUS_DEVICE uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -76,13 +119,19 @@ KUS_DEVICE bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: true when the phase with `parity` completed.
+// Bounded wait: true when the phase with `parity` completed.  On a timeout
+// the error info holds (blockIdx.x << 8) | (warp << 1) | parity.
 KUS_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int err_code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && error_set()) return false;
+    if ((i & 255u) == 0) {
+      if (error_set()) return false;
+      if (global_ns() - t0 > kWaitNs) break;
+    }
   }
-  set_error(err_code, (int)parity);
+  set_error(err_code, (int)((blockIdx.x << 8) | ((threadIdx.x / 32) << 1) | parity));
   return false;
 }
 

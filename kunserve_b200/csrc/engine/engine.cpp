@@ -1,5 +1,7 @@
 #include "engine.h"
 
+#include <cstdlib>
+
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -51,6 +53,10 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   KUS_CHECK(s.nq % s.nkv == 0, "query heads must be a multiple of KV heads");
   f_pad_ = (s.ffn + 127) / 128 * 128;
   qkv_n_ = (s.nq + 2 * s.nkv) * s.hd;
+  const char* dbg = std::getenv("KUNSERVE_SYNC_DEBUG");
+  sync_debug_ = dbg && dbg[0] == '1';
+  const char* pdl = std::getenv("KUNSERVE_PDL");
+  pdl_ = !(pdl && pdl[0] == '0');
   c10::cuda::CUDAGuard g(device_);
   auto bf = torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, device_);
   auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA, device_);
@@ -64,9 +70,10 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   tmp_ = torch::empty({T, s.hidden}, bf);
   ylast_ = torch::zeros({std::max<int64_t>(B, 128), s.hidden}, bf);
   logits_ = torch::empty({B, s.vocab}, f32);
-  // split-K workspace: enough for the largest decode GEMM split
-  const int64_t ws_floats = (int64_t)148 * 16 * 128 * 256;
-  gemm_ws_ = torch::empty({ws_floats}, f32);
+  // stream-K accumulation tiles (fewer than two waves of 128 x 256 fp32
+  // tiles); kept all zero between GEMMs by the kernels themselves
+  const int64_t ws_floats = (int64_t)2 * 148 * 128 * 256;
+  gemm_ws_ = torch::zeros({ws_floats}, f32);
   counters_ = torch::zeros({1 << 16}, i32);
   attn_split_tokens_ = std::min<int64_t>(T, 512);
   attn_o_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * s.hd}, f32);
@@ -214,12 +221,9 @@ torch::Tensor Engine::logits() { return logits_; }
 
 void Engine::gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
                   const __nv_bfloat16* res, cudaStream_t st) {
-  GemmPlan p = plan_gemm(M, N, K, epi, 256, 16);
-  const size_t need = workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn);
-  while (p.args.split_k > 1 && (need > (size_t)gemm_ws_.numel() || p.args.m_tiles * p.args.n_tiles > counters_.numel())) {
-    p = plan_gemm(M, N, K, epi, 256, p.args.split_k - 1);
-    if (workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn) <= (size_t)gemm_ws_.numel()) break;
-  }
+  GemmPlan p = plan_gemm(M, N, K, epi, 256, true);
+  if (plan_workspace_floats(p) > (size_t)gemm_ws_.numel() || plan_counters(p) >= counters_.numel())
+    p = plan_gemm(M, N, K, epi, 256, false);
   const int box = a_box_rows(p);
   p.tmA = mA[box == 16 ? 0 : box == 32 ? 1 : box == 64 ? 2 : 3];
   p.tmB = mB;
@@ -231,6 +235,16 @@ void Engine::gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, in
   p.args.tile_counters = counters_.data_ptr<int>();
   run_gemm(p, st);
   ++launches_;
+  if (sync_debug_) debug_check("gemm", M, N, K, st);
+}
+
+void Engine::debug_check(const char* what, int a, int b, int c, cudaStream_t st) {
+  check_cuda(cudaStreamSynchronize(st), what);
+  const long long e = error_flag(false);
+  if (e)
+    throw std::runtime_error(std::string("device error flag after ") + what + " (" + std::to_string(a) + ", " +
+                             std::to_string(b) + ", " + std::to_string(c) + "): code " +
+                             std::to_string(e & 0xff) + " info " + std::to_string(e >> 8));
 }
 
 void Engine::all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t st) {
@@ -304,9 +318,18 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   const float scale = 1.0f / std::sqrt((float)s_.hd);
   const auto& dropped = arena_->dropped();
 
+  // The first kernel of a step is an ordinary launch (it follows host
+  // copies); the rest may start while their predecessor drains.
+  struct PdlOff {
+    PdlOff() { set_pdl(false); }
+    ~PdlOff() { set_pdl(false); }
+  } pdl_off;
+  bool armed = false;
   if (first_stage) {
     embed(tokens, reinterpret_cast<const __nv_bfloat16*>(embed_.data_ptr()), h, (int)T, H, s_.vocab, st);
     ++launches_;
+    set_pdl(pdl_);
+    armed = true;
   }
   bool pending = false;   // tmp holds an all-reduced partial still to be added to h
   bool y_ready = false;   // the fused all-reduce already produced this layer's normed input
@@ -317,11 +340,16 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     const LayerW& W = layers_[l];
     const int ll = (int)(l - layer_start);
     if (!y_ready) rmsnorm(h, pending ? tmp : nullptr, W.in_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+    if (!armed) {
+      set_pdl(pdl_);
+      armed = true;
+    }
     y_ready = false;
     gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
     rope_append(qkv, positions, kv_page, kv_slot, cos_sin_.data_ptr<float>(), geo, ll, (int)T, s_.nq, s_.nkv,
                 s_.max_pos, st);
     paged_attention(qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
+    if (sync_debug_) debug_check("attention", (int)T, (int)B, (int)n_dec, st);
     launches_ += 3 + (splits > 1 ? 1 : 0);
     if (fused) {
       tp_push_gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, st);
@@ -433,7 +461,9 @@ void Engine::set_tp_peers(const std::vector<int64_t>& bases) {
 }
 
 void Engine::tp_push_gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, cudaStream_t st) {
-  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, 256, 16);
+  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, 256, true);
+  if (plan_workspace_floats(p) > (size_t)gemm_ws_.numel() || plan_counters(p) >= counters_.numel())
+    p = plan_gemm(M, N, K, EPI_PUSH, 256, false);
   const int box = a_box_rows(p);
   p.tmA = mA[box == 16 ? 0 : box == 32 ? 1 : box == 64 ? 2 : 3];
   p.tmB = mB;

@@ -129,6 +129,12 @@ class Engine {
   void tp_push_gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, cudaStream_t s);
   void tp_reduce(__nv_bfloat16* h, const __nv_bfloat16* w, __nv_bfloat16* y, int T, cudaStream_t s);
   int64_t launches_ = 0;
+  // KUNSERVE_SYNC_DEBUG=1: synchronize after every launch and name the
+  // first one that left the device error flag set
+  bool sync_debug_ = false;
+  // KUNSERVE_PDL=0 turns off programmatic dependent launch in forward()
+  bool pdl_ = true;
+  void debug_check(const char* what, int a, int b, int c, cudaStream_t st);
 };
 
 std::vector<int64_t> nccl_unique_id();

@@ -11,6 +11,8 @@
 #include "init.cu"
 
 namespace kus {
+void set_pdl(bool on) { pdl_flag() = on; }
+
 long long error_flag(bool reset) {
   int code = 0, info = 0;
   cudaMemcpyFromSymbol(&code, g_kus_error, sizeof(int));

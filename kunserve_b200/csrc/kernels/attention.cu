@@ -79,6 +79,8 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __nv_bfloat16* __r
                                                         __nv_bfloat16* __restrict__ out, KVGeom g, int layer,
                                                         AttnBatch b, AttnScratch sc, int T, int nq,
                                                         float scale_log2) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t qs_s = smem_u32(smem);
   const uint32_t ks_s[2] = {qs_s + kTileBytes, qs_s + 2 * kTileBytes};
@@ -269,6 +271,8 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(const __nv_bfloat16* __r
 
 __global__ void attn_combine_kernel(const AttnScratch sc, __nv_bfloat16* __restrict__ out, int T, int nq,
                                     int splits) {
+  pdl_wait();
+  pdl_trigger();
   const int tok = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
   float M = -1e30f;
   for (int s = 0; s < splits; ++s) M = fmaxf(M, sc.ml_part[(((size_t)s * T + tok) * nq + head) * 2]);
@@ -298,8 +302,9 @@ void paged_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, c
   }
   dim3 grid(b.n_items, g.kvh, b.splits);
   const float scale_log2 = scale * 1.4426950408889634f;
-  attn::attn_kernel<<<grid, attn::kThreads, smem, s>>>(q, q_stride, out, g, layer, b, sc, T, nq, scale_log2);
-  if (b.splits > 1) attn::attn_combine_kernel<<<dim3(T, nq), attn::HD, 0, s>>>(sc, out, T, nq, b.splits);
+  launch_k(attn::attn_kernel, grid, dim3(attn::kThreads), smem, s, q, q_stride, out, g, layer, b, sc, T, nq,
+           scale_log2);
+  if (b.splits > 1) launch_k(attn::attn_combine_kernel, dim3(T, nq), dim3(attn::HD), 0, s, sc, out, T, nq, b.splits);
 }
 
 }  // namespace kus

@@ -25,6 +25,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_attn_kernel(const __nv_bfl
                                                                   __nv_bfloat16* __restrict__ out, KVGeom g,
                                                                   int layer, AttnBatch b, AttnScratch sc, int nq,
                                                                   float scale_log2) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float q_s[G][HD];
   __shared__ float m_s[kWarps][G], l_s[kWarps][G];
   __shared__ float acc_s[kWarps][G][HD];
@@ -162,6 +164,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_attn_kernel(const __nv_bfl
 }
 
 __global__ void decode_combine_kernel(AttnBatch b, AttnScratch sc, __nv_bfloat16* __restrict__ out, int nq) {
+  pdl_wait();
+  pdl_trigger();
   const int di = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
   const int tok = b.q_start[b.dec_reqs[di]];
   float M = -1e30f;
@@ -185,12 +189,12 @@ void paged_decode_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16*
   dim3 grid(b.n_dec, g.kvh, b.dec_splits);
   const float sl2 = scale * 1.4426950408889634f;
   switch (G) {
-    case 1: dec::decode_attn_kernel<1><<<grid, dec::kWarps * 32, 0, s>>>(q, q_stride, out, g, layer, b, sc, nq, sl2); break;
-    case 2: dec::decode_attn_kernel<2><<<grid, dec::kWarps * 32, 0, s>>>(q, q_stride, out, g, layer, b, sc, nq, sl2); break;
-    case 4: dec::decode_attn_kernel<4><<<grid, dec::kWarps * 32, 0, s>>>(q, q_stride, out, g, layer, b, sc, nq, sl2); break;
-    default: dec::decode_attn_kernel<8><<<grid, dec::kWarps * 32, 0, s>>>(q, q_stride, out, g, layer, b, sc, nq, sl2); break;
+    case 1: launch_k(dec::decode_attn_kernel<1>, grid, dim3(dec::kWarps * 32), 0, s, q, q_stride, out, g, layer, b, sc, nq, sl2); break;
+    case 2: launch_k(dec::decode_attn_kernel<2>, grid, dim3(dec::kWarps * 32), 0, s, q, q_stride, out, g, layer, b, sc, nq, sl2); break;
+    case 4: launch_k(dec::decode_attn_kernel<4>, grid, dim3(dec::kWarps * 32), 0, s, q, q_stride, out, g, layer, b, sc, nq, sl2); break;
+    default: launch_k(dec::decode_attn_kernel<8>, grid, dim3(dec::kWarps * 32), 0, s, q, q_stride, out, g, layer, b, sc, nq, sl2); break;
   }
-  if (b.dec_splits > 1) dec::decode_combine_kernel<<<dim3(b.n_dec, nq), dec::HD, 0, s>>>(b, sc, out, nq);
+  if (b.dec_splits > 1) launch_k(dec::decode_combine_kernel, dim3(b.n_dec, nq), dim3(dec::HD), 0, s, b, sc, out, nq);
 }
 
 }  // namespace kus

@@ -12,6 +12,8 @@ namespace kus {
 // ------------------------------------------------------------- embedding
 __global__ void embed_kernel(const int* __restrict__ tokens, const __nv_bfloat16* __restrict__ table,
                              __nv_bfloat16* __restrict__ out, int T, int H, int V) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   int tok = tokens[t];
   if (tok < 0 || tok >= V) {
@@ -26,7 +28,7 @@ __global__ void embed_kernel(const int* __restrict__ tokens, const __nv_bfloat16
 void embed(const int* tokens, const __nv_bfloat16* table, __nv_bfloat16* out, int T, int H, int V,
            cudaStream_t s) {
   if (T <= 0) return;
-  embed_kernel<<<T, 128, 0, s>>>(tokens, table, out, T, H, V);
+  launch_k(embed_kernel, dim3(T), dim3(128), 0, s, tokens, table, out, T, H, V);
 }
 
 // --------------------------------------------------------------- RMSNorm
@@ -37,6 +39,8 @@ template <int VPT>
 __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ add,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                const int* __restrict__ rows, int H, float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const int src = rows ? rows[r] : r;
   uint4* xr = reinterpret_cast<uint4*>(x + (size_t)src * H);
@@ -96,13 +100,13 @@ void rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* add, const __nv_bfloat16* w,
   int threads = nv >= 256 ? 256 : ((nv + 31) / 32) * 32;
   const int vpt = (nv + threads - 1) / threads;
   if (vpt <= 1)
-    rmsnorm_kernel<1><<<R, threads, 0, s>>>(x, add, w, y, rows, H, eps);
+    launch_k(rmsnorm_kernel<1>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps);
   else if (vpt <= 2)
-    rmsnorm_kernel<2><<<R, threads, 0, s>>>(x, add, w, y, rows, H, eps);
+    launch_k(rmsnorm_kernel<2>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps);
   else if (vpt <= 4)
-    rmsnorm_kernel<4><<<R, threads, 0, s>>>(x, add, w, y, rows, H, eps);
+    launch_k(rmsnorm_kernel<4>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps);
   else
-    rmsnorm_kernel<8><<<R, 1024 / 4, 0, s>>>(x, add, w, y, rows, H, eps);
+    launch_k(rmsnorm_kernel<8>, dim3(R), dim3(1024 / 4), 0, s, x, add, w, y, rows, H, eps);
 }
 
 // ----------------------------------------------------- RoPE + KV append
@@ -112,43 +116,47 @@ void rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* add, const __nv_bfloat16* w,
 __global__ void rope_append_kernel(__nv_bfloat16* __restrict__ qkv, const int* __restrict__ positions,
                                    const int* __restrict__ pages, const int* __restrict__ slots,
                                    const float* __restrict__ cos_sin, KVGeom g, int layer, int nq, int nkv,
-                                   int max_pos) {
-  const int t = blockIdx.x;
-  const int hd = g.hd;
-  const int half = hd / 2;
+                                   int max_pos, int T) {
+  pdl_wait();
+  pdl_trigger();
+  // one warp per (token, head); head_dim 128: lane owns rotation pairs
+  // (2 lane, 2 lane + 1) of the first half and their partners 64 further
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  const int heads = nq + 2 * nkv;
+  const int t = warp / heads, h = warp % heads;
+  if (t >= T) return;
+  constexpr int hd = 128, half = 64;
+  __nv_bfloat16* src = qkv + ((size_t)t * heads + h) * hd;
+  const int page = pages[t], slot = slots[t];
+  if (h >= nq + nkv) {
+    __nv_bfloat16* dst = kv_ptr(g, page, layer, true) + ((size_t)slot * g.kvh + (h - nq - nkv)) * hd;
+    if (lane < hd / 8) reinterpret_cast<uint4*>(dst)[lane] = reinterpret_cast<const uint4*>(src)[lane];
+    return;
+  }
   int pos = positions[t];
   if (pos < 0 || pos >= max_pos) {
     set_error(kErrBounds, pos);
     pos = 0;
   }
-  const float* cs = cos_sin + (size_t)pos * hd;
-  const int warps = blockDim.x / 32, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  __nv_bfloat16* row = qkv + (size_t)t * (nq + 2 * nkv) * hd;
-  const int page = pages[t], slot = slots[t];
-  for (int h = warp; h < nq + 2 * nkv; h += warps) {
-    __nv_bfloat16* src = row + h * hd;
-    if (h < nq + nkv) {
-      __nv_bfloat16* dst = h < nq ? src : kv_ptr(g, page, layer, false) + ((size_t)slot * g.kvh + (h - nq)) * hd;
-      for (int i = lane; i < half; i += 32) {
-        const float c = cs[i], s = cs[half + i];
-        const float x1 = bf2f(src[i]), x2 = bf2f(src[i + half]);
-        dst[i] = f2bf(x1 * c - x2 * s);
-        dst[i + half] = f2bf(x2 * c + x1 * s);
-      }
-    } else {
-      __nv_bfloat16* dst = kv_ptr(g, page, layer, true) + ((size_t)slot * g.kvh + (h - nq - nkv)) * hd;
-      const uint4* s4 = reinterpret_cast<const uint4*>(src);
-      uint4* d4 = reinterpret_cast<uint4*>(dst);
-      for (int i = lane; i < hd / 8; i += 32) d4[i] = s4[i];
-    }
-  }
+  const float2 c = reinterpret_cast<const float2*>(cos_sin + (size_t)pos * hd)[lane];
+  const float2 s = reinterpret_cast<const float2*>(cos_sin + (size_t)pos * hd + half)[lane];
+  const float2 x1 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[lane]);
+  const float2 x2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src + half)[lane]);
+  __nv_bfloat16* dst = h < nq ? src : kv_ptr(g, page, layer, false) + ((size_t)slot * g.kvh + (h - nq)) * hd;
+  reinterpret_cast<__nv_bfloat162*>(dst)[lane] =
+      __floats2bfloat162_rn(x1.x * c.x - x2.x * s.x, x1.y * c.y - x2.y * s.y);
+  reinterpret_cast<__nv_bfloat162*>(dst + half)[lane] =
+      __floats2bfloat162_rn(x2.x * c.x + x1.x * s.x, x2.y * c.y + x1.y * s.y);
 }
 
 void rope_append(__nv_bfloat16* qkv, const int* positions, const int* pages, const int* slots,
                  const float* cos_sin, const KVGeom& g, int layer, int T, int nq, int nkv, int max_pos,
                  cudaStream_t s) {
   if (T <= 0) return;
-  rope_append_kernel<<<T, 256, 0, s>>>(qkv, positions, pages, slots, cos_sin, g, layer, nq, nkv, max_pos);
+  const long long warps = (long long)T * (nq + 2 * nkv);
+  const int threads = 256;
+  launch_k(rope_append_kernel, dim3((unsigned)((warps * 32 + threads - 1) / threads)), dim3(threads), 0, s, qkv,
+           positions, pages, slots, cos_sin, g, layer, nq, nkv, max_pos, T);
 }
 
 // -------------------------------------------------------------- sampling
@@ -166,6 +174,8 @@ KUS_DEVICE uint64_t splitmix64(uint64_t z) {
 __global__ void sample_kernel(const float* __restrict__ logits, int V, int ld, const float* __restrict__ temp,
                               const unsigned* __restrict__ seeds, unsigned long long step,
                               int* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const float* row = logits + (size_t)r * ld;
   const float t = temp ? temp[r] : 0.f;
@@ -216,7 +226,7 @@ __global__ void sample_kernel(const float* __restrict__ logits, int V, int ld, c
 void sample(const float* logits, int B, int V, int ld, const float* temp, const unsigned* seeds,
             unsigned long long step, int* out, cudaStream_t s) {
   if (B <= 0) return;
-  sample_kernel<<<B, 1024, 0, s>>>(logits, V, ld, temp, seeds, step, out);
+  launch_k(sample_kernel, dim3(B), dim3(1024), 0, s, logits, V, ld, temp, seeds, step, out);
 }
 
 // ------------------------------------------------------------ chunk copy
@@ -257,17 +267,21 @@ __global__ void tp_reduce_rmsnorm_kernel(const __nv_bfloat16* __restrict__ rb, i
                                          __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
                                          __nv_bfloat16* __restrict__ y, int H, float eps,
                                          const unsigned* __restrict__ flags, unsigned epoch) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   __shared__ int ok_s;
   const int row = blockIdx.x;
   if (threadIdx.x == 0) {
     int ok = 1;
+    const unsigned long long t0 = global_ns();
     for (int p = 0; p < R && ok; ++p) {
       for (uint32_t i = 0;; ++i) {
         unsigned v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + p) : "memory");
         if ((int)(v - epoch) >= 0) break;
-        if (i >= (kSpinLimit >> 6) || ((i & 255u) == 255u && error_set())) {
+        if (i >= (kSpinLimit >> 6) ||
+            ((i & 255u) == 255u && (error_set() || global_ns() - t0 > kWaitNs))) {
           set_error(kErrPeerFlag, p);
           ok = 0;
           break;
@@ -321,7 +335,7 @@ void tp_reduce_rmsnorm(const __nv_bfloat16* rb, int R, long long slot_elems, __n
                        const __nv_bfloat16* w, __nv_bfloat16* y, int T, int H, float eps, const unsigned* flags,
                        unsigned epoch, cudaStream_t s) {
   if (T <= 0) return;
-  tp_reduce_rmsnorm_kernel<<<T, 256, 0, s>>>(rb, R, slot_elems, h, w, y, H, eps, flags, epoch);
+  launch_k(tp_reduce_rmsnorm_kernel, dim3(T), dim3(256), 0, s, rb, R, slot_elems, h, w, y, H, eps, flags, epoch);
 }
 
 // -------------------------------------------------- residual add (TP path)

@@ -13,14 +13,20 @@ constexpr int kMaxTpPeers = 8;
 
 struct GemmArgs {
   int M, N, K;
-  int m_tiles, n_tiles, split_k;
+  int m_tiles, n_tiles;
+  // Work split (stream-K hybrid): tiles [0, dp_tiles) are whole-tile units
+  // walked round-robin by the CTAs; the K loops of tiles [dp_tiles,
+  // dp_tiles + sk_tiles) are concatenated and cut into gridDim.x equal
+  // ranges, one per CTA.  A tile finished by several CTAs is reduced in
+  // fp32 through the workspace by whichever CTA completes its K range last.
+  int dp_tiles, sk_tiles, num_kb;
   int n_out;            // output columns (N, or N/2 for EPI_SILU)
   void* out;
   int ldc;
   const __nv_bfloat16* residual;
   int ld_res;
-  float* workspace;     // split-K partial tiles, fp32 [tiles][split][128][BN]
-  int* tile_counters;   // one int per tile, zero between GEMMs
+  float* workspace;     // fp32 accumulation tile per stream-K tile; all zero between GEMMs
+  int* tile_counters;   // k-blocks done per stream-K tile, zero between GEMMs
   // EPI_PUSH (fused tensor-parallel all-reduce): bf16 tiles go to every
   // rank's receive slot (peer_out[p], row stride ldc); the last CTA then
   // writes `epoch` to each rank's flag for this sender (flag_remote[p]).
@@ -50,9 +56,12 @@ int num_sms();
 bool make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                     uint32_t box_rows);
 int choose_bn(int M, int N, int epi);
-// Tile counts and split-K factor for an M x N x K problem (bn <= 0: choose).
-GemmPlan plan_gemm(int M, int N, int K, int epi, int bn = 0, int max_split = 16);
-size_t workspace_floats(int m_tiles, int n_tiles, int split_k, int bn);
+// Tiles and work split for an M x N x K problem (bn <= 0: choose).  With
+// stream_k false every tile is a whole-tile unit (no workspace traffic).
+GemmPlan plan_gemm(int M, int N, int K, int epi, int bn = 0, bool stream_k = true);
+// fp32 workspace floats and counters a plan needs (workspace all zero).
+size_t plan_workspace_floats(const GemmPlan& p);
+inline int plan_counters(const GemmPlan& p) { return p.args.sk_tiles; }
 // Bind operands.  a_rows / b_rows override the rows declared to TMA (0: M / N).
 bool finalize_plan(GemmPlan& p, const void* A, int lda, const void* B, int ldb, void* out, int ldc,
                    const __nv_bfloat16* residual, int ld_res, float* workspace, int* counters,

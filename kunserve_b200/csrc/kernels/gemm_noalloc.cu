@@ -9,7 +9,7 @@ namespace noalloc {
 constexpr size_t kCounterInts = 1024;
 constexpr size_t kFloats = (KUS_NOALLOC_SCRATCH_BYTES - kCounterInts * sizeof(int)) / sizeof(float);
 
-// The scratch: split-K partial tiles, then the per-tile arrival counters.
+// The scratch: stream-K accumulation tiles, then the per-tile counters.
 // In host code this name is only a stand-in for the symbol; the device
 // address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_scratch[KUS_NOALLOC_SCRATCH_BYTES];
@@ -44,17 +44,17 @@ extern "C" int kus_gemm_bf16_noalloc(const void* A, int lda, const void* B, int 
   void* scratch = nullptr;
   int rc = noalloc::scratch_for_current_device(&scratch);
   if (rc) return rc;
-  GemmPlan p = plan_gemm(M, N, K, EPI_BF16, 0, 16);
-  const int tiles = p.args.m_tiles * p.args.n_tiles;
-  if (p.args.split_k > 1 &&
-      (workspace_floats(p.args.m_tiles, p.args.n_tiles, p.args.split_k, p.bn) > noalloc::kFloats ||
-       (size_t)tiles > noalloc::kCounterInts))
-    return KUS_NOALLOC_ERR_SCRATCH;
+  GemmPlan p = plan_gemm(M, N, K, EPI_BF16, 0, true);
+  // a plan whose stream-K tiles do not fit the scratch runs as whole tiles
+  if (plan_workspace_floats(p) > noalloc::kFloats || (size_t)plan_counters(p) > noalloc::kCounterInts)
+    p = plan_gemm(M, N, K, EPI_BF16, 0, false);
   float* ws = reinterpret_cast<float*>(scratch);
   int* counters = reinterpret_cast<int*>(ws + noalloc::kFloats);
-  if (p.args.split_k > 1) {
-    // counters must start at zero (a previous call that failed could leave some set)
-    cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)tiles * sizeof(int), stream);
+  if (p.args.sk_tiles > 0) {
+    // tiles and counters must start at zero (a previous call that failed
+    // could leave some set)
+    cudaError_t e = cudaMemsetAsync(counters, 0, (size_t)p.args.sk_tiles * sizeof(int), stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, plan_workspace_floats(p) * sizeof(float), stream);
     if (e != cudaSuccess) return (int)e;
   }
   if (!finalize_plan(p, A, lda, B, ldb, C, ldc, nullptr, ldc, ws, counters, (uint64_t)M, (uint64_t)N))

@@ -9,18 +9,20 @@
 // real-time loop with a fixed memory budget, or a host thread that cannot
 // take the caching allocator's lock.  Those callers cannot call cudaMalloc
 // (or anything that does, such as a PyTorch op), so this function never
-// does: its split-K scratch is a fixed array compiled into the library.
+// does: its stream-K scratch is a fixed array compiled into the library.
 //
 //   C[M,N] (bf16, row-major, ldc) = A[M,K] (bf16, lda) * B[N,K]^T (bf16, ldb)
 //
 // It runs the same tcgen05 kernel as the regular entry point
-// (kus::run_gemm, bf16 epilogue) with the same split-K plan, so results
-// match it.
+// (kus::run_gemm, bf16 epilogue) with the same stream-K plan when its
+// accumulation tiles fit the scratch, and as whole tiles (no split along K)
+// otherwise; either way the results match the regular entry point to fp32
+// summation order.
 //
 // Scratch: one static device array of KUS_NOALLOC_SCRATCH_BYTES per GPU
-// that loads this library, held until the process exits.  A problem whose
-// split-K plan needs more is rejected (KUS_NOALLOC_ERR_SCRATCH); every
-// problem planned on a GPU with at most 148 SMs fits.
+// that loads this library, held until the process exits.  Each call that
+// splits along K first clears the part it uses (two cudaMemsetAsync calls
+// on `stream`, which allocate nothing).
 //
 // Set-up: the first call on a device (with that device current) looks up
 // the array's device address with cudaGetSymbolAddress; make that first
@@ -41,7 +43,7 @@
 enum {
   KUS_NOALLOC_OK = 0,
   KUS_NOALLOC_ERR_ARGS = -1,      /* non-positive size, K or a leading dimension not a multiple of 8 */
-  KUS_NOALLOC_ERR_SCRATCH = -2,   /* the split-K plan needs more than KUS_NOALLOC_SCRATCH_BYTES */
+  KUS_NOALLOC_ERR_SCRATCH = -2,   /* reserved: no plan is rejected for scratch size any more */
   KUS_NOALLOC_ERR_ALIGN = -3,     /* a pointer is not 16-byte aligned */
   KUS_NOALLOC_ERR_TMAP = -4,      /* TMA descriptor encoding failed */
   KUS_NOALLOC_ERR_SETUP = -5,     /* cudaGetSymbolAddress failed on this device */

@@ -1,18 +1,19 @@
 // Decode-shaped GEMM (few tokens, many output features) on tcgen05 with the
 // operands swapped: D^T[N, M] = B[N, K] * A[M, K]^T.
 //
-// With M <= 64 tokens the regular 128-row token tile would be mostly
-// padding.  Here the weight tile (256 rows, the same TMA box the regular
+// With M <= 128 tokens the regular 128-row token tile would be mostly
+// padding (and its activation tile is re-read for every weight tile).  Here the weight tile (256 rows, the same TMA box the regular
 // kernel uses) is the MMA's A operand, split into two 128-row halves, and
-// the token tile (BNT = 16..64 rows) is the narrow N operand.  Stages are
+// the token tile (BNT = 16..128 rows) is the narrow N operand.  Stages are
 // dominated by weight bytes, so more of them fit in shared memory and more
 // HBM traffic is in flight per SM.  The epilogue writes the transpose back
 // to C[M, N]; with EPI_SILU the two halves of a tile are the gate and up
 // rows of the same 128 features (the interleave of the weight layout), so a
 // thread holds both and stores silu(gate) * up directly.
-// Split-K and its last-arriver reduction work as in gemm_tcgen05.cu.
+// The stream-K walk and its L2 reduction work as in gemm_tcgen05.cu.
 #include "../common.cuh"
 #include "gemm.h"
+#include "gemm_sched.cuh"
 
 namespace kus {
 namespace gemm_swap_impl {
@@ -34,26 +35,43 @@ struct SCfg {
 
 KUS_DEVICE float silu_s(float x) { return x / (1.0f + __expf(-x)); }
 
-// v[i] = D^T[f, tok0 + i]; store C[tok0 + i, f] for the 16 tokens.
+// v[i] = D^T[f, tok0 + i]; store C[tok0 + i, f] for the 16 tokens.  A warp
+// holds 32 consecutive features, so each token's stores (and residual
+// loads) are 64-byte coalesced; the loads are predicated rather than broken
+// out of, so all 16 are in flight at once.
 template <int EPI>
 KUS_DEVICE void store_col16(const GemmArgs& a, int f, int tok0, const float (&v)[16]) {
   if (f >= a.n_out) return;
+  if (EPI == EPI_F32) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int tok = tok0 + i;
-    if (tok >= a.M) break;
-    if (EPI == EPI_F32) {
-      reinterpret_cast<float*>(a.out)[(size_t)tok * a.ldc + f] = v[i];
-    } else if (EPI == EPI_PUSH) {
-      const __nv_bfloat16 b = f2bf(v[i]);
-      for (int p = 0; p < a.npeers; ++p)
-        reinterpret_cast<__nv_bfloat16*>(a.peer_out[p])[(size_t)tok * a.ldc + f] = b;
-    } else {
-      float x = v[i];
-      if (EPI == EPI_ADD) x += bf2f(a.residual[(size_t)tok * a.ld_res + f]);
-      reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)tok * a.ldc + f] = f2bf(x);
-    }
+    for (int i = 0; i < 16; ++i)
+      if (tok0 + i < a.M) reinterpret_cast<float*>(a.out)[(size_t)(tok0 + i) * a.ldc + f] = v[i];
+    return;
   }
+  float x[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) x[i] = v[i];
+  if (EPI == EPI_ADD) {
+    __nv_bfloat16 r[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      r[i] = (tok0 + i < a.M) ? a.residual[(size_t)(tok0 + i) * a.ld_res + f] : __float2bfloat16(0.f);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) x[i] += bf2f(r[i]);
+  }
+  if (EPI == EPI_PUSH) {
+    for (int p = 0; p < a.npeers; ++p) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (tok0 + i < a.M) dst[(size_t)(tok0 + i) * a.ldc + f] = f2bf(x[i]);
+    }
+    return;
+  }
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (tok0 + i < a.M) out[(size_t)(tok0 + i) * a.ldc + f] = f2bf(x[i]);
 }
 
 template <int BNT, int EPI>
@@ -73,11 +91,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* flag_smem = reinterpret_cast<int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int num_kb = (args.K + BK - 1) / BK;
-  const int S = args.split_k;
-  const int kbs = (num_kb + S - 1) / S;
-  const int tiles = args.n_tiles;          // one token tile
-  const int units = tiles * S;
+  const int num_kb = args.num_kb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -96,17 +110,36 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
+  // everything below except the producer's weight prefetch may depend on
+  // the previous kernel (activations, residual, workspace)
+  if (warp != 0) {
+    pdl_wait();
+    pdl_trigger();
+  }
+
   if (warp == 0) {
     if (elect_one_sync()) {
       prefetch_tmap(&tmX);
       prefetch_tmap(&tmW);
-      int stage = 0;
-      uint32_t phase = 0;
+      SegWalk walk(args);
+      int n = 0, kb0 = 0, kb1 = 0;
+      bool have = walk.next(n, kb0, kb1);
+      // weights are not written by earlier kernels: the first stages get
+      // their weight tiles while the previous kernel drains
+      const int pre = have ? min(C::kStages, kb1 - kb0) : 0;
+      for (int j = 0; j < pre; ++j) {
+        mbar_arrive_expect_tx(&full[j], C::kStageBytes);
+        tma_load_2d(smem_w + j * C::kWBytes, &tmW, &full[j], (kb0 + j) * BK, n * kWRows);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int j = 0; j < pre; ++j) tma_load_2d(smem_x + j * C::kXBytes, &tmX, &full[j], (kb0 + j) * BK, 0);
+      int stage = pre == C::kStages ? 0 : pre;
+      uint32_t phase = pre == C::kStages ? 1u : 0u;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int n = u / S, split = u % S;
-        const int kb0 = split * kbs, kb1 = min(kb0 + kbs, num_kb);
-        for (int kb = kb0; kb < kb1; ++kb) {
+      int kb_from = kb0 + pre;
+      while (ok && have) {
+        for (int kb = kb_from; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -119,6 +152,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1;
           }
         }
+        have = walk.next(n, kb0, kb1);
+        kb_from = kb0;
       }
       for (int i = 0; i < C::kStages && ok; ++i) {
         if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) break;
@@ -136,9 +171,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int split = u % S;
-        const int kb0 = split * kbs, kb1 = min(kb0 + kbs, num_kb);
+      SegWalk walk(args);
+      int n, kb0, kb1;
+      while (ok && walk.next(n, kb0, kb1)) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, kErrWaitTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * 2 * BNT;
@@ -177,15 +212,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = threadIdx.x - 64;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      const int n = u / S, split = u % S;
+    SegWalk walk(args);
+    int n, kb0, kb1;
+    while (walk.next(n, kb0, kb1)) {
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, kErrWaitTmemFull));
       tc_fence_after();
       const uint32_t t0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 2 * BNT);
-      if (S == 1) {
+      // tokens beyond M carry zeros: their columns are neither reduced nor stored
+      const int cols = args.M < BNT ? ((args.M + 15) & ~15) : BNT;
+      if (kb0 == 0 && kb1 == num_kb) {
         if (ok) {
 #pragma unroll 1
-          for (int c = 0; c < BNT; c += 16) {
+          for (int c = 0; c < cols; c += 16) {
             float v0[16], v1[16];
             tmem_ld16(t0 + c, v0);
             tmem_ld16(t0 + BNT + c, v1);
@@ -203,55 +241,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
       } else {
-        float* ws = args.workspace + ((size_t)n * S + split) * (kWRows * BNT);
+        const int sk = n - args.dp_tiles;
+        float* w0 = args.workspace + (size_t)sk * (kWRows * BNT) + (size_t)r * BNT;
+        float* w1 = w0 + (size_t)128 * BNT;
         if (ok) {
 #pragma unroll 1
-          for (int c = 0; c < BNT; c += 16) {
+          for (int c = 0; c < cols; c += 16) {
             float v0[16], v1[16];
             tmem_ld16(t0 + c, v0);
             tmem_ld16(t0 + BNT + c, v1);
-            float* d0 = ws + (size_t)r * BNT + c;
-            float* d1 = ws + (size_t)(128 + r) * BNT + c;
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-              __stcg(reinterpret_cast<float4*>(d0 + i), make_float4(v0[i], v0[i + 1], v0[i + 2], v0[i + 3]));
-              __stcg(reinterpret_cast<float4*>(d1 + i), make_float4(v1[i], v1[i + 1], v1[i + 2], v1[i + 3]));
-            }
+            red_add16(w0 + c, v0);
+            red_add16(w1 + c, v1);
           }
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
-        __threadfence();
-        named_barrier(1, 128);
-        if (et == 0) {
-          int last = 0;
-          if (!error_set()) {
-            const int prev = atomicAdd(&args.tile_counters[n], 1);
-            last = (prev == S - 1);
-            if (last) args.tile_counters[n] = 0;
-          }
-          *flag_smem = last;
-        }
-        named_barrier(1, 128);
-        const int last = *flag_smem;
-        named_barrier(1, 128);
-        if (last) {
-          __threadfence();
-          const float* base = args.workspace + (size_t)n * S * (kWRows * BNT);
+        if (sk_arrive(args, sk, kb1 - kb0, et, flag_smem)) {
 #pragma unroll 1
-          for (int c = 0; c < BNT; c += 16) {
-            float v0[16] = {}, v1[16] = {};
-            for (int s = 0; s < S; ++s) {
-              const float* p0 = base + (size_t)s * (kWRows * BNT) + (size_t)r * BNT + c;
-              const float* p1 = p0 + (size_t)128 * BNT;
-#pragma unroll
-              for (int i = 0; i < 16; i += 4) {
-                const float4 x = __ldcg(reinterpret_cast<const float4*>(p0 + i));
-                const float4 y = __ldcg(reinterpret_cast<const float4*>(p1 + i));
-                v0[i] += x.x; v0[i + 1] += x.y; v0[i + 2] += x.z; v0[i + 3] += x.w;
-                v1[i] += y.x; v1[i + 1] += y.y; v1[i + 2] += y.z; v1[i + 3] += y.w;
-              }
-            }
+          for (int c = 0; c < cols; c += 16) {
+            float v0[16], v1[16];
+            take16(w0 + c, v0);
+            take16(w1 + c, v1);
             if (EPI == EPI_SILU) {
               float o[16];
 #pragma unroll
@@ -284,7 +294,7 @@ void launch_swap(const GemmPlan& p, cudaStream_t s) {
     cudaFuncSetAttribute(gemm_swap_kernel<BNT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     attr = true;
   }
-  gemm_swap_kernel<BNT, EPI><<<p.grid, kThreads, C::kSmemBytes, s>>>(p.tmA, p.tmB, p.args);
+  launch_k(gemm_swap_kernel<BNT, EPI>, dim3(p.grid), dim3(kThreads), C::kSmemBytes, s, p.tmA, p.tmB, p.args);
 }
 
 template <int EPI>
@@ -292,7 +302,8 @@ void launch_swap_bnt(const GemmPlan& p, cudaStream_t s) {
   switch (p.bnt) {
     case 16: launch_swap<16, EPI>(p, s); break;
     case 32: launch_swap<32, EPI>(p, s); break;
-    default: launch_swap<64, EPI>(p, s); break;
+    case 64: launch_swap<64, EPI>(p, s); break;
+    default: launch_swap<128, EPI>(p, s); break;
   }
 }
 

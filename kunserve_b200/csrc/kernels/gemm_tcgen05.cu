@@ -14,12 +14,15 @@
 //
 // Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
 // owner, warps 2-5 epilogue.  The grid is persistent (<= one CTA per SM) and
-// walks (tile, k-split) units.  With split-K each unit writes an fp32
-// partial tile to a workspace and bumps a per-tile counter; the CTA that
-// arrives last sums the partials and runs the epilogue, so no CTA ever waits
-// for another.  All mbarrier waits are bounded (common.cuh).
+// walks the segments of gemm_sched.cuh: whole tiles, then an equal share of
+// the stream-K tiles' K loops.  A partial segment adds its fp32 tile into
+// the workspace with L2 reductions and counts its k-blocks; the CTA that
+// completes a tile's K loop reads the sum back (zeroing it) and runs the
+// epilogue, so no CTA ever waits for another.  All mbarrier waits are
+// bounded (common.cuh).
 #include "../common.cuh"
 #include "gemm.h"
+#include "gemm_sched.cuh"
 #include <cudaTypedefs.h>
 
 namespace kus {
@@ -150,11 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
 
-  const int num_kb = (args.K + BK - 1) / BK;
-  const int S = args.split_k;
-  const int kbs = (num_kb + S - 1) / S;
-  const int tiles = args.m_tiles * args.n_tiles;
-  const int units = tiles * S;
+  const int num_kb = args.num_kb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -173,19 +172,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
+  // everything below except the producer's weight prefetch may depend on
+  // the previous kernel (activations, residual, workspace)
+  if (warp != 0) {
+    pdl_wait();
+    pdl_trigger();
+  }
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
       prefetch_tmap(&tmA);
       prefetch_tmap(&tmB);
-      int stage = 0;
-      uint32_t phase = 0;
+      SegWalk walk(args);
+      int tile = 0, kb0 = 0, kb1 = 0;
+      bool have = walk.next(tile, kb0, kb1);
+      // weights are not written by earlier kernels: the first stages get
+      // their weight tiles while the previous kernel drains
+      const int pre = have ? min(C::kStages, kb1 - kb0) : 0;
+      for (int j = 0; j < pre; ++j) {
+        mbar_arrive_expect_tx(&full[j], C::kStageBytes);
+        tma_load_2d(smem_b + j * C::kBBytes, &tmB, &full[j], (kb0 + j) * BK, (tile / args.m_tiles) * BN);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int j = 0; j < pre; ++j)
+        tma_load_2d(smem_a + j * C::kABytes, &tmA, &full[j], (kb0 + j) * BK, (tile % args.m_tiles) * BM);
+      int stage = pre == C::kStages ? 0 : pre;
+      uint32_t phase = pre == C::kStages ? 1u : 0u;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int tile = u / S, split = u % S;
+      int kb_from = kb0 + pre;
+      while (ok && have) {
         const int m = tile % args.m_tiles, n = tile / args.m_tiles;
-        const int kb0 = split * kbs, kb1 = min(kb0 + kbs, num_kb);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb_from; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -198,6 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1;
           }
         }
+        have = walk.next(tile, kb0, kb1);
+        kb_from = kb0;
       }
       // drain: wait until the consumer released every stage we filled, so no
       // TMA write can land after the CTA exits
@@ -218,9 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int split = u % S;
-        const int kb0 = split * kbs, kb1 = min(kb0 + kbs, num_kb);
+      SegWalk walk(args);
+      int tile, kb0, kb1;
+      while (ok && walk.next(tile, kb0, kb1)) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, kErrWaitTmemEmpty)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
@@ -258,8 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     constexpr int kOutCols = (EPI == EPI_SILU) ? BN / 2 : BN;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      const int tile = u / S, split = u % S;
+    SegWalk walk(args);
+    int tile, kb0, kb1;
+    while (walk.next(tile, kb0, kb1)) {
       const int m = tile % args.m_tiles, n = tile / args.m_tiles;
       const int row = m * BM + r_in_tile;
       // A failed (timed-out) wait skips the work but keeps every thread on the
@@ -268,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
       const int col0 = n * kOutCols;
-      if (S == 1) {
+      if (kb0 == 0 && kb1 == num_kb) {
         if (ok && EPI == EPI_SILU) {
 #pragma unroll 1
           for (int c = 0; c < BN / 2; c += 16) {
@@ -290,54 +312,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
       } else {
-        // split-K: park the partial, the last split of the tile reduces
-        float* ws = args.workspace + ((size_t)tile * S + split) * (BM * BN);
+        // stream-K: add the partial into the tile's fp32 accumulator
+        const int sk = tile - args.dp_tiles;
+        float* ws = args.workspace + (size_t)sk * (BM * BN) + (size_t)r_in_tile * BN;
+        // tcgen05.ld is warp-collective: every lane loads, rows past M skip the add
         if (ok) {
 #pragma unroll 1
           for (int c = 0; c < BN; c += 16) {
             float v[16];
             tmem_ld16(taddr + c, v);
-            if (row < args.M) {
-              float* dst = ws + (size_t)r_in_tile * BN + c;
-#pragma unroll
-              for (int i = 0; i < 16; i += 4)
-                __stcg(reinterpret_cast<float4*>(dst + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
-            }
+            if (row < args.M) red_add16(ws + c, v);
           }
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
-        __threadfence();
-        named_barrier(1, 128);
-        if (et == 0) {
-          int last = 0;
-          if (!error_set()) {
-            const int prev = atomicAdd(&args.tile_counters[tile], 1);
-            last = (prev == S - 1);
-            if (last) args.tile_counters[tile] = 0;   // ready for the next GEMM
-          }
-          *flag_smem = last;
-        }
-        named_barrier(1, 128);
-        const int last = *flag_smem;
-        named_barrier(1, 128);   // flag_smem is rewritten by the next unit
+        const bool last = sk_arrive(args, sk, kb1 - kb0, et, flag_smem);
         if (last && row < args.M) {
-          __threadfence();
-          const float* base = args.workspace + (size_t)tile * S * (BM * BN) + (size_t)r_in_tile * BN;
           if (EPI == EPI_SILU) {
 #pragma unroll 1
             for (int c = 0; c < BN / 2; c += 16) {
-              float g[16] = {}, up[16] = {}, o[16];
-              for (int s = 0; s < S; ++s) {
-                const float* p = base + (size_t)s * (BM * BN);
-#pragma unroll
-                for (int i = 0; i < 16; i += 4) {
-                  float4 x = __ldcg(reinterpret_cast<const float4*>(p + c + i));
-                  float4 y = __ldcg(reinterpret_cast<const float4*>(p + BN / 2 + c + i));
-                  g[i] += x.x; g[i + 1] += x.y; g[i + 2] += x.z; g[i + 3] += x.w;
-                  up[i] += y.x; up[i + 1] += y.y; up[i + 2] += y.z; up[i + 3] += y.w;
-                }
-              }
+              float g[16], up[16], o[16];
+              take16(ws + c, g);
+              take16(ws + BN / 2 + c, up);
 #pragma unroll
               for (int i = 0; i < 16; ++i) o[i] = silu(g[i]) * up[i];
               store16<EPI_BF16>(args, row, col0 + c, o);
@@ -345,15 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
 #pragma unroll 1
             for (int c = 0; c < BN; c += 16) {
-              float v[16] = {};
-              for (int s = 0; s < S; ++s) {
-                const float* p = base + (size_t)s * (BM * BN) + c;
-#pragma unroll
-                for (int i = 0; i < 16; i += 4) {
-                  float4 x = __ldcg(reinterpret_cast<const float4*>(p + i));
-                  v[i] += x.x; v[i + 1] += x.y; v[i + 2] += x.z; v[i + 3] += x.w;
-                }
-              }
+              float v[16];
+              take16(ws + c, v);
               store16<EPI>(args, row, col0 + c, v);
             }
           }
@@ -391,7 +380,7 @@ void launch(const GemmPlan& p, cudaStream_t stream) {
     cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     attr_set = true;
   }
-  gemm_kernel<BN, EPI><<<p.grid, kThreads, C::kSmemBytes, stream>>>(p.tmA, p.tmB, p.args);
+  launch_k(gemm_kernel<BN, EPI>, dim3(p.grid), dim3(kThreads), C::kSmemBytes, stream, p.tmA, p.tmB, p.args);
 }
 
 template <int EPI>
@@ -438,17 +427,18 @@ int choose_bn(int M, int N, int epi) {
   return 64;
 }
 
-size_t workspace_floats(int m_tiles, int n_tiles, int split_k, int bn) {
-  return split_k > 1 ? (size_t)m_tiles * n_tiles * split_k * BM * bn : 0;
+size_t plan_workspace_floats(const GemmPlan& p) {
+  const size_t tile = p.swap ? (size_t)256 * p.bnt : (size_t)BM * p.bn;
+  return (size_t)p.args.sk_tiles * tile;
 }
 
-GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, int max_split) {
+GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
   GemmPlan p{};
   p.epi = epi;
-  // few tokens: swap operands so the weight tile fills the 128-row MMA side
-  if ((bn == 0 || bn == 256) && M <= 32 && N >= 256) {
+  // up to 128 tokens: swap operands so the weight tile fills the 128-row MMA side
+  if ((bn == 0 || bn == 256) && M <= 128 && N >= 256) {
     p.swap = 1;
-    p.bnt = M <= 16 ? 16 : 32;
+    p.bnt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
     p.bn = 256;
   } else {
     p.bn = bn > 0 ? bn : choose_bn(M, N, epi);
@@ -457,25 +447,34 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, int max_split) {
   const int n_tiles = (N + p.bn - 1) / p.bn;
   const int num_kb = (K + BK - 1) / BK;
   const int sms = num_sms();
-  int split = 1;
   const int tiles = m_tiles * n_tiles;
-  if (tiles < sms && max_split > 1) {
-    split = sms / tiles;
-    split = split > max_split ? max_split : split;
-    const int min_kb_per_split = 4;
-    while (split > 1 && num_kb / split < min_kb_per_split) --split;
-    // every split must own at least one k-block
-    while (split > 1 && ((num_kb + split - 1) / split) * (split - 1) >= num_kb) --split;
+  int dp = tiles, sk = 0, grid = tiles < sms ? tiles : sms;
+  if (stream_k && tiles % sms != 0) {
+    // whole waves stay data-parallel; the last partial wave plus one full
+    // wave is spread evenly over every SM along K
+    const int waves = tiles / sms;
+    dp = waves > 0 ? (waves - 1) * sms : 0;
+    sk = tiles - dp;
+    grid = sms;
+    // at least 4 k-blocks per CTA so each partial is worth its reduction
+    const long long iters = (long long)sk * num_kb;
+    if (dp == 0 && iters < 4LL * sms) grid = (int)(iters / 4 > 0 ? iters / 4 : 1);
+    if (dp == 0 && grid <= tiles) {   // no gain over whole tiles
+      dp = tiles;
+      sk = 0;
+      grid = tiles < sms ? tiles : sms;
+    }
   }
   p.args.M = M;
   p.args.N = N;
   p.args.K = K;
   p.args.m_tiles = m_tiles;
   p.args.n_tiles = n_tiles;
-  p.args.split_k = split;
+  p.args.num_kb = num_kb;
+  p.args.dp_tiles = dp;
+  p.args.sk_tiles = sk;
   p.args.n_out = epi == EPI_SILU ? N / 2 : N;
-  const int units = tiles * split;
-  p.grid = units < sms ? units : sms;
+  p.grid = grid;
   return p;
 }
 

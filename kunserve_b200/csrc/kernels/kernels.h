@@ -91,4 +91,7 @@ void fill_normal_bf16(__nv_bfloat16* p, long long n, unsigned long long seed, fl
 void fill_value_bf16(__nv_bfloat16* p, long long n, float v, cudaStream_t s);
 // Read (and optionally clear) the device error flag: code | (info << 8).
 long long error_flag(bool reset);
+// Launches of forward-pass kernels from this host thread carry programmatic
+// stream serialization (the next kernel starts while the previous drains).
+void set_pdl(bool on);
 }  // namespace kus

@@ -19,7 +19,8 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 256, 256), (7, 512, 1024), (33, 2816, 1024), (65, 1024, 512), (128, 640, 512), (300, 1024, 4096),
-                                   (1000, 768, 2048), (64, 4096, 4096), (2, 32000, 512)])
+                                   (1000, 768, 2048), (64, 4096, 4096), (2, 32000, 512), (100, 6144, 4096),
+                                   (512, 6144, 4096), (2048, 6144, 1024)])
 @pytest.mark.parametrize("max_split", [1, 16])
 def test_gemm_bf16(C, M, N, K, max_split):
     torch.manual_seed(0)
@@ -30,6 +31,23 @@ def test_gemm_bf16(C, M, N, K, max_split):
     torch.cuda.synchronize()
     ref = A.float() @ B.float().t()
     assert _rel(out, ref) < 1e-2
+    from kunserve_b200.ops import check_error
+    check_error()
+
+
+def test_gemm_stream_k_workspace_returns_to_zero(C):
+    """Tiles split along K leave the shared accumulators zero, so a second
+    (different) problem on the same workspace is exact too."""
+    torch.manual_seed(3)
+    for M, N, K in ((64, 6144, 4096), (512, 6144, 4096), (2048, 6144, 1024), (100, 28672, 4096)):
+        outs = []
+        for rep in range(2):
+            A = torch.randn(M, K, device="cuda").bfloat16()
+            B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            sk = C.gemm(A, B, out, C.EPI_BF16, None, 0, 16)
+            assert sk > 0, (M, N, K)
+            assert _rel(out, A.float() @ B.float().t()) < 1e-2
     from kunserve_b200.ops import check_error
     check_error()
 
@@ -51,11 +69,13 @@ def test_gemm_f32_add_silu(C):
     gate = (torch.randn(F, K, device="cuda") * 0.05).bfloat16()
     up = (torch.randn(F, K, device="cuda") * 0.05).bfloat16()
     inter = torch.stack([gate.view(F // 128, 128, K), up.view(F // 128, 128, K)], 1).reshape(2 * F, K).contiguous()
-    act = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
-    for ms in (1, 16):
-        C.gemm(A, inter, act, C.EPI_SILU, None, 256, ms)
-        g, u = A.float() @ gate.float().t(), A.float() @ up.float().t()
-        assert _rel(act, torch.nn.functional.silu(g) * u) < 1e-2
+    for M in (37, 100, 700):
+        A = torch.randn(M, K, device="cuda").bfloat16()
+        act = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+        for ms in (1, 16):
+            C.gemm(A, inter, act, C.EPI_SILU, None, 256, ms)
+            g, u = A.float() @ gate.float().t(), A.float() @ up.float().t()
+            assert _rel(act, torch.nn.functional.silu(g) * u) < 1e-2
     torch.cuda.synchronize()
 
 
