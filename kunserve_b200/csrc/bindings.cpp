@@ -86,6 +86,7 @@ KVGeom make_geom(torch::Tensor pool, int64_t P, int64_t N, int64_t Ls, int64_t L
   g.block_size = (int)block_size;
   g.kvh = (int)kvh;
   g.hd = (int)hd;
+  finish_geom(g);
   return g;
 }
 
@@ -120,7 +121,13 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
   b.dec_splits = (int)dec_splits;
   AttnScratch sc{o_part.data_ptr<float>(), ml_part.data_ptr<float>(), dec_o.data_ptr<float>(),
                  dec_ml.data_ptr<float>()};
-  paged_attention(bp(q), (int)q_stride, bp(out), geo, (int)layer, b, sc, q.size(0), (int)nq, (float)scale,
+  CUtensorMap tq, tkv;
+  TORCH_CHECK(make_attn_q_map(&tq, q.data_ptr(), (int)q.size(0), (int)nq, (int)q_stride, (int)(nq / nkv)),
+              "attention q tensor map");
+  TORCH_CHECK(make_attn_kv_map(&tkv, pool.data_ptr(), (long long)pool.numel() * pool.element_size(), (int)nkv,
+                               (int)block_size),
+              "attention kv tensor map");
+  paged_attention(tq, tkv, bp(q), (int)q_stride, bp(out), geo, (int)layer, b, sc, q.size(0), (int)nq, (float)scale,
                   at::cuda::getCurrentCUDAStream());
 }
 
@@ -260,6 +267,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fill_normal", &fill_normal_op);
   m.def("nccl_unique_id", &nccl_unique_id);
   m.def("error_flag", &read_error_flag, py::arg("reset") = true);
+  m.def("attention_q_rows_per_tile", &attention_q_rows_per_tile);
   m.def("num_sms", &num_sms);
   m.attr("EPI_BF16") = (int)EPI_BF16;
   m.attr("EPI_F32") = (int)EPI_F32;

@@ -52,6 +52,8 @@ class Arena {
   char* layer_ptr(int l) const { return reinterpret_cast<char*>(segs_[l].home); }
   char* kv_base() const { return reinterpret_cast<char*>(kv_va_); }
   size_t kv_base_bytes() const { return kv_base_bytes_; }
+  // whole reserved KV range: base pages plus room for every layer's extend pages
+  size_t kv_va_bytes() const { return kv_va_bytes_; }
   size_t granularity() const { return gran_; }
   size_t layer_bytes(int l) const { return segs_[l].bytes; }
   int num_layers() const { return (int)segs_.size(); }

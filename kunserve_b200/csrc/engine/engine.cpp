@@ -109,6 +109,7 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
     KUS_CHECK(make_tmap_bf16(&m_ylast_[i], ylast_.data_ptr(), ylast_.size(0), s.hidden, s.hidden, box), "tmap ylast");
   }
   KUS_CHECK(make_tmap_bf16(&m_lm_head_, lm_head_.data_ptr(), s.vocab, s.hidden, s.hidden, 256), "tmap lm_head");
+  KUS_CHECK(make_attn_q_map(&m_attn_q_, qkv_.data_ptr(), (int)T, s.nq, (int)qkv_n_, s.nq / s.nkv), "tmap attention q");
 }
 
 Engine::~Engine() {
@@ -138,6 +139,8 @@ void Engine::init_memory(int64_t num_pages) {
     build_layer_maps(l);
   }
   check_cuda(cudaMemset(arena_->kv_base(), 0, arena_->kv_phys_bytes()), "zero kv");
+  KUS_CHECK(make_attn_kv_map(&m_attn_kv_, arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv, s_.block_size),
+            "tmap attention kv");
 }
 
 void Engine::build_layer_maps(int l) {
@@ -292,6 +295,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   geo.block_size = s_.block_size;
   geo.kvh = s_.nkv;
   geo.hd = s_.hd;
+  finish_geom(geo);
 
   AttnBatch ab;
   ab.q_start = q_start;
@@ -348,7 +352,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
     rope_append(qkv, positions, kv_page, kv_slot, cos_sin_.data_ptr<float>(), geo, ll, (int)T, s_.nq, s_.nkv,
                 s_.max_pos, st);
-    paged_attention(qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
+    paged_attention(m_attn_q_, m_attn_kv_, qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
     if (sync_debug_) debug_check("attention", (int)T, (int)B, (int)n_dec, st);
     launches_ += 3 + (splits > 1 ? 1 : 0);
     if (fused) {

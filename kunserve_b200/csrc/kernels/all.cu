@@ -6,7 +6,7 @@
 #include "gemm_tcgen05.cu"
 #include "gemm_swap.cu"
 #include "elementwise.cu"
-#include "attention.cu"
+#include "attention_tc.cu"
 #include "attention_decode.cu"
 #include "init.cu"
 

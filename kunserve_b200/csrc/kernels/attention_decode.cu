@@ -57,11 +57,11 @@ __global__ void __launch_bounds__(kWarps * 32) decode_attn_kernel(const __nv_bfl
   for (int grp = g0 + warp; grp < g1; grp += kWarps) {
     const int key = grp * 32 + lane;
     const bool valid = key < ctx;
-    const int page = valid ? table[key / g.block_size] : table[0];
-    const int slot = valid ? key % g.block_size : 0;
+    const int page = valid ? table[kv_page_col(g, key)] : table[0];
+    const int slot = valid ? kv_page_slot(g, key) : 0;
     const size_t tok_off = (size_t)slot * g.kvh * HD + head_off;
     const __nv_bfloat16* kp = kv_ptr(g, page, layer, false) + tok_off;
-    const __nv_bfloat16* vp = kv_ptr(g, page, layer, true) + tok_off;
+    const __nv_bfloat16* vp = kp + (size_t)g.block_size * g.kvh * HD;   // V follows K in a slot
     float s[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) s[h] = 0.f;

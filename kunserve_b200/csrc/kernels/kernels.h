@@ -19,21 +19,49 @@ struct KVGeom {
   int block_size;
   int kvh;
   int hd;
+  int spp;                // layer slots per physical page (page_stride / layer_stride)
+  int bs_shift;           // log2(block_size) when it is a power of two, else -1
 };
 
-__host__ __device__ __forceinline__ long long kv_offset(const KVGeom& g, int page, int layer, bool v) {
-  long long off;
+// Fill the derived fields of a geometry whose other fields are set.
+inline void finish_geom(KVGeom& g) {
+  g.spp = (int)(g.page_stride / g.layer_stride);
+  g.bs_shift = -1;
+  for (int s = 0; s < 31; ++s)
+    if ((1 << s) == g.block_size) g.bs_shift = s;
+}
+
+// Index of the (page, layer) slot in units of layer_stride, with 32-bit
+// arithmetic only (the pool is an array of such slots).
+__host__ __device__ __forceinline__ int kv_slot(const KVGeom& g, int page, int layer) {
+  if (page < g.P) return page * g.spp + layer;   // unfused ids, and slice 0 of fused ids
   const int np = g.N * g.P;
   if (page < np) {
-    off = (long long)(page % g.P) * g.page_stride + ((long long)(page / g.P) * g.Ls + layer) * g.layer_stride;
-  } else {
-    off = (long long)g.P * g.page_stride + ((long long)(page - np) * g.Ls + layer) * g.layer_stride;
+    int p = page, sl = 0;
+    do {
+      p -= g.P;
+      ++sl;
+    } while (p >= g.P);
+    return p * g.spp + sl * g.Ls + layer;
   }
+  return g.P * g.spp + (page - np) * g.Ls + layer;
+}
+
+__host__ __device__ __forceinline__ long long kv_offset(const KVGeom& g, int page, int layer, bool v) {
+  const long long off = (long long)kv_slot(g, page, layer) * g.layer_stride;
   return v ? off + g.layer_stride / 2 : off;
 }
 
 __host__ __device__ __forceinline__ __nv_bfloat16* kv_ptr(const KVGeom& g, int page, int layer, bool v) {
   return reinterpret_cast<__nv_bfloat16*>(g.base + kv_offset(g, page, layer, v));
+}
+
+// Page-table column and slot of token position `key`.
+__host__ __device__ __forceinline__ int kv_page_col(const KVGeom& g, int key) {
+  return g.bs_shift >= 0 ? key >> g.bs_shift : key / g.block_size;
+}
+__host__ __device__ __forceinline__ int kv_page_slot(const KVGeom& g, int key) {
+  return g.bs_shift >= 0 ? key & (g.block_size - 1) : key % g.block_size;
 }
 
 void embed(const int* tokens, const __nv_bfloat16* table, __nv_bfloat16* out, int T, int H, int V, cudaStream_t s);
@@ -74,9 +102,16 @@ struct AttnScratch {
 };
 
 // q: [T, q_stride] bf16 (first nq*hd columns are the rotated queries);
-// out: [T, nq*hd] bf16.
-void paged_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
-                     const AttnBatch& b, const AttnScratch& sc, int T, int nq, float scale, cudaStream_t s);
+// out: [T, nq*hd] bf16.  Prefill tiles read Q and paged K/V through the
+// tensor maps of make_attn_q_map / make_attn_kv_map (attention_tc.cu);
+// decode requests read q directly (attention_decode.cu).
+void paged_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride,
+                     __nv_bfloat16* out, const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int T,
+                     int nq, float scale, cudaStream_t s);
+// 3-D map over q viewed as [tokens][nq heads][128 dims] (token stride q_stride elements).
+bool make_attn_q_map(CUtensorMap* map, const void* q, int tokens, int nq, int q_stride, int group);
+// 3-D map over a KV pool viewed as [rows][kvh][128 dims], one row per token slot.
+bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size);
 int attention_q_rows_per_tile();
 // Decode requests of the batch only (attention_decode.cu); paged_attention
 // calls it after the prefill items.

@@ -23,14 +23,14 @@ from .step import StepInput
 MAX_ENGINE_TOKENS = 16384
 ATTN_SPLIT_TOKENS = 512
 DEC_SPLIT_SLOTS = 1024          # dec_splits * n_dec bound (engine scratch)
-Q_TILE_ROWS = 64
+Q_TILE_ROWS = 128      # query rows per prefill attention tile (the kernel's BM)
 
 
 def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf: np.ndarray):
     """Fill ``buf`` (int32) with the engine's step metadata; returns
     ``(n_ints, T, B, n_items, max_ctx, n_dec)``.  Requests with one query
     token go to the decode kernel (list at the end); the others become
-    64-row query tiles (``items``) of the prefill kernel."""
+    ``Q_TILE_ROWS``-row query tiles (``items``) of the prefill kernel."""
     B = step.num_requests
     ql = np.fromiter((len(t) for t in step.input_tokens), dtype=np.int64, count=B)
     T = int(ql.sum())
@@ -85,6 +85,7 @@ class NativeRunner:
                  comm=None, num_cpu_blocks: int = 0, weights=None):
         C = native()
         self.C = C
+        assert C.attention_q_rows_per_tile() == Q_TILE_ROWS, "extension and runner disagree on the query tile"
         self.mc, self.pc, self.layout, self.comm = mc, pc, layout, comm
         self.device = device
         sh = C.EngineShape()

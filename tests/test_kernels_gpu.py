@@ -211,6 +211,55 @@ def test_paged_attention(C, nq, nkv, splits):
     assert _rel(out.view(T, nq, hd), ref) < 2e-2
 
 
+@pytest.mark.parametrize("nq,nkv", [(4, 4), (8, 2), (8, 1)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_prefill_attention_long_chunks(C, nq, nkv, splits):
+    """tcgen05 prefill tiles: chunks longer than one 128-row tile, prefixes
+    that span several 128-key blocks, causal masks inside blocks."""
+    import numpy as np
+    from kunserve_b200.engine.native_runner import pack_meta
+    from kunserve_b200.engine.step import StepInput
+    torch.manual_seed(6)
+    hd, bs, L, P, N = 128, 16, 2, 256, 1
+    lay, pool = _pool(P, L, bs, nkv, hd)
+    pool.copy_(torch.randn_like(pool.float()).bfloat16())
+    starts, qlens = [200, 0, 1000, 37], [300, 150, 64, 1]
+    rng = np.random.default_rng(1)
+    perm = rng.permutation(P).tolist()
+    tables, k = [], 0
+    for s0, n in zip(starts, qlens):
+        need = (s0 + n + bs - 1) // bs
+        tables.append(perm[k:k + need])
+        k += need
+    T = sum(qlens)
+    q = torch.randn(T, nq * hd, device="cuda").bfloat16()
+    B = len(qlens)
+    step = StepInput(list(range(B)), [[0] * n for n in qlens], starts, tables, [1] * B, 0, 1)
+    buf = np.zeros(16384, dtype=np.int32)
+    width = max(len(t) for t in tables)
+    n_int, T2, B2, n_items, _, n_dec = pack_meta(step, bs, nq // nkv, width, buf)
+    items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
+    dec = torch.from_numpy(buf[n_int - n_dec:n_int].copy()).cuda()
+    o = 2 * n_items + 4 * T
+    q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
+    ctx = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
+    tab = torch.zeros(B, width, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        tab[i, :len(t)] = torch.tensor(t)
+    out = torch.empty(T, nq * hd, device="cuda", dtype=torch.bfloat16)
+    o_part = torch.empty(splits * T * nq * hd, device="cuda")
+    ml = torch.empty(splits * T * nq * 2, device="cuda")
+    dec_o = torch.empty(4 * nq * hd, device="cuda")
+    dec_ml = torch.empty(4 * nq * 2, device="cuda")
+    C.attention(q, nq * hd, out, pool, P, N, L, L, bs, nkv, 1, q_start, ctx, tab.cuda(), items, splits,
+                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, 1, dec_o, dec_ml)
+    torch.cuda.synchronize()
+    from kunserve_b200.ops import check_error
+    check_error()
+    ref = _ref_attention(q, pool, lay, N, 1, tables, starts, qlens, nq, nkv, hd)
+    assert _rel(out.view(T, nq, hd), ref) < 2e-2
+
+
 def test_sample_greedy_and_temperature(C):
     torch.manual_seed(5)
     logits = torch.randn(6, 32000, device="cuda")
