@@ -108,7 +108,7 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
     KUS_CHECK(make_tmap_bf16(&m_act_[i], act_.data_ptr(), T, f_pad_, f_pad_, box), "tmap act");
     KUS_CHECK(make_tmap_bf16(&m_ylast_[i], ylast_.data_ptr(), ylast_.size(0), s.hidden, s.hidden, box), "tmap ylast");
   }
-  KUS_CHECK(make_tmap_bf16(&m_lm_head_, lm_head_.data_ptr(), s.vocab, s.hidden, s.hidden, 256), "tmap lm_head");
+  KUS_CHECK(make_wmap(&m_lm_head_, lm_head_.data_ptr(), s.vocab, s.hidden, false), "tmap lm_head");
   KUS_CHECK(make_attn_q_map(&m_attn_q_, qkv_.data_ptr(), (int)T, s.nq, (int)qkv_n_, s.nq / s.nkv), "tmap attention q");
 }
 
@@ -146,10 +146,11 @@ void Engine::init_memory(int64_t num_pages) {
 void Engine::build_layer_maps(int l) {
   LayerW& w = layers_[l];
   const int H = s_.hidden;
-  KUS_CHECK(make_tmap_bf16(&w.m_qkv, w.qkv, qkv_n_, H, H, 256), "tmap qkv");
-  KUS_CHECK(make_tmap_bf16(&w.m_o, w.o, H, s_.nq * s_.hd, s_.nq * s_.hd, 256), "tmap o");
-  KUS_CHECK(make_tmap_bf16(&w.m_gu, w.gu, 2 * f_pad_, H, H, 256), "tmap gu");
-  KUS_CHECK(make_tmap_bf16(&w.m_down, w.down, H, f_pad_, f_pad_, 256), "tmap down");
+  // gate/up stay on 256-row tiles: their rows interleave per 128 (gate, up)
+  KUS_CHECK(make_wmap(&w.m_qkv, w.qkv, qkv_n_, H, true), "tmap qkv");
+  KUS_CHECK(make_wmap(&w.m_o, w.o, H, s_.nq * s_.hd, true), "tmap o");
+  KUS_CHECK(make_wmap(&w.m_gu, w.gu, 2 * f_pad_, H, false), "tmap gu");
+  KUS_CHECK(make_wmap(&w.m_down, w.down, H, f_pad_, true), "tmap down");
 }
 
 static torch::Tensor dev_view(void* p, std::vector<int64_t> shape, int device) {
@@ -222,14 +223,24 @@ torch::Tensor Engine::layer_bytes_view(int l) {
 torch::Tensor Engine::hidden() { return h_; }
 torch::Tensor Engine::logits() { return logits_; }
 
-void Engine::gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
+bool make_wmap(WMap* m, const void* w, int rows, int cols, bool with128) {
+  m->has128 = with128;
+  if (!make_tmap_bf16(&m->b256, w, rows, cols, cols, 256)) return false;
+  return !with128 || make_tmap_bf16(&m->b128, w, rows, cols, cols, 128);
+}
+
+static const CUtensorMap& pick(const WMap& m, const GemmPlan& p) { return p.bn == 128 ? m.b128 : m.b256; }
+
+void Engine::gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, int epi, void* out, int ldc,
                   const __nv_bfloat16* res, cudaStream_t st) {
-  GemmPlan p = plan_gemm(M, N, K, epi, 256, true);
+  const int bn = mB.has128 ? 0 : 256;
+  GemmPlan p = plan_gemm(M, N, K, epi, bn, true);
   if (plan_workspace_floats(p) > (size_t)gemm_ws_.numel() || plan_counters(p) >= counters_.numel())
-    p = plan_gemm(M, N, K, epi, 256, false);
+    p = plan_gemm(M, N, K, epi, bn, false);
+  KUS_CHECK(p.bn == 256 || (p.bn == 128 && mB.has128), "no weight map for the planned tile");
   const int box = a_box_rows(p);
   p.tmA = mA[box == 16 ? 0 : box == 32 ? 1 : box == 64 ? 2 : 3];
-  p.tmB = mB;
+  p.tmB = pick(mB, p);
   p.args.out = out;
   p.args.ldc = ldc;
   p.args.residual = res;
@@ -464,13 +475,15 @@ void Engine::set_tp_peers(const std::vector<int64_t>& bases) {
   fused_ = true;
 }
 
-void Engine::tp_push_gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, cudaStream_t st) {
-  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, 256, true);
+void Engine::tp_push_gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, cudaStream_t st) {
+  const int bn = mB.has128 ? 0 : 256;
+  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, bn, true);
   if (plan_workspace_floats(p) > (size_t)gemm_ws_.numel() || plan_counters(p) >= counters_.numel())
-    p = plan_gemm(M, N, K, EPI_PUSH, 256, false);
+    p = plan_gemm(M, N, K, EPI_PUSH, bn, false);
+  KUS_CHECK(p.bn == 256 || (p.bn == 128 && mB.has128), "no weight map for the planned tile");
   const int box = a_box_rows(p);
   p.tmA = mA[box == 16 ? 0 : box == 32 ? 1 : box == 64 ? 2 : 3];
-  p.tmB = mB;
+  p.tmB = pick(mB, p);
   ++epoch_;
   const int64_t slot = (int64_t)s_.max_tokens * s_.hidden * 2;
   const int64_t data = kRbFlagBytes + (int64_t)(epoch_ & 1) * s_.tp * slot + (int64_t)tp_rank_ * slot;

@@ -33,9 +33,19 @@ struct EngineShape {
   int tp;
 };
 
+// Weight tensor maps for 256-row tiles and, where the planner may pick
+// them, 128-row tiles.
+struct WMap {
+  CUtensorMap b256, b128;
+  bool has128 = false;
+};
+
+// Maps for a [rows, cols] row-major bf16 weight (128-row ones if asked).
+bool make_wmap(WMap* m, const void* w, int rows, int cols, bool with128);
+
 struct LayerW {
   __nv_bfloat16 *in_norm, *post_norm, *qkv, *o, *gu, *down;
-  CUtensorMap m_qkv, m_o, m_gu, m_down;
+  WMap m_qkv, m_o, m_gu, m_down;
 };
 
 class Engine {
@@ -99,7 +109,7 @@ class Engine {
 
  private:
   void build_layer_maps(int l);
-  void gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, int epi, void* out, int ldc,
+  void gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, int epi, void* out, int ldc,
             const __nv_bfloat16* res, cudaStream_t s);
   void all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t s);
 
@@ -111,7 +121,7 @@ class Engine {
   std::unique_ptr<Arena> arena_;
   std::vector<LayerW> layers_;
   torch::Tensor embed_, final_norm_, lm_head_;
-  CUtensorMap m_lm_head_;
+  WMap m_lm_head_;
   // workspaces
   torch::Tensor h_, y_, qkv_, attn_, act_, tmp_, ylast_, logits_, gemm_ws_, counters_, attn_o_, attn_ml_,
       meta_dev_, tokens_dev_, tokens_host_, cos_sin_, dec_o_, dec_ml_;
@@ -128,7 +138,7 @@ class Engine {
   bool fused_ = false;
   int64_t fused_max_tokens_ = 32;
   unsigned epoch_ = 0;
-  void tp_push_gemm(const CUtensorMap* mA, const CUtensorMap& mB, int M, int N, int K, cudaStream_t s);
+  void tp_push_gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, cudaStream_t s);
   void tp_reduce(__nv_bfloat16* h, const __nv_bfloat16* w, __nv_bfloat16* y, int T, cudaStream_t s);
   int64_t launches_ = 0;
   // KUNSERVE_SYNC_DEBUG=1: synchronize after every launch and name the

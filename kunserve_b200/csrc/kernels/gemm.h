@@ -56,8 +56,9 @@ int num_sms();
 bool make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                     uint32_t box_rows);
 int choose_bn(int M, int N, int epi);
-// Tiles and work split for an M x N x K problem (bn <= 0: choose).  With
-// stream_k false every tile is a whole-tile unit (no workspace traffic).
+// Tiles and work split for an M x N x K problem (bn <= 0: choose).  Stream-K
+// applies to the swapped decode kernel only; with stream_k false, or for the
+// regular kernel, every tile is a whole-tile unit (no workspace traffic).
 GemmPlan plan_gemm(int M, int N, int K, int epi, int bn = 0, bool stream_k = true);
 // fp32 workspace floats and counters a plan needs (workspace all zero).
 size_t plan_workspace_floats(const GemmPlan& p);

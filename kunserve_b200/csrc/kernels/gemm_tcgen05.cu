@@ -420,11 +420,20 @@ bool make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t c
   return r == CUDA_SUCCESS;
 }
 
+// Output tile width for the data-parallel kernel: 256 columns unless 128
+// fills the SMs' waves markedly better (a 128-wide tile re-reads A twice as
+// often per FLOP, hence the 0.9 weight).
 int choose_bn(int M, int N, int epi) {
   if (epi == EPI_SILU) return 256;   // weights are interleaved in 128-row halves
-  if (N >= 256) return 256;
-  if (N >= 128) return 128;
-  return 64;
+  if (N < 256) return N >= 128 ? 128 : 64;
+  const int sms = num_sms();
+  const int mt = (M + BM - 1) / BM;
+  auto eff = [&](int bn, double w) {
+    const int t = mt * ((N + bn - 1) / bn);
+    const int waves = (t + sms - 1) / sms;
+    return w * t / (double)(waves * sms);
+  };
+  return eff(128, 0.9) > eff(256, 1.0) ? 128 : 256;
 }
 
 size_t plan_workspace_floats(const GemmPlan& p) {
@@ -449,7 +458,9 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
   const int sms = num_sms();
   const int tiles = m_tiles * n_tiles;
   int dp = tiles, sk = 0, grid = tiles < sms ? tiles : sms;
-  if (stream_k && tiles % sms != 0) {
+  // stream-K only for the memory-bound swapped kernel: for compute-bound
+  // tiles the fp32 reductions cost more than the partial last wave
+  if (stream_k && p.swap && tiles % sms != 0) {
     // whole waves stay data-parallel; the last partial wave plus one full
     // wave is spread evenly over every SM along K
     const int waves = tiles / sms;
