@@ -121,14 +121,18 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
   b.dec_splits = (int)dec_splits;
   AttnScratch sc{o_part.data_ptr<float>(), ml_part.data_ptr<float>(), dec_o.data_ptr<float>(),
                  dec_ml.data_ptr<float>()};
-  CUtensorMap tq, tkv;
+  CUtensorMap tq, tkv, tkv_dec;
+  const long long pool_bytes = (long long)pool.numel() * pool.element_size();
   TORCH_CHECK(make_attn_q_map(&tq, q.data_ptr(), (int)q.size(0), (int)nq, (int)q_stride, (int)(nq / nkv)),
               "attention q tensor map");
-  TORCH_CHECK(make_attn_kv_map(&tkv, pool.data_ptr(), (long long)pool.numel() * pool.element_size(), (int)nkv,
-                               (int)block_size),
+  TORCH_CHECK(make_attn_kv_map(&tkv, pool.data_ptr(), pool_bytes, (int)nkv, (int)block_size,
+                               attention_q_rows_per_tile()),
               "attention kv tensor map");
-  paged_attention(tq, tkv, bp(q), (int)q_stride, bp(out), geo, (int)layer, b, sc, q.size(0), (int)nq, (float)scale,
-                  at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(make_attn_kv_map(&tkv_dec, pool.data_ptr(), pool_bytes, (int)nkv, (int)block_size,
+                               decode_attention_block_keys()),
+              "decode attention kv tensor map");
+  paged_attention(tq, tkv, tkv_dec, bp(q), (int)q_stride, bp(out), geo, (int)layer, b, sc, q.size(0), (int)nq,
+                  (float)scale, at::cuda::getCurrentCUDAStream());
 }
 
 void sample_op(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, int64_t step, torch::Tensor out) {

@@ -139,8 +139,12 @@ void Engine::init_memory(int64_t num_pages) {
     build_layer_maps(l);
   }
   check_cuda(cudaMemset(arena_->kv_base(), 0, arena_->kv_phys_bytes()), "zero kv");
-  KUS_CHECK(make_attn_kv_map(&m_attn_kv_, arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv, s_.block_size),
+  KUS_CHECK(make_attn_kv_map(&m_attn_kv_, arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv, s_.block_size,
+                             attention_q_rows_per_tile()),
             "tmap attention kv");
+  KUS_CHECK(make_attn_kv_map(&m_dec_kv_, arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv, s_.block_size,
+                             decode_attention_block_keys()),
+            "tmap decode attention kv");
 }
 
 void Engine::build_layer_maps(int l) {
@@ -363,7 +367,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
     rope_append(qkv, positions, kv_page, kv_slot, cos_sin_.data_ptr<float>(), geo, ll, (int)T, s_.nq, s_.nkv,
                 s_.max_pos, st);
-    paged_attention(m_attn_q_, m_attn_kv_, qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
+    paged_attention(m_attn_q_, m_attn_kv_, m_dec_kv_, qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
     if (sync_debug_) debug_check("attention", (int)T, (int)B, (int)n_dec, st);
     launches_ += 3 + (splits > 1 ? 1 : 0);
     if (fused) {

@@ -128,7 +128,7 @@ class Engine {
   // activation TMA descriptors per token-box height (16, 32, 64, 128 rows)
   CUtensorMap m_y_[4], m_attn_[4], m_act_[4], m_ylast_[4];
   // prefill attention: queries in qkv_ and the whole reserved KV range
-  CUtensorMap m_attn_q_, m_attn_kv_;
+  CUtensorMap m_attn_q_, m_attn_kv_, m_dec_kv_;
   int64_t attn_split_tokens_ = 0;
   int attn_max_splits_ = 16;
   ncclComm_t tp_comm_ = nullptr;

@@ -1,16 +1,20 @@
-// Paged decode attention on the CUDA cores: one query token per request.
+// Paged decode attention: one query token per request, on the tensor cores.
 //
 // One CTA serves (request, KV head, key split) for the whole GQA group of G
-// query heads.  Each lane owns one key of a 32-key group: it streams the
-// key's K row (256 B, 16-byte loads) and scores it against the G queries,
-// which sit in shared memory and are read as broadcasts.  Each warp keeps an
-// online softmax per head; for P*V every lane owns 4 of the 128 dims, so the
-// V rows of the group stream coalesced (8 bytes per lane, 256 B per key) and
-// each lane's probability reaches the warp by shuffle.  Four warps walk
-// interleaved key groups and merge their (max, sum, acc) in shared memory.
+// query heads.  The G query rows form the M side of mma.sync m16n8k16 tiles
+// (rows G..15 are zero), so S = Q K^T and O += P V each cost one MMA per 8
+// keys / 8 dims and every K/V byte feeds all G heads.
+//
+//   thread 0   TMA producer: blocks of 64 keys, one box per page and 64-dim
+//              half for K and for V (128-byte swizzle), into a three-stage
+//              ring; mbarrier waits are bounded (common.cuh)
+//   4 warps    warp w takes keys 16w..16w+15 of every block: K fragments by
+//              ldmatrix, V fragments by ldmatrix.trans, online softmax in
+//              registers (the S accumulator layout is the A layout of P V),
+//              then the warps merge (max, sum, O) in shared memory
+//
 // With splits > 1 a CTA writes an unnormalized partial plus (max, sum) and
-// decode_combine_kernel merges the splits.  Memory traffic is one pass over
-// the request's K and V for all G heads; nothing is padded.
+// decode_combine_kernel merges the splits.
 #include "../common.cuh"
 #include "kernels.h"
 
@@ -19,139 +23,251 @@ namespace dec {
 
 constexpr int HD = 128;
 constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int BK = 64;                    // keys per block
+constexpr int kStages = 3;
+constexpr int kHalf = BK * 128;           // one 64-dim half of a block (8 KB)
+constexpr int kTile = 2 * kHalf;          // K or V of one block (16 KB)
+constexpr int kStageBytes = 2 * kTile;    // K and V
+constexpr int kQOff = kStages * kStageBytes;
+constexpr int kBarOff = kQOff + 16 * 256;
+constexpr int kSmemBytes = kBarOff + 64 + 1024;
 
-template <int G>
-__global__ void __launch_bounds__(kWarps * 32) decode_attn_kernel(const __nv_bfloat16* __restrict__ q, int q_stride,
-                                                                  __nv_bfloat16* __restrict__ out, KVGeom g,
-                                                                  int layer, AttnBatch b, AttnScratch sc, int nq,
-                                                                  float scale_log2) {
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float q_s[G][HD];
-  __shared__ float m_s[kWarps][G], l_s[kWarps][G];
-  __shared__ float acc_s[kWarps][G][HD];
+KUS_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+KUS_DEVICE void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+KUS_DEVICE void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+KUS_DEVICE void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Byte offset of 16-byte chunk `ch` (0..15 over the 128 dims) of key row `r`
+// in a block tile written by TMA with 128-byte swizzle: [half][row][128 B].
+KUS_DEVICE uint32_t kv_swz(int r, int ch) {
+  return (uint32_t)((ch >> 3) * kHalf + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+}
+// Q tile: 16 rows of 256 B, chunks XOR-swizzled by row.
+KUS_DEVICE uint32_t q_swz(int r, int ch) { return (uint32_t)(r * 256 + ((ch ^ (r & 7)) << 4)); }
+
+__global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ CUtensorMap tmKV,
+                                                               const __nv_bfloat16* __restrict__ q, int q_stride,
+                                                               __nv_bfloat16* __restrict__ out, KVGeom g, int layer,
+                                                               AttnBatch b, AttnScratch sc, int nq, float scale_log2) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint64_t* empty = full + kStages;
+
   const int di = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
+  const int G = nq / g.kvh;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int req = b.dec_reqs[di];
   const int tok = b.q_start[req];
   const int ctx = b.ctx_len[req];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int* table = b.page_table + (size_t)req * b.max_pages;
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
-    const int h = i / HD, d = i % HD;
-    q_s[h][d] = bf2f(q[(size_t)tok * q_stride + (size_t)(kh * G + h) * HD + d]);
-  }
-  __syncthreads();
-  // key range of this split, in whole 32-key groups
-  const int groups = (ctx + 31) / 32;
-  const int per = (groups + b.dec_splits - 1) / b.dec_splits;
-  const int g0 = split * per, g1 = min(g0 + per, groups);
+  const int nblk = (ctx + BK - 1) / BK;
+  const int per = (nblk + b.dec_splits - 1) / b.dec_splits;
+  const int blk0 = split * per;
+  const int nb = max(0, min(blk0 + per, nblk) - blk0);
 
-  float m[G], l[G], acc[G][4];
-#pragma unroll
-  for (int h = 0; h < G; ++h) {
-    m[h] = -1e30f;
-    l[h] = 0.f;
-    acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.f;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    fence_barrier_init();
   }
-  const size_t head_off = (size_t)kh * HD;
-  for (int grp = g0 + warp; grp < g1; grp += kWarps) {
-    const int key = grp * 32 + lane;
-    const bool valid = key < ctx;
-    const int page = valid ? table[kv_page_col(g, key)] : table[0];
-    const int slot = valid ? kv_page_slot(g, key) : 0;
-    const size_t tok_off = (size_t)slot * g.kvh * HD + head_off;
-    const __nv_bfloat16* kp = kv_ptr(g, page, layer, false) + tok_off;
-    const __nv_bfloat16* vp = kp + (size_t)g.block_size * g.kvh * HD;   // V follows K in a slot
-    float s[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) s[h] = 0.f;
-    // K row in two halves of 8 independent 16-byte loads (all in flight)
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint4 kr[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) kr[c] = __ldg(reinterpret_cast<const uint4*>(kp) + half * 8 + c);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float k8[8];
-        unpack_bf16x8(kr[c], k8);
-        const int d0 = (half * 8 + c) * 8;
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float4 qa = *reinterpret_cast<const float4*>(&q_s[h][d0]);
-          const float4 qb = *reinterpret_cast<const float4*>(&q_s[h][d0 + 4]);
-          s[h] += qa.x * k8[0] + qa.y * k8[1] + qa.z * k8[2] + qa.w * k8[3] + qb.x * k8[4] + qb.y * k8[5] +
-                  qb.z * k8[6] + qb.w * k8[7];
-        }
-      }
-    }
-    float p[G];
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float sv = valid ? s[h] * scale_log2 : -INFINITY;
-      const float mn = fmaxf(m[h], warp_max(sv));
-      const float alpha = exp2f(m[h] - mn);
-      p[h] = exp2f(sv - mn);
-      l[h] = l[h] * alpha + warp_sum(p[h]);
-      m[h] = mn;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[h][e] *= alpha;
-    }
-    // P * V: lane owns dims [4*lane, 4*lane+4) of every key's V row.  All 32
-    // rows of the group are loaded before any FMA (invalid keys read a valid
-    // page and carry p = 0).
-    const unsigned long long vaddr = reinterpret_cast<unsigned long long>(vp);
-#pragma unroll
-    for (int t0 = 0; t0 < 32; t0 += 16) {
-      uint2 vr[16];
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const unsigned long long va = __shfl_sync(0xffffffffu, vaddr, t0 + t);
-        vr[t] = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(va) + 4 * lane));
-      }
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&vr[t]);
-        const float2 v01 = __bfloat1622float2(v2[0]), v23 = __bfloat1622float2(v2[1]);
-#pragma unroll
-        for (int h = 0; h < G; ++h) {
-          const float pt = __shfl_sync(0xffffffffu, p[h], t0 + t);
-          acc[h][0] += pt * v01.x;
-          acc[h][1] += pt * v01.y;
-          acc[h][2] += pt * v23.x;
-          acc[h][3] += pt * v23.y;
-        }
-      }
-    }
-  }
-  // merge the warps
-  if (lane == 0) {
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      m_s[warp][h] = m[h];
-      l_s[warp][h] = l[h];
-    }
-  }
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc_s[warp][h][4 * lane + e] = acc[h][e];
   __syncthreads();
-  for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+  // q and the KV pages are written by the previous kernel (RoPE + KV append)
+  pdl_wait();
+  pdl_trigger();
+
+  const int box = g.block_size < BK ? g.block_size : BK;
+  const int rows_per_slot = 2 * g.block_size;
+  auto issue = [&](int i) {   // thread 0: K and V of block i into stage i % kStages
+    const int s = i % kStages;
+    mbar_arrive_expect_tx(&full[s], kStageBytes);
+    const int key_blk = (blk0 + i) * BK;
+    for (int j = 0; j * box < BK; ++j) {
+      const int key0 = key_blk + j * box;
+      // keys past the context read the request's first page: finite
+      // values that the mask turns into p = 0
+      const bool in = key0 < ctx;
+      const int page = in ? table[kv_page_col(g, key0)] : table[0];
+      const int row = kv_slot(g, page, layer) * rows_per_slot + (in ? kv_page_slot(g, key0) : 0);
+#pragma unroll
+      for (int kv = 0; kv < 2; ++kv)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          tma_load_3d(sbase + s * kStageBytes + kv * kTile + h * kHalf + j * box * 128, &tmKV, &full[s], 64 * h, kh,
+                      row + kv * g.block_size);
+    }
+  };
+  int issued = 0;   // blocks issued (thread 0 only)
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmKV);
+    for (; issued < nb && issued < kStages; ++issued) issue(issued);
+  }
+
+  // Q rows (G heads, zero padded to 16) into shared memory, then A fragments
+  uint8_t* qs = smem + kQOff;
+  for (int c = threadIdx.x; c < 16 * 16; c += kThreads) {
+    const int r = c >> 4, ch = c & 15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) v = *reinterpret_cast<const uint4*>(q + (size_t)tok * q_stride + (size_t)(kh * G + r) * HD + ch * 8);
+    *reinterpret_cast<uint4*>(qs + q_swz(r, ch)) = v;
+  }
+  __syncthreads();
+  uint32_t qf[8][4];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks)
+    ldsm_x4(sbase + kQOff + q_swz(lane & 15, ks * 2 + (lane >> 4)), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  bool ok = true;
+  for (int i = 0; i < nb; ++i) {
+    const int s = i % kStages;
+    const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+    ok = __all_sync(0xffffffffu, ok && mbar_wait(&full[s], ph, kErrWaitFull));
+    const uint32_t kt = sbase + s * kStageBytes, vt = kt + kTile;
+    // S (16 rows x 16 keys of this warp) = Q K^T
+    float sfr[2][4] = {};
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int key = warp * 16 + ((lane >> 4) << 3) + (lane & 7);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kt + kv_swz(key, ks * 2 + ((lane >> 3) & 1)), b0, b1, b2, b3);
+      mma16816(sfr[0], qf[ks], b0, b1);
+      mma16816(sfr[1], qf[ks], b2, b3);
+    }
+    // online softmax over the warp's 16 keys (rows lane/4 and lane/4 + 8)
+    const int key_base = (blk0 + i) * BK + warp * 16 + 2 * (lane & 3);
+    float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool valid = key_base + nt * 8 + e < ctx;
+        sfr[nt][e] = valid ? sfr[nt][e] * scale_log2 : -INFINITY;
+        sfr[nt][2 + e] = valid ? sfr[nt][2 + e] * scale_log2 : -INFINITY;
+        mx_lo = fmaxf(mx_lo, sfr[nt][e]);
+        mx_hi = fmaxf(mx_hi, sfr[nt][2 + e]);
+      }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
+    }
+    const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+    // a warp whose keys so far are all past the context keeps -inf: use 0
+    const float r_lo = mn_lo == -INFINITY ? 0.f : mn_lo, r_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
+    const float a_lo = exp2f(m_lo - r_lo), a_hi = exp2f(m_hi - r_hi);
+    m_lo = mn_lo;
+    m_hi = mn_hi;
+    uint32_t pa[4];
+    float sum_lo = 0.f, sum_hi = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const float p0 = exp2f(sfr[nt][0] - r_lo), p1 = exp2f(sfr[nt][1] - r_lo);
+      const float p2 = exp2f(sfr[nt][2] - r_hi), p3 = exp2f(sfr[nt][3] - r_hi);
+      sum_lo += p0 + p1;
+      sum_hi += p2 + p3;
+      pa[2 * nt] = pack_bf16x2(p0, p1);
+      pa[2 * nt + 1] = pack_bf16x2(p2, p3);
+    }
+    l_lo = l_lo * a_lo + sum_lo;
+    l_hi = l_hi * a_hi + sum_hi;
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      o[dt][0] *= a_lo;
+      o[dt][1] *= a_lo;
+      o[dt][2] *= a_hi;
+      o[dt][3] *= a_hi;
+    }
+    // O += P V over the warp's 16 keys
+#pragma unroll
+    for (int dp = 0; dp < 8; ++dp) {
+      const int key = warp * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vt + kv_swz(key, dp * 2 + (lane >> 4)), b0, b1, b2, b3);
+      mma16816(o[2 * dp], pa, b0, b1);
+      mma16816(o[2 * dp + 1], pa, b2, b3);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (threadIdx.x == 0 && i + kStages < nb && ok) {
+      // refill this stage once every warp released it
+      if (mbar_wait(&empty[s], ph, kErrWaitEmpty)) issue(issued++);
+    }
+  }
+  if (threadIdx.x == 0 && !ok) {
+    // after a timed-out wait the last issued blocks may still be in flight:
+    // let them land (bounded) before the shared memory is reused
+    for (int i = max(0, issued - kStages); i < issued; ++i)
+      mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1u, kErrWaitFull);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
+  }
+  float* m_s = reinterpret_cast<float*>(smem);            // [warp][16]
+  float* l_s = m_s + kWarps * 16;                          // [warp][16]
+  float* o_s = l_s + kWarps * 16;                          // [warp][16][HD]
+  const int r_lo = lane >> 2;
+  if ((lane & 3) == 0) {
+    m_s[warp * 16 + r_lo] = m_lo;
+    l_s[warp * 16 + r_lo] = l_lo;
+    m_s[warp * 16 + r_lo + 8] = m_hi;
+    l_s[warp * 16 + r_lo + 8] = l_hi;
+  }
+#pragma unroll
+  for (int dt = 0; dt < 16; ++dt) {
+    const int d = dt * 8 + 2 * (lane & 3);
+    o_s[(warp * 16 + r_lo) * HD + d] = o[dt][0];
+    o_s[(warp * 16 + r_lo) * HD + d + 1] = o[dt][1];
+    o_s[(warp * 16 + r_lo + 8) * HD + d] = o[dt][2];
+    o_s[(warp * 16 + r_lo + 8) * HD + d + 1] = o[dt][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * HD; i += kThreads) {
     const int h = i / HD, d = i % HD;
-    float M = -1e30f;
+    float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m_s[w][h]);
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m_s[w * 16 + h]);
     float L = 0.f, A = 0.f;
+    if (M != -INFINITY) {
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float f = exp2f(m_s[w][h] - M);
-      L += l_s[w][h] * f;
-      A += acc_s[w][h][d] * f;
+      for (int w = 0; w < kWarps; ++w) {
+        const float f = exp2f(m_s[w * 16 + h] - M);
+        L += l_s[w * 16 + h] * f;
+        A += o_s[(w * 16 + h) * HD + d] * f;
+      }
     }
     const int head = kh * G + h;
     if (b.dec_splits == 1) {
-      out[(size_t)tok * nq * HD + (size_t)head * HD + d] = f2bf(L > 0.f ? A / L : 0.f);
+      if (ok) out[(size_t)tok * nq * HD + (size_t)head * HD + d] = f2bf(L > 0.f ? A / L : 0.f);
     } else {
       const size_t idx = ((size_t)split * b.n_dec + di) * nq + head;
       sc.dec_o[idx * HD + d] = A;
@@ -168,33 +284,38 @@ __global__ void decode_combine_kernel(AttnBatch b, AttnScratch sc, __nv_bfloat16
   pdl_trigger();
   const int di = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
   const int tok = b.q_start[b.dec_reqs[di]];
-  float M = -1e30f;
+  float M = -INFINITY;
   for (int s = 0; s < b.dec_splits; ++s) M = fmaxf(M, sc.dec_ml[(((size_t)s * b.n_dec + di) * nq + head) * 2]);
   float L = 0.f, A = 0.f;
-  for (int s = 0; s < b.dec_splits; ++s) {
-    const size_t idx = ((size_t)s * b.n_dec + di) * nq + head;
-    const float f = exp2f(sc.dec_ml[idx * 2] - M);
-    L += sc.dec_ml[idx * 2 + 1] * f;
-    A += sc.dec_o[idx * HD + d] * f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < b.dec_splits; ++s) {
+      const size_t idx = ((size_t)s * b.n_dec + di) * nq + head;
+      const float f = exp2f(sc.dec_ml[idx * 2] - M);
+      L += sc.dec_ml[idx * 2 + 1] * f;
+      A += sc.dec_o[idx * HD + d] * f;
+    }
   }
   out[(size_t)tok * nq * HD + (size_t)head * HD + d] = f2bf(L > 0.f ? A / L : 0.f);
 }
 
 }  // namespace dec
 
-void paged_decode_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
-                            const AttnBatch& b, const AttnScratch& sc, int nq, float scale, cudaStream_t s) {
+int decode_attention_block_keys() { return dec::BK; }
+
+void paged_decode_attention(const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out,
+                            const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int nq, float scale,
+                            cudaStream_t s) {
   if (b.n_dec <= 0) return;
-  const int G = nq / g.kvh;
-  dim3 grid(b.n_dec, g.kvh, b.dec_splits);
-  const float sl2 = scale * 1.4426950408889634f;
-  switch (G) {
-    case 1: launch_k(dec::decode_attn_kernel<1>, grid, dim3(dec::kWarps * 32), 0, s, q, q_stride, out, g, layer, b, sc, nq, sl2); break;
-    case 2: launch_k(dec::decode_attn_kernel<2>, grid, dim3(dec::kWarps * 32), 0, s, q, q_stride, out, g, layer, b, sc, nq, sl2); break;
-    case 4: launch_k(dec::decode_attn_kernel<4>, grid, dim3(dec::kWarps * 32), 0, s, q, q_stride, out, g, layer, b, sc, nq, sl2); break;
-    default: launch_k(dec::decode_attn_kernel<8>, grid, dim3(dec::kWarps * 32), 0, s, q, q_stride, out, g, layer, b, sc, nq, sl2); break;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(dec::decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
+    attr = true;
   }
-  if (b.dec_splits > 1) launch_k(dec::decode_combine_kernel, dim3(b.n_dec, nq), dim3(dec::HD), 0, s, b, sc, out, nq);
+  const float sl2 = scale * 1.4426950408889634f;
+  launch_k(dec::decode_attn_kernel, dim3(b.n_dec, g.kvh, b.dec_splits), dim3(dec::kThreads), dec::kSmemBytes, s, tmKV,
+           q, q_stride, out, g, layer, b, sc, nq, sl2);
+  if (b.dec_splits > 1)
+    launch_k(dec::decode_combine_kernel, dim3(b.n_dec, nq), dim3(dec::HD), 0, s, b, sc, out, nq);
 }
 
 }  // namespace kus

@@ -435,11 +435,11 @@ bool make_attn_q_map(CUtensorMap* map, const void* q, int tokens, int nq, int q_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size) {
+bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size, int max_rows) {
   auto fn = gemm_impl::get_encode_fn();
   const long long row_bytes = (long long)kvh * fatc::HD * 2;
-  const int box_rows = block_size < fatc::BN ? block_size : fatc::BN;
-  if (!fn || box_rows <= 0 || fatc::BN % box_rows) return false;
+  const int box_rows = block_size < max_rows ? block_size : max_rows;
+  if (!fn || box_rows <= 0 || max_rows % box_rows) return false;
   cuuint64_t dims[3] = {(cuuint64_t)fatc::HD, (cuuint64_t)kvh, (cuuint64_t)(bytes / row_bytes)};
   cuuint64_t strides[2] = {(cuuint64_t)fatc::HD * 2, (cuuint64_t)row_bytes};
   cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
@@ -453,13 +453,13 @@ void paged_prefill_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, __
                              int layer, const AttnBatch& b, const AttnScratch& sc, int T, int nq, float scale,
                              cudaStream_t s);
 
-void paged_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride,
-                     __nv_bfloat16* out, const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int T,
-                     int nq, float scale, cudaStream_t s) {
+void paged_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const CUtensorMap& tmKVdec,
+                     const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
+                     const AttnBatch& b, const AttnScratch& sc, int T, int nq, float scale, cudaStream_t s) {
   // prefill tiles (and their combine, which sweeps every token of the
   // step) first; the decode kernel then writes the decode tokens' rows
   if (b.n_items > 0) paged_prefill_attention(tmQ, tmKV, out, g, layer, b, sc, T, nq, scale, s);
-  paged_decode_attention(q, q_stride, out, g, layer, b, sc, nq, scale, s);
+  paged_decode_attention(tmKVdec, q, q_stride, out, g, layer, b, sc, nq, scale, s);
 }
 
 void paged_prefill_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, __nv_bfloat16* out, const KVGeom& g,

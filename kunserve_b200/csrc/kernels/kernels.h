@@ -105,18 +105,22 @@ struct AttnScratch {
 // out: [T, nq*hd] bf16.  Prefill tiles read Q and paged K/V through the
 // tensor maps of make_attn_q_map / make_attn_kv_map (attention_tc.cu);
 // decode requests read q directly (attention_decode.cu).
-void paged_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride,
-                     __nv_bfloat16* out, const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int T,
-                     int nq, float scale, cudaStream_t s);
+void paged_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const CUtensorMap& tmKVdec,
+                     const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
+                     const AttnBatch& b, const AttnScratch& sc, int T, int nq, float scale, cudaStream_t s);
 // 3-D map over q viewed as [tokens][nq heads][128 dims] (token stride q_stride elements).
 bool make_attn_q_map(CUtensorMap* map, const void* q, int tokens, int nq, int q_stride, int group);
-// 3-D map over a KV pool viewed as [rows][kvh][128 dims], one row per token slot.
-bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size);
+// 3-D map over a KV pool viewed as [rows][kvh][128 dims], one row per token
+// slot; boxes of min(block_size, max_rows) rows (128 for prefill tiles,
+// decode_attention_block_keys() for decode).
+bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size, int max_rows);
+int decode_attention_block_keys();
 int attention_q_rows_per_tile();
 // Decode requests of the batch only (attention_decode.cu); paged_attention
-// calls it after the prefill items.
-void paged_decode_attention(const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out, const KVGeom& g, int layer,
-                            const AttnBatch& b, const AttnScratch& sc, int nq, float scale, cudaStream_t s);
+// calls it after the prefill tiles.
+void paged_decode_attention(const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out,
+                            const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int nq, float scale,
+                            cudaStream_t s);
 
 }  // namespace kus
 
