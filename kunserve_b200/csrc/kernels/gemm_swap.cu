@@ -30,48 +30,99 @@ struct SCfg {
   static constexpr int kStageBytes = kWBytes + kXBytes;
   static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
   static constexpr int kTmemCols = (4 * BNT) < 32 ? 32 : 4 * BNT;   // 2 halves x 2 buffers
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kEpiBytes = 16 * kWRows * 4;                  // 16 tokens x 256 features fp32
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + 256;
 };
 
 KUS_DEVICE float silu_s(float x) { return x / (1.0f + __expf(-x)); }
 
-// v[i] = D^T[f, tok0 + i]; store C[tok0 + i, f] for the 16 tokens.  A warp
-// holds 32 consecutive features, so each token's stores (and residual
-// loads) are 64-byte coalesced; the loads are predicated rather than broken
-// out of, so all 16 are in flight at once.
+// Epilogue of 16 tokens (tok0..tok0+15) of weight tile n.  Each thread
+// holds feature r of both 128-row halves (v0, v1); the tile goes through a
+// shared-memory transpose E[16][256] so that every warp then writes whole
+// token rows: 16-byte residual loads and stores, 512 contiguous bytes per
+// token (256 for SiLU, whose tile yields 128 features).
 template <int EPI>
-KUS_DEVICE void store_col16(const GemmArgs& a, int f, int tok0, const float (&v)[16]) {
-  if (f >= a.n_out) return;
-  if (EPI == EPI_F32) {
+KUS_DEVICE void emit16(const GemmArgs& a, float* E, int n, int tok0, int r, int we, int lane, const float (&v0)[16],
+                       const float (&v1)[16]) {
+  constexpr int W = EPI == EPI_SILU ? 128 : 256;   // output features of the tile
+  constexpr int PL = W / 32;                       // per lane: 8 or 4
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      if (tok0 + i < a.M) reinterpret_cast<float*>(a.out)[(size_t)(tok0 + i) * a.ldc + f] = v[i];
-    return;
-  }
-  float x[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) x[i] = v[i];
-  if (EPI == EPI_ADD) {
-    __nv_bfloat16 r[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      r[i] = (tok0 + i < a.M) ? a.residual[(size_t)(tok0 + i) * a.ld_res + f] : __float2bfloat16(0.f);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) x[i] += bf2f(r[i]);
-  }
-  if (EPI == EPI_PUSH) {
-    for (int p = 0; p < a.npeers; ++p) {
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]);
-#pragma unroll
-      for (int i = 0; i < 16; ++i)
-        if (tok0 + i < a.M) dst[(size_t)(tok0 + i) * a.ldc + f] = f2bf(x[i]);
+  for (int i = 0; i < 16; ++i) {
+    if (EPI == EPI_SILU) {
+      E[i * 256 + r] = silu_s(v0[i]) * v1[i];
+    } else {
+      E[i * 256 + r] = v0[i];
+      E[i * 256 + 128 + r] = v1[i];
     }
-    return;
   }
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  named_barrier(2, 128);
+  const int f0 = n * W + lane * PL;
+  const bool full = f0 + PL <= a.n_out;
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    if (tok0 + i < a.M) out[(size_t)(tok0 + i) * a.ldc + f] = f2bf(x[i]);
+  for (int j = 0; j < 4; ++j) {
+    const int t = we * 4 + j;
+    const int tok = tok0 + t;
+    if (tok >= a.M || f0 >= a.n_out) continue;
+    float x[PL];
+#pragma unroll
+    for (int e = 0; e < PL; e += 4) {
+      const float4 q4 = *reinterpret_cast<const float4*>(&E[t * 256 + lane * PL + e]);
+      x[e] = q4.x;
+      x[e + 1] = q4.y;
+      x[e + 2] = q4.z;
+      x[e + 3] = q4.w;
+    }
+    if (EPI == EPI_F32) {
+      float* dst = reinterpret_cast<float*>(a.out) + (size_t)tok * a.ldc + f0;
+      if (full) {
+#pragma unroll
+        for (int e = 0; e < PL; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+      } else {
+        for (int e = 0; e < PL && f0 + e < a.n_out; ++e) dst[e] = x[e];
+      }
+      continue;
+    }
+    if (EPI == EPI_ADD) {
+      const __nv_bfloat16* res = a.residual + (size_t)tok * a.ld_res + f0;
+      if (full) {
+        float rv[8];
+        unpack_bf16x8(*reinterpret_cast<const uint4*>(res), rv);
+#pragma unroll
+        for (int e = 0; e < PL; ++e) x[e] += rv[e];
+      } else {
+        for (int e = 0; e < PL && f0 + e < a.n_out; ++e) x[e] += bf2f(res[e]);
+      }
+    }
+    if (full) {
+      if (PL == 8) {
+        float lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lo[e] = x[e % PL];
+        const uint4 u = pack_bf16x8(lo);
+        if (EPI == EPI_PUSH) {
+          for (int p = 0; p < a.npeers; ++p)
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]) + (size_t)tok * a.ldc + f0) = u;
+        } else {
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)tok * a.ldc + f0) = u;
+        }
+      } else {
+        uint2 u;
+        u.x = pack_bf16x2(x[0], x[1 % PL]);
+        u.y = pack_bf16x2(x[2 % PL], x[3 % PL]);
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)tok * a.ldc + f0) = u;
+      }
+    } else {
+      for (int e = 0; e < PL && f0 + e < a.n_out; ++e) {
+        if (EPI == EPI_PUSH) {
+          for (int p = 0; p < a.npeers; ++p)
+            reinterpret_cast<__nv_bfloat16*>(a.peer_out[p])[(size_t)tok * a.ldc + f0 + e] = f2bf(x[e]);
+        } else {
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)tok * a.ldc + f0 + e] = f2bf(x[e]);
+        }
+      }
+    }
+  }
+  named_barrier(2, 128);   // E is rewritten by the next chunk
 }
 
 template <int BNT, int EPI>
@@ -83,7 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_w = smem;
   uint8_t* smem_x = smem + C::kStages * C::kWBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  float* epi = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes + C::kEpiBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* tfull = empty + C::kStages;
   uint64_t* tempty = tfull + 2;
@@ -227,15 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v0[16], v1[16];
             tmem_ld16(t0 + c, v0);
             tmem_ld16(t0 + BNT + c, v1);
-            if (EPI == EPI_SILU) {
-              float o[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) o[i] = silu_s(v0[i]) * v1[i];
-              store_col16<EPI_BF16>(args, n * 128 + r, c, o);
-            } else {
-              store_col16<EPI>(args, n * kWRows + r, c, v0);
-              store_col16<EPI>(args, n * kWRows + 128 + r, c, v1);
-            }
+            emit16<EPI>(args, epi, n, c, r, warp - 2, lane, v0, v1);
           }
         }
         tc_fence_before();
@@ -262,15 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             float v0[16], v1[16];
             take16(w0 + c, v0);
             take16(w1 + c, v1);
-            if (EPI == EPI_SILU) {
-              float o[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) o[i] = silu_s(v0[i]) * v1[i];
-              store_col16<EPI_BF16>(args, n * 128 + r, c, o);
-            } else {
-              store_col16<EPI>(args, n * kWRows + r, c, v0);
-              store_col16<EPI>(args, n * kWRows + 128 + r, c, v1);
-            }
+            emit16<EPI>(args, epi, n, c, r, warp - 2, lane, v0, v1);
           }
         }
       }

@@ -458,9 +458,11 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
   const int sms = num_sms();
   const int tiles = m_tiles * n_tiles;
   int dp = tiles, sk = 0, grid = tiles < sms ? tiles : sms;
-  // stream-K only for the memory-bound swapped kernel: for compute-bound
-  // tiles the fp32 reductions cost more than the partial last wave
-  if (stream_k && p.swap && tiles % sms != 0) {
+  // Stream-K only for the memory-bound swapped kernel, and only where the
+  // whole-tile grid would leave most SMs idle: its fp32 reductions grow with
+  // the token tile, and measured on B200 whole tiles win from 17 tokens up
+  // unless fewer than 20 tiles exist (N = 4096: o_proj, down_proj).
+  if (stream_k && p.swap && tiles % sms != 0 && (M <= 16 || tiles < 20)) {
     // whole waves stay data-parallel; the last partial wave plus one full
     // wave is spread evenly over every SM along K
     const int waves = tiles / sms;

@@ -39,7 +39,7 @@ def test_gemm_stream_k_workspace_returns_to_zero(C):
     """Tiles split along K (decode-sized GEMMs) leave the shared accumulators
     zero, so a second (different) problem on the same workspace is exact too."""
     torch.manual_seed(3)
-    for M, N, K in ((64, 6144, 4096), (1, 4096, 14336), (16, 4096, 4096), (100, 28672, 4096)):
+    for M, N, K in ((64, 4096, 4096), (1, 4096, 14336), (16, 4096, 4096), (100, 4096, 14336), (8, 28672, 4096)):
         outs = []
         for rep in range(2):
             A = torch.randn(M, K, device="cuda").bfloat16()
