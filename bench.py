@@ -137,7 +137,7 @@ async def timed_engine_run(inst, trace, steps, t_window_start_cb, sync, sp_facto
 
     def on_out(outs):
         for o in outs:
-            finished[o.request_id] = (o.arrival_time, [t.new_token_time for t in o.outputs])
+            finished[o.request_id] = (o.arrival_time, [t.new_token_time for t in o.outputs], True)
 
     inst.output_callback = on_out
     inst.step_log = []
@@ -164,21 +164,39 @@ async def timed_engine_run(inst, trace, steps, t_window_start_cb, sync, sp_facto
     feeder.cancel()
     inst.terminate()
     await asyncio.wait_for(loop_task, 30)
-    return finished, end_wall, t0
+    return list(finished.values()) + in_flight(inst), end_wall, t0
+
+
+def in_flight(inst):
+    """(arrival, token times, finished=False) of every request still in the
+    instance (queued or running) when the window closes."""
+    reqs = list(inst.unaccepted_queue) + [r for s in inst.scheduler for r in s.all_requests()]
+    return [(r.arrival_time, [o.new_token_time for o in r.outputs], False) for r in reqs]
 
 
 def summarize(records, t_end, slo_ttft, slo_tpot):
+    """SLO accounting at the end of the window.  A request that arrived in
+    the window counts as good when it finished inside it within both
+    objectives, or is still on track at the window's end: first token within
+    the TTFT objective and mean inter-token time so far within the TPOT
+    objective, or no token yet but younger than the TTFT objective.  Counting
+    on-track requests keeps the goodput a rate of the offered load that does
+    not depend on how many requests happen to straddle the window's end."""
     ttft, tpot, ok = [], [], 0
-    for arrival, times in records:
-        if not times or times[-1] > t_end:
+    for arrival, times, finished in records:
+        if arrival > t_end:
             continue
-        a = times[0] - arrival
-        b = (times[-1] - times[0]) / (len(times) - 1) if len(times) > 1 else 0.0
-        ttft.append(a)
-        if len(times) > 1:
-            tpot.append(b)
-        if a <= slo_ttft and b <= slo_tpot:
-            ok += 1
+        times = [t for t in times if t <= t_end]
+        if times:
+            a = times[0] - arrival
+            b = (times[-1] - times[0]) / (len(times) - 1) if len(times) > 1 else 0.0
+            ttft.append(a)
+            if len(times) > 1:
+                tpot.append(b)
+            good = a <= slo_ttft and b <= slo_tpot
+        else:
+            good = not finished and t_end - arrival <= slo_ttft
+        ok += int(good)
     return ttft, tpot, ok
 
 
@@ -276,7 +294,7 @@ def main():
         ev1.record(torch.cuda.current_stream(dev))
         torch.cuda.synchronize(dev)
 
-    finished, t_end, t0 = asyncio.run(timed_engine_run(inst, trace, args.steps, window_start, window_end, sp))
+    records, t_end, t0 = asyncio.run(timed_engine_run(inst, trace, args.steps, window_start, window_end, sp))
     clock_info = clocks.stop() if rank == 0 else None
     dev_ms = ev0.elapsed_time(ev1)
     barrier_sync()
@@ -285,10 +303,11 @@ def main():
     h2d = (runner.h2d_bytes - h2d0) / max(n_steps, 1)
     d2h = (runner.d2h_bytes - d2h0) / max(n_steps, 1)
     check_error()
-    ttft, tpot, ok = summarize(finished.values(), t0 + dev_ms / 1000.0, args.ttft_slo, args.tpot_slo)
+    ttft, tpot, ok = summarize(records, t0 + dev_ms / 1000.0, args.ttft_slo, args.tpot_slo)
     preempt = inst.get_num_preemption()
     local_res = {"dev_ms": dev_ms, "ttft": ttft, "tpot": tpot, "ok": ok, "launches": launches,
-                 "h2d": h2d, "d2h": d2h, "n_steps": n_steps, "finished": len(ttft), "preempt": preempt,
+                 "h2d": h2d, "d2h": d2h, "n_steps": n_steps, "preempt": preempt,
+                 "finished": sum(1 for a, tt, fin in records if fin and tt and tt[-1] <= t0 + dev_ms / 1000.0),
                  "arrived": sum(1 for r in trace if r.arrival <= dev_ms / 1000.0)}
     inst.reset()
 
@@ -329,8 +348,8 @@ def main():
             llm.coordinator.stop()
             inst.terminate()
             await asyncio.sleep(0.05)
-            recs = [(t_start + trace[r["request_id"]].arrival, r["metrics"].token_times) for r in results]
-            return recs, t_stop - t_start, t_start
+            recs = [(t_start + trace[r["request_id"]].arrival, r["metrics"].token_times, True) for r in results]
+            return recs + in_flight(inst), t_stop - t_start, t_start
         recs, wall, ts = asyncio.run(e2e())
         e_ttft, e_tpot, e_ok = summarize(recs, ts + wall, args.ttft_slo, args.tpot_slo)
         e2e_res = {"wall_s": wall, "ok": e_ok, "ttft": e_ttft, "tpot": e_tpot}
