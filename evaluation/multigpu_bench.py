@@ -3,6 +3,12 @@
 * fused tensor-parallel GEMM + all-reduce (push epilogue over NVLink +
   reduce) against cuBLAS GEMM + NCCL all-reduce, for the row-parallel
   projections (o_proj: K = H/tp; down_proj: K = F/tp) at M tokens;
+* fused GEMM + reduce-scatter (each output row block pushed only to its
+  owner) against cuBLAS GEMM + NCCL reduce-scatter, same shapes;
+* fused all-gather + GEMM (the A shards of every rank read by TMA inside the
+  GEMM from the owning GPU) against NCCL all-gather + cuBLAS GEMM, for the
+  column-parallel projections (qkv: N = (H + 2 kv)/tp ~ H/tp here; gate/up:
+  N = 2F/tp) with K = H;
 * paged KV-block migration (blocks of 16 tokens x 8 KV heads x 128 dim, K and
   V) and parameter restore (contiguous bytes) pulled by the copy kernel from
   a peer's mapped memory, against NCCL send/recv of the same bytes.
@@ -115,6 +121,116 @@ def bench_tp(args, C, dev, rank, world):
             del keep
 
 
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / (b.norm() + 1e-6))
+
+
+def bench_rs(args, C, dev, rank, world):
+    peak, src = peak_flops()
+    for H in args.hidden:
+        for kind, K_full in (("o_proj", H), ("down_proj", args.ffn.get(H, 4 * H))):
+            K = K_full // world
+            max_m = max(args.tokens)
+            bases, keep = share(C, dev, 4096 + 2 * world * max_m * H * 2, rank, world)
+            W = (torch.randn(H, K, device=dev) * 0.02).bfloat16()
+            ws = torch.zeros(2 * 148 * 128 * 256, device=dev)
+            counters = torch.zeros(1 << 16, device=dev, dtype=torch.int32)
+            epoch = [0]
+            for M in args.tokens:
+                Mp = (M + world - 1) // world * world
+                A = torch.randn(M, K, device=dev).bfloat16()
+                h = torch.zeros(M, H, device=dev, dtype=torch.bfloat16)
+
+                def fused():
+                    epoch[0] += 1
+                    C.tp_gemm_reduce_scatter(A, W, h, bases, rank, max_m, epoch[0], counters, ws)
+
+                Ap = torch.zeros(Mp, K, device=dev).bfloat16()
+                Ap[:M] = A
+                shard = torch.empty(Mp // world, H, device=dev, dtype=torch.bfloat16)
+
+                def baseline():
+                    out = torch.matmul(Ap, W.t())
+                    dist.reduce_scatter_tensor(shard, out)
+
+                if args.check:
+                    h.zero_()
+                    fused()
+                    torch.cuda.synchronize(dev)
+                    full = torch.matmul(A.float(), W.float().t())
+                    dist.all_reduce(full)
+                    Mr = (M + world - 1) // world
+                    lo, hi = rank * Mr, min(M, (rank + 1) * Mr)
+                    err = rel_err(h[lo:hi], full[lo:hi]) if hi > lo else 0.0
+                    assert err < 2e-2, (kind, M, err)
+                tf = time_ms(fused, args.warmup, args.iters, dev)
+                tb = time_ms(baseline, args.warmup, args.iters, dev)
+                flops = 2.0 * M * H * K
+                link_bytes = (world - 1) / world * M * H * 2
+                roof = max(flops / peak, link_bytes / LINK) * 1e3
+                if rank == 0:
+                    print(json.dumps({"kernel": f"fused_gemm_reduce_scatter_{kind}", "tp": world, "M": M, "H": H,
+                                      "K": K, "fused_us": round(tf * 1e3, 2), "cublas_nccl_us": round(tb * 1e3, 2),
+                                      "speedup": round(tb / tf, 3), "roofline_us": round(roof * 1e3, 2),
+                                      "roofline_frac": round(roof / tf, 3), "peaks": src,
+                                      "checked": bool(args.check)}), flush=True)
+            del keep
+
+
+def bench_ag(args, C, dev, rank, world):
+    peak, src = peak_flops()
+    for H in args.hidden:
+        for kind, N_full in (("qkv", H), ("gate_up", 2 * args.ffn.get(H, 4 * H))):
+            N = N_full // world
+            W = (torch.randn(N, H, device=dev) * 0.02).bfloat16()
+            maps = torch.empty(128 * world, device=dev, dtype=torch.uint8)
+            for M in args.tokens:
+                rows = M // world
+                if rows < 128 or rows % 128:
+                    continue     # shards of whole 128-row tiles only
+                bases, keep = share(C, dev, 4096 + rows * H * 2, rank, world)
+                local = (torch.randn(rows, H, device=dev) * 1.0).bfloat16()
+                C.copy_chunks(bases[rank] + 4096, local.data_ptr(),
+                              torch.zeros(1, device=dev, dtype=torch.int64), torch.zeros(1, device=dev, dtype=torch.int64),
+                              rows * H * 2, 148)
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                epoch = [0]
+
+                def fused():
+                    epoch[0] += 1
+                    C.tp_signal(bases, rank, epoch[0])
+                    C.tp_allgather_gemm(W, out, bases, rank, rows, H, epoch[0], maps)
+
+                gathered = torch.empty(M, H, device=dev, dtype=torch.bfloat16)
+
+                def baseline():
+                    dist.all_gather_into_tensor(gathered, local)
+                    torch.matmul(gathered, W.t())
+
+                if args.check:
+                    fused()
+                    torch.cuda.synchronize(dev)
+                    dist.all_gather_into_tensor(gathered, local)
+                    err = rel_err(out, gathered.float() @ W.float().t())
+                    assert err < 2e-2, (kind, M, err)
+                tf = time_ms(fused, args.warmup, args.iters, dev)
+                tb = time_ms(baseline, args.warmup, args.iters, dev)
+                flops = 2.0 * M * N * H
+                link_bytes = (world - 1) / world * M * H * 2
+                roof = max(flops / peak, link_bytes / LINK) * 1e3
+                if rank == 0:
+                    print(json.dumps({"kernel": f"fused_allgather_gemm_{kind}", "tp": world, "M": M, "H": H,
+                                      "N": N, "fused_us": round(tf * 1e3, 2), "nccl_cublas_us": round(tb * 1e3, 2),
+                                      "speedup": round(tb / tf, 3), "roofline_us": round(roof * 1e3, 2),
+                                      "roofline_frac": round(roof / tf, 3), "peaks": src,
+                                      "checked": bool(args.check)}), flush=True)
+                dist.barrier()
+                del keep
+
+
 def bench_copy(args, C, dev, rank, world):
     block = 16 * 8 * 128 * 2 * 2            # K and V of one layer
     for nblocks in args.blocks:
@@ -149,7 +265,8 @@ def bench_copy(args, C, dev, rank, world):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("--what", choices=["tp", "copy", "all"], default="all")
+    p.add_argument("--what", nargs="+", choices=["tp", "rs", "ag", "copy", "all"], default=["all"])
+    p.add_argument("--check", action="store_true", help="compare the fused results with PyTorch first")
     p.add_argument("--tokens", type=int, nargs="+", default=[1, 16, 256, 4096])
     p.add_argument("--hidden", type=int, nargs="+", default=[4096, 5120, 8192])
     p.add_argument("--blocks", type=int, nargs="+", default=[1024, 16384, 65536])
@@ -165,9 +282,14 @@ def main():
     from kunserve_b200.ops import check_error, native
     C = native()
     try:
-        if a.what in ("tp", "all"):
+        want = set(a.what)
+        if want & {"tp", "all"}:
             bench_tp(a, C, local, rank, world)
-        if a.what in ("copy", "all"):
+        if want & {"rs", "all"}:
+            bench_rs(a, C, local, rank, world)
+        if want & {"ag", "all"}:
+            bench_ag(a, C, local, rank, world)
+        if want & {"copy", "all"}:
             bench_copy(a, C, local, rank, world)
         check_error()
     finally:

@@ -189,6 +189,82 @@ void tp_gemm_allreduce_op(torch::Tensor A, torch::Tensor B, torch::Tensor h, c10
                     reinterpret_cast<const unsigned*>(base), (unsigned)epoch, st);
 }
 
+// Fused tensor-parallel GEMM + reduce-scatter: rows [r*Mr, (r+1)*Mr) of
+// A @ B^T (Mr = ceil(M / R)) are pushed only to rank r's receive slot for
+// this sender; this rank then reduces its own row block into h.
+void tp_gemm_reduce_scatter_op(torch::Tensor A, torch::Tensor B, torch::Tensor h, std::vector<int64_t> bases,
+                               int64_t rank, int64_t max_tokens, int64_t epoch, torch::Tensor counters,
+                               torch::Tensor ws) {
+  CHECK_CUDA_BF16(A);
+  CHECK_CUDA_BF16(B);
+  c10::cuda::CUDAGuard g(A.device());
+  const int M = A.size(0), K = A.size(1), N = B.size(0), R = (int)bases.size();
+  TORCH_CHECK(R <= kMaxTpPeers && M <= max_tokens, "tp_gemm_reduce_scatter sizes");
+  const int Mr = (M + R - 1) / R;
+  GemmPlan p = plan_gemm(M, N, K, EPI_PUSH, 256, true);
+  TORCH_CHECK(plan_workspace_floats(p) <= (size_t)ws.numel() && plan_counters(p) < counters.numel() - 1,
+              "ws (zero-filled fp32) too small");
+  const int64_t slot = max_tokens * N * 2, flags = 4096;
+  const int64_t data = flags + (epoch & 1) * R * slot + rank * slot;
+  for (int q = 0; q < R; ++q) {
+    p.args.peer_out[q] = reinterpret_cast<void*>(bases[q] + data);
+    p.args.flag_remote[q] = reinterpret_cast<unsigned*>(bases[q] + 4 * rank);
+  }
+  p.args.npeers = R;
+  p.args.rs_rows = Mr;
+  p.args.epoch = (unsigned)epoch;
+  p.args.done_counter = counters.data_ptr<int>() + (counters.numel() - 1);
+  TORCH_CHECK(finalize_plan(p, A.data_ptr(), K, B.data_ptr(), K, nullptr, N, nullptr, N, ws.data_ptr<float>(),
+                            counters.data_ptr<int>()),
+              "tensor map encoding failed");
+  auto st = at::cuda::getCurrentCUDAStream();
+  run_gemm(p, st);
+  const char* base = reinterpret_cast<const char*>(bases[rank]);
+  const int row0 = (int)rank * Mr, rows = std::max(0, std::min(M, row0 + Mr) - row0);
+  tp_reduce_rmsnorm(reinterpret_cast<const __nv_bfloat16*>(base + flags + (epoch & 1) * R * slot), R,
+                    max_tokens * N, bp(h), nullptr, bp(h), rows, N, 1e-5f, reinterpret_cast<const unsigned*>(base),
+                    (unsigned)epoch, st, row0);
+}
+
+// Publish this rank's A shard: write `epoch` to flag slot `rank` of every
+// rank's buffer (bases[q] + 4 * rank).
+void tp_signal_op(std::vector<int64_t> bases, int64_t rank, int64_t epoch) {
+  FlagList f{};
+  f.n = (int)bases.size();
+  TORCH_CHECK(f.n <= 8, "at most 8 ranks");
+  for (int q = 0; q < f.n; ++q) f.ptr[q] = reinterpret_cast<unsigned*>(bases[q] + 4 * rank);
+  signal_flags(f, (unsigned)epoch, at::cuda::getCurrentCUDAStream());
+}
+
+// Fused all-gather + GEMM: out[M, N] = A_all @ B^T with A_all the row
+// concatenation of every rank's shard (rows_per_rank x K at bases[q] + 4096),
+// read by TMA from the owning GPU inside the GEMM once its flag (slot q of
+// this rank's buffer) reaches `epoch`.  maps: uint8 CUDA tensor, >= 128 * R bytes.
+void tp_allgather_gemm_op(torch::Tensor B, torch::Tensor out, std::vector<int64_t> bases, int64_t rank,
+                          int64_t rows_per_rank, int64_t K, int64_t epoch, torch::Tensor maps) {
+  CHECK_CUDA_BF16(B);
+  c10::cuda::CUDAGuard g(B.device());
+  const int R = (int)bases.size(), N = B.size(0), M = R * (int)rows_per_rank;
+  TORCH_CHECK(R <= kMaxTpPeers && rows_per_rank % 128 == 0 && M > 128, "tp_allgather_gemm: shards of 128-row tiles");
+  TORCH_CHECK(maps.is_cuda() && maps.numel() >= 128 * R, "maps buffer");
+  GemmPlan p = plan_gemm(M, N, (int)K, EPI_BF16, 0, false);
+  TORCH_CHECK(!p.swap, "all-gather GEMM needs the 128-row kernel");
+  std::vector<CUtensorMap> host(R);
+  for (int q = 0; q < R; ++q)
+    TORCH_CHECK(make_tmap_bf16(&host[q], reinterpret_cast<const void*>(bases[q] + 4096), rows_per_rank, K, K, 128),
+                "shard tensor map");
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaMemcpyAsync(maps.data_ptr(), host.data(), sizeof(CUtensorMap) * R, cudaMemcpyHostToDevice, st);
+  TORCH_CHECK(finalize_plan(p, reinterpret_cast<const void*>(bases[rank] + 4096), (int)K, B.data_ptr(), (int)K,
+                            out.data_ptr(), N, nullptr, N, nullptr, nullptr, (uint64_t)rows_per_rank, 0),
+              "tensor map encoding failed");
+  p.args.ag_maps = reinterpret_cast<const CUtensorMap*>(maps.data_ptr());
+  p.args.ag_rows = (int)rows_per_rank;
+  p.args.ag_flags = reinterpret_cast<const unsigned*>(bases[rank]);
+  p.args.ag_epoch = (unsigned)epoch;
+  run_gemm(p, st);
+}
+
 void fill_normal_op(torch::Tensor t, int64_t seed, double std) {
   CHECK_CUDA_BF16(t);
   c10::cuda::CUDAGuard g(t.device());
@@ -272,6 +348,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nccl_unique_id", &nccl_unique_id);
   m.def("error_flag", &read_error_flag, py::arg("reset") = true);
   m.def("attention_q_rows_per_tile", &attention_q_rows_per_tile);
+  m.def("tp_gemm_reduce_scatter", &tp_gemm_reduce_scatter_op);
+  m.def("tp_allgather_gemm", &tp_allgather_gemm_op);
+  m.def("tp_signal", &tp_signal_op);
   m.def("num_sms", &num_sms);
   m.attr("EPI_BF16") = (int)EPI_BF16;
   m.attr("EPI_F32") = (int)EPI_F32;

@@ -266,12 +266,12 @@ void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off,
 __global__ void tp_reduce_rmsnorm_kernel(const __nv_bfloat16* __restrict__ rb, int R, long long slot_elems,
                                          __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ w,
                                          __nv_bfloat16* __restrict__ y, int H, float eps,
-                                         const unsigned* __restrict__ flags, unsigned epoch) {
+                                         const unsigned* __restrict__ flags, unsigned epoch, int row0) {
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
   __shared__ int ok_s;
-  const int row = blockIdx.x;
+  const int row = row0 + blockIdx.x;
   if (threadIdx.x == 0) {
     int ok = 1;
     const unsigned long long t0 = global_ns();
@@ -333,10 +333,25 @@ __global__ void tp_reduce_rmsnorm_kernel(const __nv_bfloat16* __restrict__ rb, i
 
 void tp_reduce_rmsnorm(const __nv_bfloat16* rb, int R, long long slot_elems, __nv_bfloat16* h,
                        const __nv_bfloat16* w, __nv_bfloat16* y, int T, int H, float eps, const unsigned* flags,
-                       unsigned epoch, cudaStream_t s) {
+                       unsigned epoch, cudaStream_t s, int row0) {
   if (T <= 0) return;
-  launch_k(tp_reduce_rmsnorm_kernel, dim3(T), dim3(256), 0, s, rb, R, slot_elems, h, w, y, H, eps, flags, epoch);
+  launch_k(tp_reduce_rmsnorm_kernel, dim3(T), dim3(256), 0, s, rb, R, slot_elems, h, w, y, H, eps, flags, epoch,
+           row0);
 }
+
+// Publish `epoch` to every listed flag (peer memory included) once this
+// GPU's earlier work is visible system-wide.
+__global__ void signal_flags_kernel(FlagList f, unsigned epoch) {
+  pdl_wait();
+  __threadfence_system();
+  for (int i = 0; i < f.n; ++i)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f.ptr[i]), "r"(epoch) : "memory");
+}
+
+void signal_flags(const FlagList& f, unsigned epoch, cudaStream_t s) {
+  launch_k(signal_flags_kernel, dim3(1), dim3(1), 0, s, f, epoch);
+}
+
 
 // -------------------------------------------------- residual add (TP path)
 __global__ void add_inplace_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y, long long n8) {

@@ -35,6 +35,19 @@ struct GemmArgs {
   int npeers;
   unsigned epoch;
   int* done_counter;    // CTA completion count, zero between GEMMs
+  // EPI_PUSH as reduce-scatter: with rs_rows > 0, output row r goes only to
+  // rank r / rs_rows (the owner of that row block), not to every rank.
+  int rs_rows;
+  // All-gather fused into the A operand (regular kernel): with ag_rows > 0,
+  // rows [q*ag_rows, (q+1)*ag_rows) of A are read by TMA straight from rank
+  // q's memory through ag_maps[q] (tensor maps in global memory, 128-row
+  // boxes, no multicast); ag_rows is a multiple of 128.
+  const CUtensorMap* ag_maps;
+  int ag_rows;
+  // optional readiness flags of the A shards: ag_flags[q] >= ag_epoch once
+  // rank q's rows are written (bounded wait by the producer before any load)
+  const unsigned* ag_flags;
+  unsigned ag_epoch;
 };
 
 struct GemmPlan {

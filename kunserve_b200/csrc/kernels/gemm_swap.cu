@@ -100,7 +100,10 @@ KUS_DEVICE void emit16(const GemmArgs& a, float* E, int n, int tok0, int r, int 
         for (int e = 0; e < 8; ++e) lo[e] = x[e % PL];
         const uint4 u = pack_bf16x8(lo);
         if (EPI == EPI_PUSH) {
-          for (int p = 0; p < a.npeers; ++p)
+          // all-reduce: every rank; reduce-scatter: the owner of this token only
+          const int p0 = a.rs_rows > 0 ? tok / a.rs_rows : 0;
+          const int p1 = a.rs_rows > 0 ? p0 + 1 : a.npeers;
+          for (int p = p0; p < p1; ++p)
             *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]) + (size_t)tok * a.ldc + f0) = u;
         } else {
           *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)tok * a.ldc + f0) = u;
@@ -114,7 +117,9 @@ KUS_DEVICE void emit16(const GemmArgs& a, float* E, int n, int tok0, int r, int 
     } else {
       for (int e = 0; e < PL && f0 + e < a.n_out; ++e) {
         if (EPI == EPI_PUSH) {
-          for (int p = 0; p < a.npeers; ++p)
+          const int p0 = a.rs_rows > 0 ? tok / a.rs_rows : 0;
+          const int p1 = a.rs_rows > 0 ? p0 + 1 : a.npeers;
+          for (int p = p0; p < p1; ++p)
             reinterpret_cast<__nv_bfloat16*>(a.peer_out[p])[(size_t)tok * a.ldc + f0 + e] = f2bf(x[e]);
         } else {
           reinterpret_cast<__nv_bfloat16*>(a.out)[(size_t)tok * a.ldc + f0 + e] = f2bf(x[e]);

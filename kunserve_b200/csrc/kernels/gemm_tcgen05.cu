@@ -41,7 +41,9 @@ struct Cfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kEpiStride = 65;                         // floats per staged row (64 + pad)
+  static constexpr int kEpiBytes = BM * kEpiStride * 4;         // epilogue transpose buffer
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + 256;
 };
 
 KUS_DEVICE float silu(float x) { return x / (1.0f + __expf(-x)); }
@@ -69,7 +71,10 @@ KUS_DEVICE void store16(const GemmArgs& a, int row, int col, const float (&v)[16
       hi[i] = v[8 + i];
     }
     const uint4 u0 = pack_bf16x8(lo), u1 = pack_bf16x8(hi);
-    for (int p = 0; p < a.npeers; ++p) {
+    // all-reduce: every rank; reduce-scatter: the owner of this row only
+    const int p0 = a.rs_rows > 0 ? row / a.rs_rows : 0;
+    const int p1 = a.rs_rows > 0 ? p0 + 1 : a.npeers;
+    for (int p = p0; p < p1; ++p) {
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]) + (size_t)row * a.ldc + col;
       if (col + 16 <= a.n_out) {
         *reinterpret_cast<uint4*>(dst) = u0;
@@ -114,6 +119,55 @@ KUS_DEVICE void store16(const GemmArgs& a, int row, int col, const float (&v)[16
   }
 }
 
+// Eight consecutive output columns (col..col+7) of one row, staged in
+// shared memory by the tile epilogue; 16-byte loads and stores.
+template <int EPI>
+KUS_DEVICE void out8(const GemmArgs& a, int row, int col, float (&x)[8]) {
+  const bool full = col + 8 <= a.n_out;
+  if (EPI == EPI_F32) {
+    float* dst = reinterpret_cast<float*>(a.out) + (size_t)row * a.ldc + col;
+    if (full) {
+      *reinterpret_cast<float4*>(dst) = make_float4(x[0], x[1], x[2], x[3]);
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(x[4], x[5], x[6], x[7]);
+    } else {
+      for (int e = 0; e < 8 && col + e < a.n_out; ++e) dst[e] = x[e];
+    }
+    return;
+  }
+  if (EPI == EPI_ADD) {
+    const __nv_bfloat16* res = a.residual + (size_t)row * a.ld_res + col;
+    if (full) {
+      float rv[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(res), rv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] += rv[e];
+    } else {
+      for (int e = 0; e < 8 && col + e < a.n_out; ++e) x[e] += bf2f(res[e]);
+    }
+  }
+  const uint4 u = pack_bf16x8(x);
+  if (EPI == EPI_PUSH) {
+    // all-reduce: every rank; reduce-scatter: the owner of this row only
+    const int p0 = a.rs_rows > 0 ? row / a.rs_rows : 0;
+    const int p1 = a.rs_rows > 0 ? p0 + 1 : a.npeers;
+    for (int p = p0; p < p1; ++p) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_out[p]) + (size_t)row * a.ldc + col;
+      if (full) {
+        *reinterpret_cast<uint4*>(dst) = u;
+      } else {
+        for (int e = 0; e < 8 && col + e < a.n_out; ++e) dst[e] = f2bf(x[e]);
+      }
+    }
+    return;
+  }
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + (size_t)row * a.ldc + col;
+  if (full) {
+    *reinterpret_cast<uint4*>(dst) = u;
+  } else {
+    for (int e = 0; e < 8 && col + e < a.n_out; ++e) dst[e] = f2bf(x[e]);
+  }
+}
+
 }  // namespace gemm_impl
 
 // Every epilogue thread of a CTA calls this once its pushes are issued: the
@@ -143,7 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + C::kStages * C::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+  float* epi = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes + C::kEpiBytes);
   uint64_t* empty = full + C::kStages;
   uint64_t* tfull = empty + C::kStages;
   uint64_t* tempty = tfull + 2;
@@ -184,9 +239,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one_sync()) {
       prefetch_tmap(&tmA);
       prefetch_tmap(&tmB);
+      // A tile source: this GPU's A, or (all-gather) the owning rank's rows
       SegWalk walk(args);
       int tile = 0, kb0 = 0, kb1 = 0;
       bool have = walk.next(tile, kb0, kb1);
+      auto a_src = [&](int m, int& row) -> const CUtensorMap* {
+        row = m * BM;
+        if (args.ag_rows <= 0) return &tmA;
+        const int q = row / args.ag_rows;
+        row -= q * args.ag_rows;
+        return args.ag_maps + q;
+      };
+      if (args.ag_rows > 0) {
+        // the maps were written to global memory by the host: order them
+        // before their use by the tensor-map proxy
+        const int nq_ranks = (args.M + args.ag_rows - 1) / args.ag_rows;
+        for (int q = 0; q < nq_ranks; ++q)
+          asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(args.ag_maps + q) : "memory");
+        // every shard must be published by its rank before it is read
+        if (args.ag_flags != nullptr) {
+          const unsigned long long t0 = global_ns();
+          for (int q = 0; q < nq_ranks; ++q) {
+            for (uint32_t i = 0;; ++i) {
+              unsigned v;
+              asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(args.ag_flags + q) : "memory");
+              if ((int)(v - args.ag_epoch) >= 0) break;
+              if ((i & 255u) == 255u && (error_set() || global_ns() - t0 > kWaitNs)) {
+                set_error(kErrPeerFlag, q);
+                have = false;   // load nothing; the other roles time out on their barriers
+                break;
+              }
+              __nanosleep(64);
+            }
+          }
+        }
+      }
       // weights are not written by earlier kernels: the first stages get
       // their weight tiles while the previous kernel drains
       const int pre = have ? min(C::kStages, kb1 - kb0) : 0;
@@ -196,8 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pdl_wait();
       pdl_trigger();
-      for (int j = 0; j < pre; ++j)
-        tma_load_2d(smem_a + j * C::kABytes, &tmA, &full[j], (kb0 + j) * BK, (tile % args.m_tiles) * BM);
+      for (int j = 0; j < pre; ++j) {
+        int arow;
+        const CUtensorMap* am = a_src(tile % args.m_tiles, arow);
+        tma_load_2d(smem_a + j * C::kABytes, am, &full[j], (kb0 + j) * BK, arow);
+      }
       int stage = pre == C::kStages ? 0 : pre;
       uint32_t phase = pre == C::kStages ? 1u : 0u;
       bool ok = true;
@@ -210,7 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-          tma_load_2d(smem_a + stage * C::kABytes, &tmA, &full[stage], kb * BK, m * BM);
+          int arow;
+          const CUtensorMap* am = a_src(m, arow);
+          tma_load_2d(smem_a + stage * C::kABytes, am, &full[stage], kb * BK, arow);
           tma_load_2d(smem_b + stage * C::kBBytes, &tmB, &full[stage], kb * BK, n * BN);
           if (++stage == C::kStages) {
             stage = 0;
@@ -291,23 +383,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
       const int col0 = n * kOutCols;
       if (kb0 == 0 && kb1 == num_kb) {
-        if (ok && EPI == EPI_SILU) {
+        // 64 output columns per pass: TMEM -> registers -> E[row][col] (one
+        // row per thread), then each warp writes 4 rows x 128 contiguous
+        // bytes (bf16) per instruction.  The barriers run whether or not the wait
+        // succeeded, so all four warps always meet them.
+        float* erow = epi + r_in_tile * C::kEpiStride;
+        const int we = warp - 2;
 #pragma unroll 1
-          for (int c = 0; c < BN / 2; c += 16) {
-            float g[16], up[16], o[16];
-            tmem_ld16(taddr + c, g);
-            tmem_ld16(taddr + BN / 2 + c, up);
+        for (int c0 = 0; c0 < kOutCols; c0 += 64) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = silu(g[i]) * up[i];
-            store16<EPI_BF16>(args, row, col0 + c, o);
-          }
-        } else if (ok) {
-#pragma unroll 1
-          for (int c = 0; c < BN; c += 16) {
+          for (int c = 0; c < 64; c += 16) {
             float v[16];
-            tmem_ld16(taddr + c, v);
-            store16<EPI>(args, row, col0 + c, v);
+            if (EPI == EPI_SILU) {
+              float up[16];
+              tmem_ld16(taddr + c0 + c, v);
+              tmem_ld16(taddr + BN / 2 + c0 + c, up);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = silu(v[i]) * up[i];
+            } else {
+              tmem_ld16(taddr + c0 + c, v);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) erow[c + i] = v[i];
           }
+          named_barrier(2, 128);
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = we * 32 + it * 4 + (lane >> 3);   // 4 rows x 8 lanes of 16 B per pass
+            const int cc = (lane & 7) * 8;
+            const int grow = m * BM + rr, gcol = col0 + c0 + cc;
+            if (ok && grow < args.M && gcol < args.n_out) {
+              float x[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) x[e] = epi[rr * C::kEpiStride + cc + e];
+              out8<EPI>(args, grow, gcol, x);
+            }
+          }
+          named_barrier(2, 128);
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);

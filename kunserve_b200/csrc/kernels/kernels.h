@@ -76,9 +76,15 @@ void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off,
                  long long chunk, int max_blocks, cudaStream_t s);
 void add_inplace(__nv_bfloat16* x, const __nv_bfloat16* y, long long n, cudaStream_t s);
 // Reduce side of the fused tensor-parallel all-reduce (see elementwise.cu).
+// Rows [row0, row0 + T) (row0 > 0: the reduce-scatter owner's block).
 void tp_reduce_rmsnorm(const __nv_bfloat16* rb, int R, long long slot_elems, __nv_bfloat16* h,
                        const __nv_bfloat16* w, __nv_bfloat16* y, int T, int H, float eps, const unsigned* flags,
-                       unsigned epoch, cudaStream_t s);
+                       unsigned epoch, cudaStream_t s, int row0 = 0);
+struct FlagList {
+  unsigned* ptr[8];
+  int n;
+};
+void signal_flags(const FlagList& f, unsigned epoch, cudaStream_t s);
 
 // Paged attention over a ragged batch (prefill chunks and decodes mixed).
 struct AttnBatch {

@@ -153,3 +153,23 @@ def test_balloon_cycle_two_gpus(p2p):
     by = {r["request_id"]: r for r in res}
     assert all(len(by[i]["outputs"]) == 60 for i in range(10))
     assert all(len(by[100 + i]["outputs"]) == 20 for i in range(4))
+
+
+def test_fused_reduce_scatter_and_allgather_gemm_two_gpus():
+    """GEMM + reduce-scatter (row blocks pushed to their owners) and
+    all-gather + GEMM (A shards read by TMA from the owning GPU) against
+    PyTorch on 2 ranks (the sweep's --check mode asserts the numbers)."""
+    _need2()
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", "29533", os.path.join(root, "evaluation", "multigpu_bench.py"),
+           "--what", "rs", "ag", "--check", "--tokens", "1", "16", "256", "512", "--hidden", "4096",
+           "--iters", "2", "--warmup", "1"]
+    r = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert any("reduce_scatter" in ln for ln in lines) and any("allgather" in ln for ln in lines), r.stdout[-2000:]
