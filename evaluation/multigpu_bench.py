@@ -184,7 +184,7 @@ def bench_ag(args, C, dev, rank, world):
         for kind, N_full in (("qkv", H), ("gate_up", 2 * args.ffn.get(H, 4 * H))):
             N = N_full // world
             W = (torch.randn(N, H, device=dev) * 0.02).bfloat16()
-            maps = torch.empty(128 * world, device=dev, dtype=torch.uint8)
+            maps = torch.empty(128, device=dev, dtype=torch.uint8)
             for M in args.tokens:
                 rows = M // world
                 if rows < 128 or rows % 128:
@@ -197,12 +197,15 @@ def bench_ag(args, C, dev, rank, world):
                 torch.cuda.synchronize(dev)
                 dist.barrier()
                 out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                gbuf = torch.empty(M, H, device=dev, dtype=torch.bfloat16)
+                ready = torch.zeros(M // 128, device=dev, dtype=torch.int32)
+                chunks = 0       # the binding picks enough slices for every SM
                 epoch = [0]
 
                 def fused():
                     epoch[0] += 1
                     C.tp_signal(bases, rank, epoch[0])
-                    C.tp_allgather_gemm(W, out, bases, rank, rows, H, epoch[0], maps)
+                    C.tp_allgather_gemm(W, out, bases, rank, rows, H, epoch[0], maps, gbuf, ready, chunks)
 
                 gathered = torch.empty(M, H, device=dev, dtype=torch.bfloat16)
 

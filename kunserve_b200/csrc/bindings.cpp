@@ -237,24 +237,36 @@ void tp_signal_op(std::vector<int64_t> bases, int64_t rank, int64_t epoch) {
 }
 
 // Fused all-gather + GEMM: out[M, N] = A_all @ B^T with A_all the row
-// concatenation of every rank's shard (rows_per_rank x K at bases[q] + 4096),
-// read by TMA from the owning GPU inside the GEMM once its flag (slot q of
-// this rank's buffer) reaches `epoch`.  maps: uint8 CUDA tensor, >= 128 * R bytes.
+// concatenation of every rank's shard (rows_per_rank x K at bases[q] + 4096,
+// published by tp_signal with `epoch`).  This rank's rows are computed
+// first from its own shard while the GEMM's gather warps copy the other
+// shards into `gather` ([M, K] bf16) once over NVLink; `ready` (int32,
+// M/128 entries, zero at allocation, reused across calls with increasing
+// epochs) counts landed slices (chunks per 128-row tile; <= 0 picks enough
+// for every SM).  maps: uint8 CUDA tensor of >= 128 bytes.
 void tp_allgather_gemm_op(torch::Tensor B, torch::Tensor out, std::vector<int64_t> bases, int64_t rank,
-                          int64_t rows_per_rank, int64_t K, int64_t epoch, torch::Tensor maps) {
+                          int64_t rows_per_rank, int64_t K, int64_t epoch, torch::Tensor maps, torch::Tensor gather,
+                          torch::Tensor ready, int64_t chunks) {
   CHECK_CUDA_BF16(B);
+  CHECK_CUDA_BF16(gather);
   c10::cuda::CUDAGuard g(B.device());
   const int R = (int)bases.size(), N = B.size(0), M = R * (int)rows_per_rank;
   TORCH_CHECK(R <= kMaxTpPeers && rows_per_rank % 128 == 0 && M > 128, "tp_allgather_gemm: shards of 128-row tiles");
-  TORCH_CHECK(maps.is_cuda() && maps.numel() >= 128 * R, "maps buffer");
+  TORCH_CHECK(maps.is_cuda() && maps.numel() >= 128, "maps buffer");
+  TORCH_CHECK(gather.numel() >= (int64_t)M * K && ready.numel() >= M / 128, "gather / ready buffers");
+  if (chunks <= 0) {
+    // enough slices for every SM's gather warps, each at least 64 columns
+    const int remote_tiles = (M - (int)rows_per_rank) / 128;
+    chunks = std::max<int64_t>(1, std::min<int64_t>(K / 64, (148 + remote_tiles - 1) / remote_tiles));
+    while (K % (8 * chunks)) --chunks;
+  }
+  TORCH_CHECK(chunks > 0 && K % (8 * chunks) == 0, "K must split into chunks of 8-column multiples");
   GemmPlan p = plan_gemm(M, N, (int)K, EPI_BF16, 0, false);
   TORCH_CHECK(!p.swap, "all-gather GEMM needs the 128-row kernel");
-  std::vector<CUtensorMap> host(R);
-  for (int q = 0; q < R; ++q)
-    TORCH_CHECK(make_tmap_bf16(&host[q], reinterpret_cast<const void*>(bases[q] + 4096), rows_per_rank, K, K, 128),
-                "shard tensor map");
+  CUtensorMap host;
+  TORCH_CHECK(make_tmap_bf16(&host, gather.data_ptr(), M, K, K, 128), "gather tensor map");
   auto st = at::cuda::getCurrentCUDAStream();
-  cudaMemcpyAsync(maps.data_ptr(), host.data(), sizeof(CUtensorMap) * R, cudaMemcpyHostToDevice, st);
+  cudaMemcpyAsync(maps.data_ptr(), &host, sizeof(CUtensorMap), cudaMemcpyHostToDevice, st);
   TORCH_CHECK(finalize_plan(p, reinterpret_cast<const void*>(bases[rank] + 4096), (int)K, B.data_ptr(), (int)K,
                             out.data_ptr(), N, nullptr, N, nullptr, nullptr, (uint64_t)rows_per_rank, 0),
               "tensor map encoding failed");
@@ -262,6 +274,11 @@ void tp_allgather_gemm_op(torch::Tensor B, torch::Tensor out, std::vector<int64_
   p.args.ag_rows = (int)rows_per_rank;
   p.args.ag_flags = reinterpret_cast<const unsigned*>(bases[rank]);
   p.args.ag_epoch = (unsigned)epoch;
+  p.args.ag_rank = (int)rank;
+  p.args.ag_chunks = (int)chunks;
+  p.args.ag_gather = bp(gather);
+  p.args.ag_ready = ready.data_ptr<int>();
+  for (int q = 0; q < R; ++q) p.args.ag_src[q] = reinterpret_cast<const __nv_bfloat16*>(bases[q] + 4096);
   run_gemm(p, st);
 }
 

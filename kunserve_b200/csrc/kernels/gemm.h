@@ -38,16 +38,24 @@ struct GemmArgs {
   // EPI_PUSH as reduce-scatter: with rs_rows > 0, output row r goes only to
   // rank r / rs_rows (the owner of that row block), not to every rank.
   int rs_rows;
-  // All-gather fused into the A operand (regular kernel): with ag_rows > 0,
-  // rows [q*ag_rows, (q+1)*ag_rows) of A are read by TMA straight from rank
-  // q's memory through ag_maps[q] (tensor maps in global memory, 128-row
-  // boxes, no multicast); ag_rows is a multiple of 128.
+  // All-gather fused into the A operand (regular kernel).  With ag_rows > 0,
+  // rank q owns rows [q*ag_rows, (q+1)*ag_rows) of A (a multiple of 128);
+  // this rank's rows come from tmA (its own shard) and are computed first,
+  // while two gather warps per CTA pull the other shards (ag_src[q], peer
+  // memory, after a bounded wait on flag ag_flags[q] >= ag_epoch) into the
+  // local buffer ag_gather [M x K] in ag_chunks column slices per 128-row
+  // tile, counting finished slices in ag_ready[m-tile]; the producer loads a
+  // remote tile through ag_maps[0] (a map over ag_gather) once its count
+  // reaches ag_epoch * ag_chunks.  Every remote byte crosses NVLink once.
   const CUtensorMap* ag_maps;
   int ag_rows;
-  // optional readiness flags of the A shards: ag_flags[q] >= ag_epoch once
-  // rank q's rows are written (bounded wait by the producer before any load)
   const unsigned* ag_flags;
   unsigned ag_epoch;
+  int ag_rank;
+  int ag_chunks;
+  __nv_bfloat16* ag_gather;
+  const __nv_bfloat16* ag_src[kMaxTpPeers];
+  int* ag_ready;
 };
 
 struct GemmPlan {

@@ -189,8 +189,102 @@ KUS_DEVICE void signal_push_done(const GemmArgs& a, int et) {
 
 namespace gemm_impl {
 
-template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+// (m, n) of data-parallel tile `tile`: m-fastest, or with the fused
+// all-gather this rank's m-tiles (all n) first, then the remote ones.
+KUS_DEVICE void tile_mn(const GemmArgs& a, int tile, int& m, int& n) {
+  if (a.ag_rows <= 0) {
+    m = tile % a.m_tiles;
+    n = tile / a.m_tiles;
+    return;
+  }
+  const int L = a.ag_rows / BM, first = a.ag_rank * L;
+  if (tile < L * a.n_tiles) {
+    m = first + tile % L;
+    n = tile / L;
+    return;
+  }
+  const int t = tile - L * a.n_tiles, rm = a.m_tiles - L;
+  const int mr = t % rm;
+  n = t / rm;
+  m = mr < first ? mr : mr + L;
+}
+
+KUS_DEVICE bool ag_local(const GemmArgs& a, int m) {
+  const int L = a.ag_rows / BM;
+  return m >= a.ag_rank * L && m < (a.ag_rank + 1) * L;
+}
+
+// Gather warps (64 threads, named barrier 3): copy the remote shards' column
+// slices assigned to this CTA into ag_gather and count each finished slice.
+KUS_DEVICE void ag_gather_slices(const GemmArgs& a, int gt) {
+  const int L = a.ag_rows / BM, first = a.ag_rank * L, rm = a.m_tiles - L;
+  const int nranks = a.m_tiles / L;
+  // every remote shard must be published before it is read; both warps
+  // agree on the outcome (barrier reduction) so they leave together
+  bool ok = true;
+  if (a.ag_flags != nullptr) {
+    const unsigned long long t0 = global_ns();
+    for (int q = 0; q < nranks && ok; ++q) {
+      if (q == a.ag_rank) continue;
+      for (uint32_t i = 0;; ++i) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.ag_flags + q) : "memory");
+        if ((int)(v - a.ag_epoch) >= 0) break;
+        if ((i & 255u) == 255u && (error_set() || global_ns() - t0 > kWaitNs)) {
+          set_error(kErrPeerFlag, q);
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  uint32_t all_ok;
+  asm volatile("{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbarrier.red.and.pred q, 3, 64, p;\nselp.u32 %0, 1, 0, q;\n}"
+               : "=r"(all_ok)
+               : "r"((uint32_t)ok));
+  if (!all_ok) return;
+  const int colw = a.K / a.ag_chunks;          // columns per slice (multiple of 8)
+  const int vec_per_row = colw / 8;
+  const int units = rm * a.ag_chunks;
+  for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    const int mr = u / a.ag_chunks, c = u % a.ag_chunks;
+    const int m = mr < first ? mr : mr + L;
+    const int q = (m * BM) / a.ag_rows;
+    const int lrow0 = m * BM - q * a.ag_rows;
+    const __nv_bfloat16* src = a.ag_src[q] + (size_t)lrow0 * a.K + (size_t)c * colw;
+    __nv_bfloat16* dst = a.ag_gather + (size_t)m * BM * a.K + (size_t)c * colw;
+    const int total = BM * vec_per_row;
+    for (int i0 = gt; i0 < total; i0 += 64 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + 64 * j;
+        if (i < total) {
+          const int r = i / vec_per_row, e = i - r * vec_per_row;
+          v[j] = *reinterpret_cast<const uint4*>(src + (size_t)r * a.K + e * 8);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int i = i0 + 64 * j;
+        if (i < total) {
+          const int r = i / vec_per_row, e = i - r * vec_per_row;
+          *reinterpret_cast<uint4*>(dst + (size_t)r * a.K + e * 8) = v[j];
+        }
+      }
+    }
+    // the slice is read by TMA (async proxy) on other SMs: order the
+    // generic stores before the release of the count
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __threadfence();
+    named_barrier(3, 64);
+    if (gt == 0) atomicAdd(a.ag_ready + m, 1);
+  }
+}
+
+template <int BN, int EPI, int GW>
+__global__ void __launch_bounds__(kThreads + 32 * GW, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -234,7 +328,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_trigger();
   }
 
-  if (warp == 0) {
+  if (GW > 0 && warp >= 6) {
+    // -------------------------------------------------------- gather warps
+    if (args.ag_rows > 0) ag_gather_slices(args, threadIdx.x - 192);
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one_sync()) {
       prefetch_tmap(&tmA);
@@ -243,49 +340,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       SegWalk walk(args);
       int tile = 0, kb0 = 0, kb1 = 0;
       bool have = walk.next(tile, kb0, kb1);
+      // A tile source: this GPU's A, or (all-gather) the own shard for local
+      // rows and the gathered copy for remote rows once it has landed
+      const unsigned ready_target = args.ag_epoch * (unsigned)args.ag_chunks;
       auto a_src = [&](int m, int& row) -> const CUtensorMap* {
         row = m * BM;
         if (args.ag_rows <= 0) return &tmA;
-        const int q = row / args.ag_rows;
-        row -= q * args.ag_rows;
-        return args.ag_maps + q;
-      };
-      if (args.ag_rows > 0) {
-        // the maps were written to global memory by the host: order them
-        // before their use by the tensor-map proxy
-        const int nq_ranks = (args.M + args.ag_rows - 1) / args.ag_rows;
-        for (int q = 0; q < nq_ranks; ++q)
-          asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(args.ag_maps + q) : "memory");
-        // every shard must be published by its rank before it is read
-        if (args.ag_flags != nullptr) {
-          const unsigned long long t0 = global_ns();
-          for (int q = 0; q < nq_ranks; ++q) {
-            for (uint32_t i = 0;; ++i) {
-              unsigned v;
-              asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(args.ag_flags + q) : "memory");
-              if ((int)(v - args.ag_epoch) >= 0) break;
-              if ((i & 255u) == 255u && (error_set() || global_ns() - t0 > kWaitNs)) {
-                set_error(kErrPeerFlag, q);
-                have = false;   // load nothing; the other roles time out on their barriers
-                break;
-              }
-              __nanosleep(64);
-            }
-          }
+        if (ag_local(args, m)) {
+          row -= args.ag_rank * args.ag_rows;
+          return &tmA;
         }
-      }
+        const unsigned long long t0 = global_ns();
+        for (uint32_t i = 0;; ++i) {
+          int v;
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(args.ag_ready + m) : "memory");
+          if ((int)((unsigned)v - ready_target) >= 0) break;
+          if ((i & 255u) == 255u && (error_set() || global_ns() - t0 > kWaitNs)) {
+            set_error(kErrPeerFlag, 100 + m);
+            break;
+          }
+          __nanosleep(32);
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        return args.ag_maps;
+      };
+      if (args.ag_rows > 0)
+        asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(args.ag_maps) : "memory");
       // weights are not written by earlier kernels: the first stages get
       // their weight tiles while the previous kernel drains
       const int pre = have ? min(C::kStages, kb1 - kb0) : 0;
       for (int j = 0; j < pre; ++j) {
         mbar_arrive_expect_tx(&full[j], C::kStageBytes);
-        tma_load_2d(smem_b + j * C::kBBytes, &tmB, &full[j], (kb0 + j) * BK, (tile / args.m_tiles) * BN);
+        int m0, n0;
+        tile_mn(args, tile, m0, n0);
+        tma_load_2d(smem_b + j * C::kBBytes, &tmB, &full[j], (kb0 + j) * BK, n0 * BN);
       }
       pdl_wait();
       pdl_trigger();
       for (int j = 0; j < pre; ++j) {
-        int arow;
-        const CUtensorMap* am = a_src(tile % args.m_tiles, arow);
+        int arow, m0, n0;
+        tile_mn(args, tile, m0, n0);
+        const CUtensorMap* am = a_src(m0, arow);
         tma_load_2d(smem_a + j * C::kABytes, am, &full[j], (kb0 + j) * BK, arow);
       }
       int stage = pre == C::kStages ? 0 : pre;
@@ -293,15 +388,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int kb_from = kb0 + pre;
       while (ok && have) {
-        const int m = tile % args.m_tiles, n = tile / args.m_tiles;
+        int m, n;
+        tile_mn(args, tile, m, n);
+        int arow;
+        const CUtensorMap* am = a_src(m, arow);   // once per tile (a bounded wait for remote rows)
         for (int kb = kb_from; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-          int arow;
-          const CUtensorMap* am = a_src(m, arow);
           tma_load_2d(smem_a + stage * C::kABytes, am, &full[stage], kb * BK, arow);
           tma_load_2d(smem_b + stage * C::kBBytes, &tmB, &full[stage], kb * BK, n * BN);
           if (++stage == C::kStages) {
@@ -374,7 +470,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     SegWalk walk(args);
     int tile, kb0, kb1;
     while (walk.next(tile, kb0, kb1)) {
-      const int m = tile % args.m_tiles, n = tile / args.m_tiles;
+      int m, n;
+      tile_mn(args, tile, m, n);
       const int row = m * BM + r_in_tile;
       // A failed (timed-out) wait skips the work but keeps every thread on the
       // same barrier sequence; once the error flag is set later waits fail fast.
@@ -466,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
-  if (EPI == EPI_PUSH && warp >= 2) signal_push_done(args, threadIdx.x - 64);
+  if (EPI == EPI_PUSH && warp >= 2 && warp < 6) signal_push_done(args, threadIdx.x - 64);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
@@ -484,19 +581,27 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int GW = 0>
 void launch(const GemmPlan& p, cudaStream_t stream) {
   using C = Cfg<BN>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    cudaFuncSetAttribute(gemm_kernel<BN, EPI, GW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     attr_set = true;
   }
-  launch_k(gemm_kernel<BN, EPI>, dim3(p.grid), dim3(kThreads), C::kSmemBytes, stream, p.tmA, p.tmB, p.args);
+  launch_k(gemm_kernel<BN, EPI, GW>, dim3(p.grid), dim3(kThreads + 32 * GW), C::kSmemBytes, stream, p.tmA, p.tmB,
+           p.args);
 }
 
 template <int EPI>
 void launch_bn(const GemmPlan& p, cudaStream_t s) {
+  if (p.args.ag_rows > 0) {   // fused all-gather: two gather warps per CTA
+    switch (p.bn) {
+      case 128: launch<128, EPI, 2>(p, s); break;
+      default: launch<256, EPI, 2>(p, s); break;
+    }
+    return;
+  }
   switch (p.bn) {
     case 64: launch<64, EPI>(p, s); break;
     case 128: launch<128, EPI>(p, s); break;
