@@ -73,7 +73,21 @@ async def _run(mode):
         assert leader.get_num_fusion_requests() == 0
         await group.trigger_init()
         assert group.state == EngineState.INITIAL and leader.num_instances == 1
-        results = await asyncio.wait_for(asyncio.gather(*tasks), 300)
+        try:
+            results = await asyncio.wait_for(asyncio.gather(*tasks), 300)
+        except asyncio.TimeoutError:
+            # name where every unfinished request sits, so a stall is debuggable
+            where = []
+            for inst in group.instances:
+                where.append(f"instance {inst.instance_id} state={inst.state} stopped={inst.stopped} "
+                             f"unaccepted={[r.request_id for r in inst.unaccepted_queue]}")
+                for k, s in enumerate(inst.scheduler):
+                    where.append(f"  ve{k} running={[r.request_id for r in s.running_queue.requests]} "
+                                 f"waiting={[r.request_id for r in s.waiting_queue]} "
+                                 f"swapped={[r.request_id for r in s.swapped_queue]} "
+                                 f"unaccepted={[r.request_id for r in s.unaccepted_queue]} "
+                                 f"long={[r.request_id for r in s.long_unaccepted_queue]}")
+            raise AssertionError("requests did not finish after the balloon cycle:\n" + "\n".join(where))
         for inst in group.instances:
             for bm in inst.block_managers:
                 bm.check_invariants()
