@@ -59,6 +59,9 @@ def bench_gemm(args, cublas=False):
                 out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
                 if cublas:
                     fn = lambda i: torch.matmul(A, Ws[i % len(Ws)].t(), out=out)
+                elif args.partials:
+                    parts = torch.empty(16 * M * N, device="cuda")
+                    fn = lambda i: C.gemm_partials(A, Ws[i % len(Ws)], parts, 16)
                 else:
                     fn = lambda i: C.gemm(A, Ws[i % len(Ws)], out, C.EPI_BF16, None, args.bn, args.max_split)
                 t = timeit(fn, args.warmup, args.iters)
@@ -149,6 +152,7 @@ def main():
     p.add_argument("--k", type=int, nargs="+", default=[4096])
     p.add_argument("--bn", type=int, default=0)
     p.add_argument("--max-split", type=int, default=16)
+    p.add_argument("--partials", action="store_true", help="split-K into fp32 partial slots (decode GEMMs)")
     p.add_argument("--batch", type=int, nargs="+", default=[1, 16, 64, 256])
     p.add_argument("--ctx", type=int, nargs="+", default=[512, 2048])
     p.add_argument("--nq", type=int, default=32)

@@ -62,6 +62,23 @@ int64_t gemm_op(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi
   return p.args.sk_tiles;
 }
 
+// Split-K into fp32 partial slots: parts[s, M, N]; returns the slot count
+// (1: no split, slot 0 holds the whole product).
+int64_t gemm_partials_op(torch::Tensor A, torch::Tensor B, torch::Tensor parts, int64_t max_slots) {
+  CHECK_CUDA_BF16(A);
+  CHECK_CUDA_BF16(B);
+  c10::cuda::CUDAGuard g(A.device());
+  const int M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(parts.is_cuda() && parts.scalar_type() == torch::kFloat32 && parts.numel() >= max_slots * (int64_t)M * N,
+              "parts: fp32 [max_slots, M, N]");
+  GemmPlan p = plan_gemm(M, N, K, EPI_F32, 0, false);
+  int S = plan_split_partials(p, (int)max_slots, (long long)M * N);
+  TORCH_CHECK(finalize_plan(p, A.data_ptr(), K, B.data_ptr(), K, parts.data_ptr(), N, nullptr, N, nullptr, nullptr),
+              "tensor map encoding failed");
+  run_gemm(p, at::cuda::getCurrentCUDAStream());
+  return S;
+}
+
 void rmsnorm_op(torch::Tensor x, c10::optional<torch::Tensor> add, torch::Tensor w, torch::Tensor y,
                 c10::optional<torch::Tensor> rows, double eps) {
   CHECK_CUDA_BF16(x);
@@ -368,6 +385,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_gemm_reduce_scatter", &tp_gemm_reduce_scatter_op);
   m.def("tp_allgather_gemm", &tp_allgather_gemm_op);
   m.def("tp_signal", &tp_signal_op);
+  m.def("gemm_partials", &gemm_partials_op);
   m.def("num_sms", &num_sms);
   m.attr("EPI_BF16") = (int)EPI_BF16;
   m.attr("EPI_F32") = (int)EPI_F32;

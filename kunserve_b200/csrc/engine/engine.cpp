@@ -57,6 +57,8 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   sync_debug_ = dbg && dbg[0] == '1';
   const char* pdl = std::getenv("KUNSERVE_PDL");
   pdl_ = !(pdl && pdl[0] == '0');
+  const char* parts = std::getenv("KUNSERVE_SPLITK_PARTIALS");
+  parts_ = !(parts && parts[0] == '0');
   c10::cuda::CUDAGuard g(device_);
   auto bf = torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, device_);
   auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA, device_);
@@ -74,6 +76,8 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   // tiles); kept all zero between GEMMs by the kernels themselves
   const int64_t ws_floats = (int64_t)2 * 148 * 128 * 256;
   gemm_ws_ = torch::zeros({ws_floats}, f32);
+  // split-K partial slots of decode-sized GEMMs (up to 128 tokens)
+  part_ws_ = torch::empty({(int64_t)kMaxPartSlots * 128 * std::max<int64_t>(qkv_n_, s.hidden)}, f32);
   counters_ = torch::zeros({1 << 16}, i32);
   attn_split_tokens_ = std::min<int64_t>(T, 512);
   attn_o_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * s.hd}, f32);
@@ -256,6 +260,25 @@ void Engine::gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, in
   if (sync_debug_) debug_check("gemm", M, N, K, st);
 }
 
+int Engine::gemm_partials(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, cudaStream_t st) {
+  if (!parts_ || s_.tp > 1 || M > 128) return 0;
+  GemmPlan p = plan_gemm(M, N, K, EPI_F32, mB.has128 ? 0 : 256, false);
+  if (!p.swap) return 0;
+  const long long stride = (long long)M * N;
+  const int max_slots = (int)std::min<long long>(kMaxPartSlots, part_ws_.numel() / stride);
+  const int S = plan_split_partials(p, max_slots, stride);
+  if (S < 2) return 0;
+  const int box = a_box_rows(p);
+  p.tmA = mA[box == 16 ? 0 : box == 32 ? 1 : box == 64 ? 2 : 3];
+  p.tmB = pick(mB, p);
+  p.args.out = part_ws_.data_ptr<float>();
+  p.args.ldc = N;
+  run_gemm(p, st);
+  ++launches_;
+  if (sync_debug_) debug_check("gemm_partials", M, N, K, st);
+  return S;
+}
+
 void Engine::debug_check(const char* what, int a, int b, int c, cudaStream_t st) {
   check_cuda(cudaStreamSynchronize(st), what);
   const long long e = error_flag(false);
@@ -351,6 +374,8 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     armed = true;
   }
   bool pending = false;   // tmp holds an all-reduced partial still to be added to h
+  int pend_parts = 0;     // split-K slots of down_proj still to be added to h (by the next norm)
+  float* part = part_ws_.data_ptr<float>();
   bool y_ready = false;   // the fused all-reduce already produced this layer's normed input
   // the push epilogue wins at decode sizes; NCCL's ring wins for large steps
   const bool fused = tp && fused_ && T <= fused_max_tokens_;
@@ -358,15 +383,20 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     for (int d : dropped) KUS_CHECK(d != l, "step touches a dropped layer");
     const LayerW& W = layers_[l];
     const int ll = (int)(l - layer_start);
-    if (!y_ready) rmsnorm(h, pending ? tmp : nullptr, W.in_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+    if (!y_ready)
+      rmsnorm(h, pending ? tmp : nullptr, W.in_norm, y, nullptr, (int)T, H, (float)s_.eps, st,
+              pend_parts ? part : nullptr, pend_parts, (long long)T * H);
+    pend_parts = 0;
     if (!armed) {
       set_pdl(pdl_);
       armed = true;
     }
     y_ready = false;
-    gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
+    // decode-sized steps: split-K partial slots, summed by RoPE + KV append
+    int np = gemm_partials(m_y_, W.m_qkv, (int)T, qkv_n_, H, st);
+    if (np == 0) gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
     rope_append(qkv, positions, kv_page, kv_slot, cos_sin_.data_ptr<float>(), geo, ll, (int)T, s_.nq, s_.nkv,
-                s_.max_pos, st);
+                s_.max_pos, st, np ? part : nullptr, np, (long long)T * qkv_n_);
     paged_attention(m_attn_q_, m_attn_kv_, m_dec_kv_, qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
     if (sync_debug_) debug_check("attention", (int)T, (int)B, (int)n_dec, st);
     launches_ += 3 + (splits > 1 ? 1 : 0);
@@ -377,6 +407,9 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
       gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_BF16, tmp, H, nullptr, st);
       all_reduce(tmp, T * H, st);
       rmsnorm(h, tmp, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+    } else if ((np = gemm_partials(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, st)) > 0) {
+      // residual add of the partial slots fused into the post-attention norm
+      rmsnorm(h, nullptr, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st, part, np, (long long)T * H);
     } else {
       gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_ADD, h, H, h, st);
       rmsnorm(h, nullptr, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
@@ -394,7 +427,11 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
       all_reduce(tmp, T * H, st);
       pending = true;
     } else {
-      gemm(m_act_, W.m_down, (int)T, H, f_pad_, EPI_ADD, h, H, h, st);
+      // partial slots are added by the next norm; a stage that hands h to
+      // the next pipeline stage finishes its last layer in place
+      const bool hand_off = l + 1 == layer_end && !last_stage;
+      pend_parts = hand_off ? 0 : gemm_partials(m_act_, W.m_down, (int)T, H, f_pad_, st);
+      if (pend_parts == 0) gemm(m_act_, W.m_down, (int)T, H, f_pad_, EPI_ADD, h, H, h, st);
       pending = false;
     }
   }
@@ -406,7 +443,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   if (!last_stage) return out;
   auto* yl = reinterpret_cast<__nv_bfloat16*>(ylast_.data_ptr());
   rmsnorm(h, nullptr, reinterpret_cast<const __nv_bfloat16*>(final_norm_.data_ptr()), yl, last_idx, (int)B, H,
-          (float)s_.eps, st);
+          (float)s_.eps, st, pend_parts ? part : nullptr, pend_parts, (long long)T * H);
   ++launches_;
   gemm(m_ylast_, m_lm_head_, (int)B, s_.vocab, H, EPI_F32, logits_.data_ptr(), s_.vocab, nullptr, st);
   if (sample_mode == 1) return out;   // caller samples from logits()

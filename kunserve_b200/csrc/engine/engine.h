@@ -146,6 +146,14 @@ class Engine {
   bool sync_debug_ = false;
   // KUNSERVE_PDL=0 turns off programmatic dependent launch in forward()
   bool pdl_ = true;
+  // KUNSERVE_SPLITK_PARTIALS=0 keeps decode GEMMs on whole tiles / stream-K
+  bool parts_ = true;
+  static constexpr int kMaxPartSlots = 16;
+  torch::Tensor part_ws_;
+  // Decode-sized GEMM as split-K fp32 partial slots in part_ws_ (slot s at
+  // s * M * N); returns the slot count, or 0 when the plan does not split
+  // (the caller then runs the regular GEMM).
+  int gemm_partials(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, cudaStream_t st);
   void debug_check(const char* what, int a, int b, int c, cudaStream_t st);
 };
 

@@ -38,7 +38,8 @@ void embed(const int* tokens, const __nv_bfloat16* table, __nv_bfloat16* out, in
 template <int VPT>
 __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ add,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
-                               const int* __restrict__ rows, int H, float eps) {
+                               const int* __restrict__ rows, int H, float eps, const float* __restrict__ parts,
+                               int nparts, long long pstride) {
   pdl_wait();
   pdl_trigger();
   const int r = blockIdx.x;
@@ -55,11 +56,25 @@ __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat1
     const int i = threadIdx.x + j * blockDim.x;
     if (i < nv) {
       unpack_bf16x8(xr[i], v[j]);
-      if (ar) {
-        float a[8];
-        unpack_bf16x8(ar[i], a);
+      if (ar || parts) {
+        if (ar) {
+          float a[8];
+          unpack_bf16x8(ar[i], a);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[j][k] += a[k];
+          for (int k = 0; k < 8; ++k) v[j][k] += a[k];
+        }
+        if (parts) {
+          // split-K partial slots of the GEMM that produced this residual update
+          float acc[8] = {};
+          for (int p = 0; p < nparts; ++p) {
+            const float4* pp = reinterpret_cast<const float4*>(parts + (size_t)p * pstride + (size_t)src * H) + 2 * i;
+            const float4 a0 = __ldcg(pp), a1 = __ldcg(pp + 1);
+            acc[0] += a0.x; acc[1] += a0.y; acc[2] += a0.z; acc[3] += a0.w;
+            acc[4] += a1.x; acc[5] += a1.y; acc[6] += a1.z; acc[7] += a1.w;
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[j][k] += acc[k];
+        }
         // round the residual stream to bf16 exactly as stored
         uint4 packed = pack_bf16x8(v[j]);
         xr[i] = packed;
@@ -94,19 +109,24 @@ __global__ void rmsnorm_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat1
 }
 
 void rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* add, const __nv_bfloat16* w, __nv_bfloat16* y,
-             const int* rows, int R, int H, float eps, cudaStream_t s) {
+             const int* rows, int R, int H, float eps, cudaStream_t s, const float* parts, int nparts,
+             long long pstride) {
   if (R <= 0) return;
   const int nv = H / 8;
   int threads = nv >= 256 ? 256 : ((nv + 31) / 32) * 32;
   const int vpt = (nv + threads - 1) / threads;
   if (vpt <= 1)
-    launch_k(rmsnorm_kernel<1>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps);
+    launch_k(rmsnorm_kernel<1>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps, parts, nparts,
+             pstride);
   else if (vpt <= 2)
-    launch_k(rmsnorm_kernel<2>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps);
+    launch_k(rmsnorm_kernel<2>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps, parts, nparts,
+             pstride);
   else if (vpt <= 4)
-    launch_k(rmsnorm_kernel<4>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps);
+    launch_k(rmsnorm_kernel<4>, dim3(R), dim3(threads), 0, s, x, add, w, y, rows, H, eps, parts, nparts,
+             pstride);
   else
-    launch_k(rmsnorm_kernel<8>, dim3(R), dim3(1024 / 4), 0, s, x, add, w, y, rows, H, eps);
+    launch_k(rmsnorm_kernel<8>, dim3(R), dim3(1024 / 4), 0, s, x, add, w, y, rows, H, eps, parts, nparts,
+             pstride);
 }
 
 // ----------------------------------------------------- RoPE + KV append
@@ -116,21 +136,38 @@ void rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* add, const __nv_bfloat16* w,
 __global__ void rope_append_kernel(__nv_bfloat16* __restrict__ qkv, const int* __restrict__ positions,
                                    const int* __restrict__ pages, const int* __restrict__ slots,
                                    const float* __restrict__ cos_sin, KVGeom g, int layer, int nq, int nkv,
-                                   int max_pos, int T) {
+                                   int max_pos, int T, const float* __restrict__ parts, int nparts,
+                                   long long pstride) {
   pdl_wait();
   pdl_trigger();
   // one warp per (token, head); head_dim 128: lane owns rotation pairs
-  // (2 lane, 2 lane + 1) of the first half and their partners 64 further
+  // (2 lane, 2 lane + 1) of the first half and their partners 64 further.
+  // With split-K partials the head's values are the sum of the fp32 slots
+  // (qkv then only receives the rotated queries).
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   const int heads = nq + 2 * nkv;
   const int t = warp / heads, h = warp % heads;
   if (t >= T) return;
   constexpr int hd = 128, half = 64;
   __nv_bfloat16* src = qkv + ((size_t)t * heads + h) * hd;
+  const float* psrc = parts ? parts + ((size_t)t * heads + h) * hd : nullptr;
   const int page = pages[t], slot = slots[t];
   if (h >= nq + nkv) {
     __nv_bfloat16* dst = kv_ptr(g, page, layer, true) + ((size_t)slot * g.kvh + (h - nq - nkv)) * hd;
-    if (lane < hd / 8) reinterpret_cast<uint4*>(dst)[lane] = reinterpret_cast<const uint4*>(src)[lane];
+    if (lane < hd / 8) {
+      if (psrc) {
+        float acc[8] = {};
+        for (int p = 0; p < nparts; ++p) {
+          const float4* pp = reinterpret_cast<const float4*>(psrc + (size_t)p * pstride) + 2 * lane;
+          const float4 a0 = __ldcg(pp), a1 = __ldcg(pp + 1);
+          acc[0] += a0.x; acc[1] += a0.y; acc[2] += a0.z; acc[3] += a0.w;
+          acc[4] += a1.x; acc[5] += a1.y; acc[6] += a1.z; acc[7] += a1.w;
+        }
+        reinterpret_cast<uint4*>(dst)[lane] = pack_bf16x8(acc);
+      } else {
+        reinterpret_cast<uint4*>(dst)[lane] = reinterpret_cast<const uint4*>(src)[lane];
+      }
+    }
     return;
   }
   int pos = positions[t];
@@ -140,8 +177,20 @@ __global__ void rope_append_kernel(__nv_bfloat16* __restrict__ qkv, const int* _
   }
   const float2 c = reinterpret_cast<const float2*>(cos_sin + (size_t)pos * hd)[lane];
   const float2 s = reinterpret_cast<const float2*>(cos_sin + (size_t)pos * hd + half)[lane];
-  const float2 x1 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[lane]);
-  const float2 x2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src + half)[lane]);
+  float2 x1, x2;
+  if (psrc) {
+    x1 = make_float2(0.f, 0.f);
+    x2 = make_float2(0.f, 0.f);
+    for (int p = 0; p < nparts; ++p) {
+      const float2 a = __ldcg(reinterpret_cast<const float2*>(psrc + (size_t)p * pstride) + lane);
+      const float2 b = __ldcg(reinterpret_cast<const float2*>(psrc + (size_t)p * pstride + half) + lane);
+      x1.x += a.x; x1.y += a.y;
+      x2.x += b.x; x2.y += b.y;
+    }
+  } else {
+    x1 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src)[lane]);
+    x2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(src + half)[lane]);
+  }
   __nv_bfloat16* dst = h < nq ? src : kv_ptr(g, page, layer, false) + ((size_t)slot * g.kvh + (h - nq)) * hd;
   reinterpret_cast<__nv_bfloat162*>(dst)[lane] =
       __floats2bfloat162_rn(x1.x * c.x - x2.x * s.x, x1.y * c.y - x2.y * s.y);
@@ -151,12 +200,12 @@ __global__ void rope_append_kernel(__nv_bfloat16* __restrict__ qkv, const int* _
 
 void rope_append(__nv_bfloat16* qkv, const int* positions, const int* pages, const int* slots,
                  const float* cos_sin, const KVGeom& g, int layer, int T, int nq, int nkv, int max_pos,
-                 cudaStream_t s) {
+                 cudaStream_t s, const float* parts, int nparts, long long pstride) {
   if (T <= 0) return;
   const long long warps = (long long)T * (nq + 2 * nkv);
   const int threads = 256;
   launch_k(rope_append_kernel, dim3((unsigned)((warps * 32 + threads - 1) / threads)), dim3(threads), 0, s, qkv,
-           positions, pages, slots, cos_sin, g, layer, nq, nkv, max_pos, T);
+           positions, pages, slots, cos_sin, g, layer, nq, nkv, max_pos, T, parts, nparts, pstride);
 }
 
 // -------------------------------------------------------------- sampling

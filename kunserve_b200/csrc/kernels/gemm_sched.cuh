@@ -15,6 +15,7 @@ namespace kus {
 
 struct SegWalk {
   int t, stride, dp_tiles, num_kb;
+  int parts, part_kbs, units;   // split-K with partial slots
   long long i, end;
 
   __device__ __forceinline__ SegWalk(const GemmArgs& a) {
@@ -22,6 +23,9 @@ struct SegWalk {
     stride = gridDim.x;
     dp_tiles = a.dp_tiles;
     num_kb = a.num_kb;
+    parts = a.part_splits;
+    part_kbs = a.part_kbs;
+    units = parts > 0 ? a.n_tiles * a.m_tiles * parts : 0;
     const long long total = (long long)a.sk_tiles * a.num_kb;
     i = total * blockIdx.x / gridDim.x;
     end = total * (blockIdx.x + 1) / gridDim.x;
@@ -29,6 +33,14 @@ struct SegWalk {
 
   // Next segment of this CTA; false when the walk is over.
   __device__ __forceinline__ bool next(int& tile, int& kb0, int& kb1) {
+    if (parts > 0) {   // unit u = (tile, split): fixed K ranges, one slot each
+      if (t >= units) return false;
+      tile = t / parts;
+      kb0 = (t - tile * parts) * part_kbs;
+      kb1 = min(kb0 + part_kbs, num_kb);
+      t += stride;
+      return true;
+    }
     if (t < dp_tiles) {
       tile = t;
       kb0 = 0;

@@ -43,7 +43,7 @@ KUS_DEVICE float silu_s(float x) { return x / (1.0f + __expf(-x)); }
 // token (256 for SiLU, whose tile yields 128 features).
 template <int EPI>
 KUS_DEVICE void emit16(const GemmArgs& a, float* E, int n, int tok0, int r, int we, int lane, const float (&v0)[16],
-                       const float (&v1)[16]) {
+                       const float (&v1)[16], int slot = 0) {
   constexpr int W = EPI == EPI_SILU ? 128 : 256;   // output features of the tile
   constexpr int PL = W / 32;                       // per lane: 8 or 4
 #pragma unroll
@@ -73,7 +73,7 @@ KUS_DEVICE void emit16(const GemmArgs& a, float* E, int n, int tok0, int r, int 
       x[e + 3] = q4.w;
     }
     if (EPI == EPI_F32) {
-      float* dst = reinterpret_cast<float*>(a.out) + (size_t)tok * a.ldc + f0;
+      float* dst = reinterpret_cast<float*>(a.out) + (size_t)slot * a.part_stride + (size_t)tok * a.ldc + f0;
       if (full) {
 #pragma unroll
         for (int e = 0; e < PL; e += 4) *reinterpret_cast<float4*>(dst + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
@@ -277,14 +277,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * 2 * BNT);
       // tokens beyond M carry zeros: their columns are neither reduced nor stored
       const int cols = args.M < BNT ? ((args.M + 15) & ~15) : BNT;
-      if (kb0 == 0 && kb1 == num_kb) {
+      if (args.part_splits > 0 || (kb0 == 0 && kb1 == num_kb)) {
+        // whole tile, or one split's partial into its own slot
+        const int slot = args.part_splits > 0 ? kb0 / args.part_kbs : 0;
         if (ok) {
 #pragma unroll 1
           for (int c = 0; c < cols; c += 16) {
             float v0[16], v1[16];
             tmem_ld16(t0 + c, v0);
             tmem_ld16(t0 + BNT + c, v1);
-            emit16<EPI>(args, epi, n, c, r, warp - 2, lane, v0, v1);
+            emit16<EPI>(args, epi, n, c, r, warp - 2, lane, v0, v1, slot);
           }
         }
         tc_fence_before();

@@ -708,6 +708,29 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
   return p;
 }
 
+int plan_split_partials(GemmPlan& p, int max_splits, long long part_stride) {
+  if (!p.swap || p.epi != EPI_F32) return 1;
+  const int sms = num_sms();
+  const int tiles = p.args.m_tiles * p.args.n_tiles;
+  int S = sms / tiles;
+  if (S > max_splits) S = max_splits;
+  if (S > p.args.num_kb / 4) S = p.args.num_kb / 4;
+  if (S < 2) return 1;
+  int kbs = (p.args.num_kb + S - 1) / S;
+  while (S > 1 && (S - 1) * kbs >= p.args.num_kb) {   // every split owns k-blocks
+    --S;
+    kbs = (p.args.num_kb + S - 1) / S;
+  }
+  if (S < 2) return 1;
+  p.args.part_splits = S;
+  p.args.part_kbs = kbs;
+  p.args.part_stride = part_stride;
+  p.args.dp_tiles = 0;
+  p.args.sk_tiles = 0;
+  p.grid = tiles * S < sms ? tiles * S : sms;
+  return S;
+}
+
 bool finalize_plan(GemmPlan& p, const void* A, int lda, const void* B, int ldb, void* out, int ldc,
                    const __nv_bfloat16* residual, int ld_res, float* workspace, int* counters, uint64_t a_rows,
                    uint64_t b_rows) {

@@ -65,11 +65,14 @@ __host__ __device__ __forceinline__ int kv_page_slot(const KVGeom& g, int key) {
 }
 
 void embed(const int* tokens, const __nv_bfloat16* table, __nv_bfloat16* out, int T, int H, int V, cudaStream_t s);
+// x[row] += add[row] (if given) + sum of the split-K partial slots
+// parts[p * pstride + row * H] (if given); y[r] = rmsnorm(x[rows[r]]) * w.
 void rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* add, const __nv_bfloat16* w, __nv_bfloat16* y,
-             const int* rows, int R, int H, float eps, cudaStream_t s);
+             const int* rows, int R, int H, float eps, cudaStream_t s, const float* parts = nullptr,
+             int nparts = 0, long long pstride = 0);
 void rope_append(__nv_bfloat16* qkv, const int* positions, const int* pages, const int* slots,
                  const float* cos_sin, const KVGeom& g, int layer, int T, int nq, int nkv, int max_pos,
-                 cudaStream_t s);
+                 cudaStream_t s, const float* parts = nullptr, int nparts = 0, long long pstride = 0);
 void sample(const float* logits, int B, int V, int ld, const float* temp, const unsigned* seeds,
             unsigned long long step, int* out, cudaStream_t s);
 void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off, const long long* src_off, int n,

@@ -52,6 +52,21 @@ def test_gemm_stream_k_workspace_returns_to_zero(C):
     check_error()
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (16, 6144, 4096), (64, 4096, 14336), (128, 4096, 4096), (37, 1024, 512)])
+def test_gemm_split_partials_sum_to_product(C, M, N, K):
+    torch.manual_seed(7)
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    parts = torch.full((16, M, N), float("nan"), device="cuda")
+    S = C.gemm_partials(A, B, parts, 16)
+    torch.cuda.synchronize()
+    assert S >= 1
+    got = parts[:S].sum(0)
+    assert _rel(got, A.float() @ B.float().t()) < 1e-2
+    from kunserve_b200.ops import check_error
+    check_error()
+
+
 def test_gemm_f32_add_silu(C):
     torch.manual_seed(1)
     M, K, F = 37, 512, 384
