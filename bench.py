@@ -284,6 +284,7 @@ def main():
     clocks = ClockSampler(list(range(world)) if rank == 0 else [])
     barrier_sync()
     launches0, h2d0, d2h0, steps0 = runner.eng.launches(), runner.h2d_bytes, runner.d2h_bytes, runner.num_steps
+    gpu0 = runner.gpu_ms
     if rank == 0:
         clocks.start()
 
@@ -306,6 +307,7 @@ def main():
     ttft, tpot, ok = summarize(records, t0 + dev_ms / 1000.0, args.ttft_slo, args.tpot_slo)
     preempt = inst.get_num_preemption()
     local_res = {"dev_ms": dev_ms, "ttft": ttft, "tpot": tpot, "ok": ok, "launches": launches,
+                 "fwd_gpu_ms": runner.gpu_ms - gpu0,
                  "h2d": h2d, "d2h": d2h, "n_steps": n_steps, "preempt": preempt,
                  "finished": sum(1 for a, tt, fin in records if fin and tt and tt[-1] <= t0 + dev_ms / 1000.0),
                  "arrived": sum(1 for r in trace if r.arrival <= dev_ms / 1000.0)}
@@ -384,6 +386,9 @@ def main():
             "finished": sum(r[0]["finished"] for r in allres), "arrived": sum(r[0]["arrived"] for r in allres),
             "preemptions": sum(r[0]["preempt"] for r in allres), "window_s": round(win_s, 3),
             "gpu_launches": int(sum(r[0]["launches"] for r in allres)),
+            # share of the window the device spent inside forward() (the rest is
+            # host-side scheduling between steps and idle time between arrivals)
+            "forward_busy_frac": round(max(r[0]["fwd_gpu_ms"] / r[0]["dev_ms"] for r in allres), 3),
             "clocks": clock_info,
         }
         if e2e_res is not None:

@@ -70,14 +70,16 @@ def main(argv=None):
             w.step(step)
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0 = w.runner.gpu_ms
         s.record()
         for _ in range(a.iters):
             w.step(step)
         e.record()
         torch.cuda.synchronize()
         ms = s.elapsed_time(e) / a.iters
+        fwd_ms = (w.runner.gpu_ms - g0) / a.iters
         row = {"mode": a.mode, "model": a.model, "batch": B, ("ctx" if a.mode == "decode" else "len"): n,
-               "ms_per_step": round(ms, 3)}
+               "ms_per_step": round(ms, 3), "forward_gpu_ms": round(fwd_ms, 3)}
         if a.mode == "decode":
             kv = B * (n + 1) * L * arch.num_key_value_heads * hd * 2 * 2
             roof = (wbytes + kv) / bw * 1e3

@@ -130,6 +130,8 @@ class NativeRunner:
         self.num_sms = C.num_sms()
         self.ext_pages = 0
         self.fusion_size = 1
+        self.gpu_ms = 0.0      # device time inside forward(), summed over steps
+        self._ev = None
         self.peer_maps = {}
         self.h2d_bytes = 0
         self.d2h_bytes = 0
@@ -185,11 +187,11 @@ class NativeRunner:
 
     def _dec_splits(self, n_dec: int, max_ctx: int) -> int:
         """Key splits per decode request: enough CTAs to fill the GPU a few
-        times over, at least 256 keys per split, within the scratch."""
+        times over, at least two 64-key blocks per split, within the scratch."""
         if n_dec == 0:
             return 1
         want = math.ceil(4 * self.num_sms / (n_dec * self.shape.nkv))
-        return int(max(1, min(32, want, max_ctx // 256, DEC_SPLIT_SLOTS // n_dec)))
+        return int(max(1, min(32, want, max_ctx // 128, DEC_SPLIT_SLOTS // n_dec)))
 
     def _splits(self, T: int, n_items: int, max_ctx: int) -> int:
         if T > ATTN_SPLIT_TOKENS:
@@ -212,8 +214,16 @@ class NativeRunner:
         if last_stage and step.top_k is not None and (any(k > 0 for k in step.top_k) or
                                                       any(p < 1.0 for p in (step.top_p or []))):
             sample_mode = 1
+        if self._ev is None:
+            self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        self._ev[0].record()
         out = self.eng.forward(self.meta, T, B, width, n_items, splits, n_dec, dec_splits, step.layer_start,
                                step.layer_end, step.fusion_size, first, last_stage, sample_mode, step.step_id)
+        # the forward returned after its device work (it reads the sampled ids
+        # back), so this bracket is the step's time on the GPU
+        self._ev[1].record()
+        self._ev[1].synchronize()
+        self.gpu_ms += self._ev[0].elapsed_time(self._ev[1])
         self.num_steps += 1
         self.h2d_bytes += 4 * n
         if last_stage and sample_mode == 0:
