@@ -103,7 +103,8 @@ def bench_attention(args):
             ctxl = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
             tab = torch.tensor(tables, dtype=torch.int32, device="cuda")
             if n_dec:
-                splits = int(max(1, min(32, math.ceil(4 * 148 / (n_dec * nkv)), ctx // 128, 1024 // n_dec)))
+                min_keys = 128 if n_dec * nkv < 64 else 256
+                splits = int(max(1, min(32, math.ceil(4 * 148 / (n_dec * nkv)), ctx // min_keys, 1024 // n_dec)))
             else:
                 splits = 1
             if args.splits > 0:

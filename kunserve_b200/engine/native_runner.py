@@ -187,11 +187,14 @@ class NativeRunner:
 
     def _dec_splits(self, n_dec: int, max_ctx: int) -> int:
         """Key splits per decode request: enough CTAs to fill the GPU a few
-        times over, at least two 64-key blocks per split, within the scratch."""
+        times over, at least 256 keys per split (128 when there are fewer
+        than 64 request-head pairs), within the scratch."""
         if n_dec == 0:
             return 1
-        want = math.ceil(4 * self.num_sms / (n_dec * self.shape.nkv))
-        return int(max(1, min(32, want, max_ctx // 128, DEC_SPLIT_SLOTS // n_dec)))
+        pairs = n_dec * self.shape.nkv
+        want = math.ceil(4 * self.num_sms / pairs)
+        min_keys = 128 if pairs < 64 else 256
+        return int(max(1, min(32, want, max_ctx // min_keys, DEC_SPLIT_SLOTS // n_dec)))
 
     def _splits(self, T: int, n_items: int, max_ctx: int) -> int:
         if T > ATTN_SPLIT_TOKENS:
