@@ -19,6 +19,7 @@ from ..engine.instance import InstanceEngine
 from ..request import Request
 from ..utils.logger import init_logger
 from ..utils.misc import EngineState, Event
+from ..utils.trace import nvtx_range
 
 logger = init_logger(__name__)
 
@@ -120,6 +121,10 @@ class GroupEngine:
 
     # ------------------------------------------------------- transitions
     async def trigger_balloon(self, from_restore: bool = False) -> int:
+        with nvtx_range(f"kunserve.group{self.group_id}.balloon"):
+            return await self._trigger_balloon(from_restore)
+
+    async def _trigger_balloon(self, from_restore: bool) -> int:
         t0 = time.perf_counter()
         prev = self.state
         self.state = EngineState.STOP
@@ -132,6 +137,10 @@ class GroupEngine:
         return int(free * self.max_balloon_memory_ratio)
 
     async def trigger_restore(self) -> None:
+        with nvtx_range(f"kunserve.group{self.group_id}.restore"):
+            await self._trigger_restore()
+
+    async def _trigger_restore(self) -> None:
         t0 = time.perf_counter()
         leader = self.leader
         await leader.reclaim_extra_blocks()
@@ -146,6 +155,10 @@ class GroupEngine:
         logger.info(f"group {self.group_id}: BALLOON -> RESTORE in {dt:.3f}s")
 
     async def trigger_init(self) -> None:
+        with nvtx_range(f"kunserve.group{self.group_id}.init"):
+            await self._trigger_init()
+
+    async def _trigger_init(self) -> None:
         t0 = time.perf_counter()
         self.state = EngineState.STOP
         await self.stop_all_engines()

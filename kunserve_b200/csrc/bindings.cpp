@@ -103,7 +103,8 @@ KVGeom make_geom(torch::Tensor pool, int64_t P, int64_t N, int64_t Ls, int64_t L
   g.block_size = (int)block_size;
   g.kvh = (int)kvh;
   g.hd = (int)hd;
-  finish_geom(g);
+  const long long pool_bytes = (long long)pool.numel() * pool.element_size();
+  finish_geom(g, std::max<long long>(0, pool_bytes - (long long)P * g.page_stride));
   return g;
 }
 
@@ -299,6 +300,16 @@ void tp_allgather_gemm_op(torch::Tensor B, torch::Tensor out, std::vector<int64_
   run_gemm(p, st);
 }
 
+// The reduce half of the fused all-reduce on its own (tests): waits for
+// every flags[q] >= epoch (bounded), then h += sum of the R slots of rb.
+void tp_reduce_op(int64_t rb_ptr, int64_t R, int64_t slot_elems, torch::Tensor h, int64_t flags_ptr, int64_t epoch) {
+  CHECK_CUDA_BF16(h);
+  c10::cuda::CUDAGuard g(h.device());
+  tp_reduce_rmsnorm(reinterpret_cast<const __nv_bfloat16*>(rb_ptr), (int)R, slot_elems, bp(h), nullptr, bp(h),
+                    (int)h.size(0), (int)h.size(1), 1e-5f, reinterpret_cast<const unsigned*>(flags_ptr),
+                    (unsigned)epoch, at::cuda::getCurrentCUDAStream());
+}
+
 void fill_normal_op(torch::Tensor t, int64_t seed, double std) {
   CHECK_CUDA_BF16(t);
   c10::cuda::CUDAGuard g(t.device());
@@ -386,6 +397,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_allgather_gemm", &tp_allgather_gemm_op);
   m.def("tp_signal", &tp_signal_op);
   m.def("gemm_partials", &gemm_partials_op);
+  m.def("tp_reduce", &tp_reduce_op);
+  m.def("raise_error_flag", &raise_error_flag, "host-side fault injection: set the device error flag");
   m.def("num_sms", &num_sms);
   m.attr("EPI_BF16") = (int)EPI_BF16;
   m.attr("EPI_F32") = (int)EPI_F32;

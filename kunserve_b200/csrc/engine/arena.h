@@ -54,6 +54,8 @@ class Arena {
   size_t kv_base_bytes() const { return kv_base_bytes_; }
   // whole reserved KV range: base pages plus room for every layer's extend pages
   size_t kv_va_bytes() const { return kv_va_bytes_; }
+  // bytes mapped after the base pages: padding plus the dropped layers' memory
+  size_t after_base_bytes() const { return ext_bytes_ + (kv_phys_bytes_ - kv_base_bytes_); }
   size_t granularity() const { return gran_; }
   size_t layer_bytes(int l) const { return segs_[l].bytes; }
   int num_layers() const { return (int)segs_.size(); }

@@ -6,9 +6,19 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include <cmath>
+#include <cstdio>
 #include <stdexcept>
 
+#include <nvtx3/nvToolsExt.h>
+
 namespace kus {
+
+// NVTX range for the lifetime of a scope (visible under Nsight Systems; the
+// header-only NVTX 3 calls are no-ops when no tool is attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+};
 
 #define KUS_CHECK(cond, msg)                                        \
   do {                                                              \
@@ -89,6 +99,7 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
                             B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + 64;
   meta_dev_ = torch::empty({meta_ints}, i32);
   tokens_dev_ = torch::empty({B}, i32);
+  err_host_ = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).pinned_memory(true));
   tokens_host_ = torch::empty({B}, torch::TensorOptions().dtype(torch::kInt32).pinned_memory(true));
   // RoPE table: [max_pos, hd] = cos (hd/2) then sin (hd/2), computed in double
   auto cs = torch::empty({s.max_pos, s.hd}, torch::kFloat32);
@@ -279,6 +290,20 @@ int Engine::gemm_partials(const CUtensorMap* mA, const WMap& mB, int M, int N, i
   return S;
 }
 
+void Engine::fail_on_device_error() {
+  const int code = *err_host_.data_ptr<int>();
+  if (code == 0) return;
+  // a kernel gave up on a wait (or failed a bounds check): peers must not
+  // block on this rank's collectives, so the TP communicator is aborted
+  if (tp_comm_ != nullptr) {
+    ncclCommAbort(tp_comm_);
+    tp_comm_ = nullptr;
+  }
+  const long long e = error_flag(false);
+  throw std::runtime_error("device error flag set during the step: code " + std::to_string(e & 0xff) + " info " +
+                           std::to_string(e >> 8) + " (1-4: pipeline wait timed out, 5: peer flag, 6: bounds)");
+}
+
 void Engine::debug_check(const char* what, int a, int b, int c, cudaStream_t st) {
   check_cuda(cudaStreamSynchronize(st), what);
   const long long e = error_flag(false);
@@ -296,6 +321,10 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
                                      int64_t splits, int64_t n_dec, int64_t dec_splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
                                      bool first_stage, bool last_stage, int64_t sample_mode, int64_t step) {
   c10::cuda::CUDAGuard g(device_);
+  char range_name[96];
+  std::snprintf(range_name, sizeof(range_name), "kunserve.forward T=%lld B=%lld dec=%lld layers=[%lld,%lld)",
+                (long long)T, (long long)B, (long long)n_dec, (long long)layer_start, (long long)layer_end);
+  NvtxRange range_fwd(range_name);
   KUS_CHECK(T > 0 && T <= s_.max_tokens, "step tokens exceed max_tokens");
   KUS_CHECK(B > 0 && B <= s_.max_batch, "step requests exceed max_batch");
   KUS_CHECK(layer_start >= 0 && layer_end <= s_.layers && layer_start < layer_end, "bad layer slice");
@@ -333,7 +362,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   geo.block_size = s_.block_size;
   geo.kvh = s_.nkv;
   geo.hd = s_.hd;
-  finish_geom(geo);
+  finish_geom(geo, (long long)arena_->after_base_bytes());
 
   AttnBatch ab;
   ab.q_start = q_start;
@@ -383,6 +412,9 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     for (int d : dropped) KUS_CHECK(d != l, "step touches a dropped layer");
     const LayerW& W = layers_[l];
     const int ll = (int)(l - layer_start);
+    char layer_name[32];
+    std::snprintf(layer_name, sizeof(layer_name), "layer %lld", (long long)l);
+    NvtxRange range_layer(layer_name);
     if (!y_ready)
       rmsnorm(h, pending ? tmp : nullptr, W.in_norm, y, nullptr, (int)T, H, (float)s_.eps, st,
               pend_parts ? part : nullptr, pend_parts, (long long)T * H);
@@ -446,24 +478,33 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
           (float)s_.eps, st, pend_parts ? part : nullptr, pend_parts, (long long)T * H);
   ++launches_;
   gemm(m_ylast_, m_lm_head_, (int)B, s_.vocab, H, EPI_F32, logits_.data_ptr(), s_.vocab, nullptr, st);
-  if (sample_mode == 1) return out;   // caller samples from logits()
+  if (sample_mode == 1) {   // caller samples from logits(); still surface device errors
+    read_error_async(err_host_.data_ptr<int>(), st);
+    check_cuda(cudaStreamSynchronize(st), "step sync");
+    fail_on_device_error();
+    return out;
+  }
   sample(logits_.data_ptr<float>(), (int)B, s_.vocab, s_.vocab, temps, seeds, (unsigned long long)step,
          tokens_dev_.data_ptr<int>(), st);
   ++launches_;
   check_cuda(cudaMemcpyAsync(tokens_host_.data_ptr(), tokens_dev_.data_ptr(), B * 4, cudaMemcpyDeviceToHost, st),
              "tokens D2H");
+  read_error_async(err_host_.data_ptr<int>(), st);
   check_cuda(cudaStreamSynchronize(st), "step sync");
+  fail_on_device_error();
   const int* th = tokens_host_.data_ptr<int>();
   out.assign(th, th + B);
   return out;
 }
 
 int64_t Engine::drop_layers(const std::vector<int64_t>& layers) {
+  NvtxRange range("kunserve.pmm_drop");
   std::vector<int> ls(layers.begin(), layers.end());
   return (int64_t)arena_->drop_layers(ls);
 }
 
 std::vector<int64_t> Engine::restore_layers() {
+  NvtxRange range("kunserve.pmm_restore.remap");
   auto r = arena_->restore_layers();
   for (int l : r) build_layer_maps(l);
   return std::vector<int64_t>(r.begin(), r.end());

@@ -148,6 +148,8 @@ class Engine {
   bool pdl_ = true;
   // KUNSERVE_SPLITK_PARTIALS=0 keeps decode GEMMs on whole tiles / stream-K
   bool parts_ = true;
+  torch::Tensor err_host_;   // pinned copy of the device error code, read with every step's ids
+  void fail_on_device_error();
   static constexpr int kMaxPartSlots = 16;
   torch::Tensor part_ws_;
   // Decode-sized GEMM as split-K fp32 partial slots in part_ws_ (slot s at

@@ -13,6 +13,15 @@
 namespace kus {
 void set_pdl(bool on) { pdl_flag() = on; }
 
+void read_error_async(int* host_pinned, cudaStream_t s) {
+  cudaMemcpyFromSymbolAsync(host_pinned, g_kus_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+}
+
+void raise_error_flag(int code, int info) {
+  cudaMemcpyToSymbol(g_kus_error, &code, sizeof(int));
+  cudaMemcpyToSymbol(g_kus_error_info, &info, sizeof(int));
+}
+
 long long error_flag(bool reset) {
   int code = 0, info = 0;
   cudaMemcpyFromSymbol(&code, g_kus_error, sizeof(int));

@@ -152,6 +152,11 @@ __global__ void rope_append_kernel(__nv_bfloat16* __restrict__ qkv, const int* _
   __nv_bfloat16* src = qkv + ((size_t)t * heads + h) * hd;
   const float* psrc = parts ? parts + ((size_t)t * heads + h) * hd : nullptr;
   const int page = pages[t], slot = slots[t];
+  // KV writes are the one place a bad page id corrupts memory: check it
+  if (h >= nq && (page < 0 || page >= g.pages_total || slot < 0 || slot >= g.block_size)) {
+    if (lane == 0) set_error(kErrBounds, page);
+    return;
+  }
   if (h >= nq + nkv) {
     __nv_bfloat16* dst = kv_ptr(g, page, layer, true) + ((size_t)slot * g.kvh + (h - nq - nkv)) * hd;
     if (lane < hd / 8) {

@@ -21,11 +21,13 @@ struct KVGeom {
   int hd;
   int spp;                // layer slots per physical page (page_stride / layer_stride)
   int bs_shift;           // log2(block_size) when it is a power of two, else -1
+  int pages_total;        // valid page ids are [0, pages_total): fused ids plus extend pages
 };
 
 // Fill the derived fields of a geometry whose other fields are set.
-inline void finish_geom(KVGeom& g) {
+inline void finish_geom(KVGeom& g, long long extend_bytes = 0) {
   g.spp = (int)(g.page_stride / g.layer_stride);
+  g.pages_total = g.N * g.P + (int)(extend_bytes / ((long long)g.Ls * g.layer_stride));
   g.bs_shift = -1;
   for (int s = 0; s < 31; ++s)
     if ((1 << s) == g.block_size) g.bs_shift = s;
@@ -142,4 +144,8 @@ long long error_flag(bool reset);
 // Launches of forward-pass kernels from this host thread carry programmatic
 // stream serialization (the next kernel starts while the previous drains).
 void set_pdl(bool on);
+// Stream-ordered copy of the device error code into pinned host memory.
+void read_error_async(int* host_pinned, cudaStream_t s);
+// Host-side fault injection for tests: set the device error flag.
+void raise_error_flag(int code, int info);
 }  // namespace kus
