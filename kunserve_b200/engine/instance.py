@@ -109,7 +109,6 @@ class InstanceEngine(AdmissionMixin):
         self.event_log: List[Tuple[float, str, float]] = []  # (time, event, seconds)
         self._loop_task: Optional[asyncio.Task] = None
         # per VE scheduler: was its next batch prepared after its last step?
-        self._prepared: Dict[int, bool] = {}
 
     # ------------------------------------------------------------ set-up
     def _new_scheduler(self) -> ColocatedScheduler:
@@ -278,12 +277,12 @@ class InstanceEngine(AdmissionMixin):
             resharding: List[Request] = []
             if ve < len(self.is_resharding) and self.is_resharding[ve]:
                 resharding = await self._live_reshard_prepare(ve)
-            if not self._prepared.get(id(self.scheduler[ve]), False):
+            if not self.scheduler[ve].next_batch_prepared:
                 # a transition stopped the previous step before it prepared
                 # this VE's next batch (page growth, admission): do it now
                 async with self.allocate_lock:
                     await self._get_next_batch(ve)
-            self._prepared[id(self.scheduler[ve])] = False
+            self.scheduler[ve].next_batch_prepared = False
             batch, _ = self.scheduler[ve].schedule(prefill_only_chunk=True)
             batch.set_sched_time()
             pipe, replica = batch.get_fusion_requests()
@@ -365,7 +364,7 @@ class InstanceEngine(AdmissionMixin):
         if self.stopped:
             return
         s = self.scheduler[ve]
-        self._prepared[id(s)] = True
+        s.next_batch_prepared = True
         for r in s.pop_finished_requests():
             self._free_blocks(r)
         # 1. grow the running requests; preempt on shortage
@@ -553,6 +552,7 @@ class InstanceEngine(AdmissionMixin):
             for r in s.running_queue.requests + list(s.swapped_queue) + list(s.waiting_queue):
                 r.kv_fusion_rank = rank
             s.block_managers = self.block_managers
+            s.next_batch_prepared = False
             self.scheduler.append(s)
             self.scheduler_running.append(False)
             self.is_resharding.append(False)
@@ -581,6 +581,7 @@ class InstanceEngine(AdmissionMixin):
             for s in other.scheduler:
                 s.block_managers = other.block_managers
                 s.is_fusion_state = False
+                s.next_batch_prepared = False
                 for r in s.all_requests():
                     r.kv_fusion_rank = 0
                     r.fusion_exec = False
@@ -596,6 +597,7 @@ class InstanceEngine(AdmissionMixin):
         for s in self.scheduler:
             s.block_managers = self.block_managers
             s.is_fusion_state = False
+            s.next_batch_prepared = False
             for r in s.all_requests():
                 r.fusion_exec = False
                 r.kv_fusion_rank = 0

@@ -41,6 +41,10 @@ class ColocatedScheduler:
         self.num_pending_prefill_tokens = 0
         self.num_preemption = 0
         self.is_fusion_state = False
+        # the owning instance grew this VE's running requests for the next
+        # step (page growth, admission); travels with the VE across
+        # merge/split so a new owner never trusts another's bookkeeping
+        self.next_batch_prepared = False
 
     # ------------------------------------------------------------- queues
     def _blocks(self, n_tokens: int) -> int:
