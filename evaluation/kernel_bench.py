@@ -75,7 +75,7 @@ def bench_gemm(args, cublas=False):
 
 
 def bench_attention(args):
-    from kunserve_b200.engine.native_runner import pack_meta
+    from kunserve_b200.engine.native_runner import decode_splits, pack_meta, prefill_splits
     from kunserve_b200.engine.step import StepInput
     from kunserve_b200.ops import native
     import numpy as np
@@ -102,18 +102,15 @@ def bench_attention(args):
             q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
             ctxl = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
             tab = torch.tensor(tables, dtype=torch.int32, device="cuda")
-            if n_dec:
-                min_keys = 128 if n_dec * nkv < 64 else 256
-                splits = int(max(1, min(32, math.ceil(4 * 148 / (n_dec * nkv)), ctx // min_keys, 1024 // n_dec)))
-            else:
-                splits = 1
+            splits = decode_splits(n_dec, ctx, nkv, 148) if n_dec else prefill_splits(T, n_items, ctx, nkv, 148)
             if args.splits > 0:
                 splits = args.splits
             out = torch.empty(T, nq * hd, device="cuda", dtype=torch.bfloat16)
             op = torch.empty(max(splits, 1) * T * nq * hd, device="cuda")
             ml = torch.empty(max(splits, 1) * T * nq * 2, device="cuda")
+            psplits = 1 if n_dec else splits
             fn = lambda i: C.attention(q, nq * hd, out, pool, P, 1, L, L, bs, nkv, 0, q_start, ctxl, tab, items,
-                                       1, op, ml, nq, 1 / math.sqrt(hd), dec, splits, op, ml)
+                                       psplits, op, ml, nq, 1 / math.sqrt(hd), dec, splits if n_dec else 1, op, ml)
             t = timeit(fn, args.warmup, args.iters)
             kv_bytes = B * ctx * nkv * hd * 2 * 2
             # causal FLOPs: query i of a request sees (ctx - ql + i + 1) keys; QK^T and PV, 2 FLOP per MAC

@@ -137,14 +137,22 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
   b.dec_reqs = dec_reqs.data_ptr<int>();
   b.n_dec = dec_reqs.numel();
   b.dec_splits = (int)dec_splits;
+  // split-arrival counts of the decode kernel: one zeroed buffer per device,
+  // returned to zero by every launch
+  static torch::Tensor counts[64];
+  const int dev = q.get_device();
+  TORCH_CHECK(dev >= 0 && dev < 64, "attention: bad device");
+  if (!counts[dev].defined())
+    counts[dev] = torch::zeros({(int64_t)kDecCountSlots}, torch::TensorOptions().dtype(torch::kInt32).device(q.device()));
+  TORCH_CHECK((int64_t)dec_reqs.numel() * nkv <= kDecCountSlots, "attention: too many decode requests");
   AttnScratch sc{o_part.data_ptr<float>(), ml_part.data_ptr<float>(), dec_o.data_ptr<float>(),
-                 dec_ml.data_ptr<float>()};
+                 dec_ml.data_ptr<float>(), counts[dev].data_ptr<int>()};
   CUtensorMap tq, tkv, tkv_dec;
   const long long pool_bytes = (long long)pool.numel() * pool.element_size();
   TORCH_CHECK(make_attn_q_map(&tq, q.data_ptr(), (int)q.size(0), (int)nq, (int)q_stride, (int)(nq / nkv)),
               "attention q tensor map");
   TORCH_CHECK(make_attn_kv_map(&tkv, pool.data_ptr(), pool_bytes, (int)nkv, (int)block_size,
-                               attention_q_rows_per_tile()),
+                               attention_kv_block_keys()),
               "attention kv tensor map");
   TORCH_CHECK(make_attn_kv_map(&tkv_dec, pool.data_ptr(), pool_bytes, (int)nkv, (int)block_size,
                                decode_attention_block_keys()),

@@ -94,6 +94,7 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   attn_ml_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * 2}, f32);
   dec_o_ = torch::empty({kDecSplitSlots * s.nq * s.hd}, f32);
   dec_ml_ = torch::empty({kDecSplitSlots * s.nq * 2}, f32);
+  dec_count_ = torch::zeros({(int64_t)kDecCountSlots}, i32);
   const int64_t max_items = T * std::max(1, s.nq / s.nkv) / 64 + B + 1;
   const int64_t meta_ints = 2 * max_items + 4 * T + 5 * B + 1 +
                             B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + 64;
@@ -155,7 +156,7 @@ void Engine::init_memory(int64_t num_pages) {
   }
   check_cuda(cudaMemset(arena_->kv_base(), 0, arena_->kv_phys_bytes()), "zero kv");
   KUS_CHECK(make_attn_kv_map(&m_attn_kv_, arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv, s_.block_size,
-                             attention_q_rows_per_tile()),
+                             attention_kv_block_keys()),
             "tmap attention kv");
   KUS_CHECK(make_attn_kv_map(&m_dec_kv_, arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv, s_.block_size,
                              decode_attention_block_keys()),
@@ -300,6 +301,8 @@ void Engine::fail_on_device_error() {
     tp_comm_ = nullptr;
   }
   const long long e = error_flag(false);
+  // a kernel that gave up may have left split-arrival counts behind
+  cudaMemset(dec_count_.data_ptr<int>(), 0, dec_count_.numel() * sizeof(int));
   throw std::runtime_error("device error flag set during the step: code " + std::to_string(e & 0xff) + " info " +
                            std::to_string(e >> 8) + " (1-4: pipeline wait timed out, 5: peer flag, 6: bounds)");
 }
@@ -376,7 +379,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   ab.n_dec = (int)n_dec;
   ab.dec_splits = (int)dec_splits;
   AttnScratch sc{attn_o_.data_ptr<float>(), attn_ml_.data_ptr<float>(), dec_o_.data_ptr<float>(),
-                 dec_ml_.data_ptr<float>()};
+                 dec_ml_.data_ptr<float>(), dec_count_.data_ptr<int>()};
 
   const int H = s_.hidden;
   auto* h = reinterpret_cast<__nv_bfloat16*>(h_.data_ptr());

@@ -124,7 +124,7 @@ class Engine {
   WMap m_lm_head_;
   // workspaces
   torch::Tensor h_, y_, qkv_, attn_, act_, tmp_, ylast_, logits_, gemm_ws_, counters_, attn_o_, attn_ml_,
-      meta_dev_, tokens_dev_, tokens_host_, cos_sin_, dec_o_, dec_ml_;
+      meta_dev_, tokens_dev_, tokens_host_, cos_sin_, dec_o_, dec_ml_, dec_count_;
   // activation TMA descriptors per token-box height (16, 32, 64, 128 rows)
   CUtensorMap m_y_[4], m_attn_[4], m_act_[4], m_ylast_[4];
   // prefill attention: queries in qkv_ and the whole reserved KV range

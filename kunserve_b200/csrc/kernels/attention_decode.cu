@@ -13,8 +13,9 @@
 //              registers (the S accumulator layout is the A layout of P V),
 //              then the warps merge (max, sum, O) in shared memory
 //
-// With splits > 1 a CTA writes an unnormalized partial plus (max, sum) and
-// decode_combine_kernel merges the splits.
+// With splits > 1 a CTA writes an unnormalized partial plus (max, sum); the
+// last of a (request, KV head)'s split CTAs to finish, found by an atomic
+// arrival count, merges them and writes the output rows.
 #include "../common.cuh"
 #include "kernels.h"
 
@@ -277,25 +278,57 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       }
     }
   }
-}
-
-__global__ void decode_combine_kernel(AttnBatch b, AttnScratch sc, __nv_bfloat16* __restrict__ out, int nq) {
-  pdl_wait();
-  pdl_trigger();
-  const int di = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
-  const int tok = b.q_start[b.dec_reqs[di]];
-  float M = -INFINITY;
-  for (int s = 0; s < b.dec_splits; ++s) M = fmaxf(M, sc.dec_ml[(((size_t)s * b.n_dec + di) * nq + head) * 2]);
-  float L = 0.f, A = 0.f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < b.dec_splits; ++s) {
-      const size_t idx = ((size_t)s * b.n_dec + di) * nq + head;
-      const float f = exp2f(sc.dec_ml[idx * 2] - M);
-      L += sc.dec_ml[idx * 2 + 1] * f;
-      A += sc.dec_o[idx * HD + d] * f;
-    }
+  if (b.dec_splits == 1) return;
+  // The last split CTA of this (request, KV head) to finish merges the
+  // partials of all splits (G x 128 values each, read from L2): no separate
+  // combine launch.  Every CTA arrives (waits are bounded), so the counter
+  // is back at zero after each launch.
+  __shared__ int last_s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();   // publish this CTA's partial before counting it
+    int* cnt = sc.dec_count + di * g.kvh + kh;
+    const bool last = atomicAdd(cnt, 1) == b.dec_splits - 1;
+    if (last) *cnt = 0;
+    last_s = last;
   }
-  out[(size_t)tok * nq * HD + (size_t)head * HD + d] = f2bf(L > 0.f ? A / L : 0.f);
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  // one warp per head row of the group: lane s holds split s's (max, sum),
+  // lane l accumulates dims 4l..4l+3, all splits' loads in flight
+  const size_t plane = (size_t)b.n_dec * nq;
+  for (int h = warp; h < G; h += kWarps) {
+    const size_t row = (size_t)di * nq + kh * G + h;
+    float m = -INFINITY, l = 0.f;
+    if (lane < b.dec_splits) {
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(sc.dec_ml) + lane * plane + row);
+      m = ml.x;
+      l = ml.y;
+    }
+    float M = m;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float w = M == -INFINITY ? 0.f : exp2f(m - M);
+    float L = l * w;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int sp = 0; sp < b.dec_splits; ++sp) {
+      const float ws = __shfl_sync(0xffffffffu, w, sp);
+      const float4 o4 = __ldcg(reinterpret_cast<const float4*>(sc.dec_o + (sp * plane + row) * HD) + lane);
+      acc.x += ws * o4.x;
+      acc.y += ws * o4.y;
+      acc.z += ws * o4.z;
+      acc.w += ws * o4.w;
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    uint2 u;
+    u.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+    u.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(out + (size_t)tok * nq * HD + (size_t)(kh * G + h) * HD + 4 * lane) = u;
+  }
 }
 
 }  // namespace dec
@@ -314,8 +347,6 @@ void paged_decode_attention(const CUtensorMap& tmKV, const __nv_bfloat16* q, int
   const float sl2 = scale * 1.4426950408889634f;
   launch_k(dec::decode_attn_kernel, dim3(b.n_dec, g.kvh, b.dec_splits), dim3(dec::kThreads), dec::kSmemBytes, s, tmKV,
            q, q_stride, out, g, layer, b, sc, nq, sl2);
-  if (b.dec_splits > 1)
-    launch_k(dec::decode_combine_kernel, dim3(b.n_dec, nq), dim3(dec::HD), 0, s, b, sc, out, nq);
 }
 
 }  // namespace kus

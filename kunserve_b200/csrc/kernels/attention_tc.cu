@@ -1,29 +1,28 @@
 // Paged causal prefill attention on the sm_100a tensor cores (tcgen05).
 //
-// One CTA computes a tile of 128 query rows of one request against one KV
-// head: row r is token r / G, query head r % G of the head's GQA group, so
-// every K/V byte feeds all G heads (G = 1 for multi-head attention).  Keys
-// go in blocks of 128 (whole pages gathered through the page table).
+// One CTA computes 256 query rows of one request against one KV head as two
+// 128-row tiles (A, B) that share every K/V block: row r is token r / G,
+// query head r % G of the head's GQA group, so each K/V byte feeds all G
+// heads of both tiles (G = 1 for multi-head attention).  Keys go in blocks
+// of 64 (whole pages gathered through the page table).
 //
-//   warp 0     TMA producer of the Q tile (once; a 3-D box over
-//              [token][head][dim]) and of K blocks; warp 10 the same for V
-//              blocks.  One box per page and 64-dim half of a block (pages
-//              gathered through the page table, all index math in 32 bits),
-//              128-byte swizzle, two stages each
-//   warp 1     TMEM owner and MMA issuer:  S_j = Q K_j^T  into one of two
-//              S buffers (128 x 128 fp32), then  O += P_j V_j  (V read
-//              MN-major straight from its TMA layout); S_{j+1} is issued
-//              before P_j V_j so the tensor core works during the softmax
-//   warps 2-9  softmax, two threads per query row (TMEM lane = row; warps
-//              w and w+4 share a lane quarter and take keys 0-63 / 64-127 of
-//              each block): the two half-row maxima meet in shared memory,
-//              exp2 in registers, P_j as bf16 into shared memory in the UMMA
-//              K-major layout (each half owns one 64-key swizzle atom), O
-//              rescaled in TMEM (each half owns 64 dims) only when a row's
-//              running max grew by more than 2^8 (the stale max is exact: l
-//              and O share it), then the epilogue O / l
+//   warp 0     TMA producer of the two Q tiles (once; 3-D boxes over
+//              [token][head][dim]) and of K blocks; warp 10 the same for V.
+//              One box per page and 64-dim half (128-byte swizzle), all
+//              paged index math in 32 bits, three stages each
+//   warp 1     TMEM owner and MMA issuer, alternating the tiles:
+//                S_A(i+1), O_A += P_A(i) V(i), S_B(i+1), O_B += P_B(i) V(i)
+//              so one tile's tensor work covers the other tile's softmax
+//              handoff; each tile has two S buffers (128 x 64 fp32) and an
+//              O accumulator (128 x 128) in TMEM; V is read MN-major straight
+//              from its TMA layout
+//   warps 2-5  softmax of tile A, warps 6-9 of tile B: one query row per
+//              thread (TMEM lane = row), the block's 64 scores in registers,
+//              P as bf16 into shared memory in the UMMA K-major layout, O
+//              rescaled in TMEM only when a row max grew by more than 2^8
+//              (the stale max is exact: l and O share it), then O / l
 //
-// Rows of one request only; rows past the request (or past a causal limit)
+// Rows of one request only; rows past the request or past a causal limit
 // are masked.  Long contexts with few tiles split the key range over
 // gridDim.z CTAs whose partial (O, max, sum) a combine kernel merges.  All
 // mbarrier waits are bounded (common.cuh).
@@ -38,23 +37,28 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn();
 namespace fatc {
 
 constexpr int HD = 128;
-constexpr int BM = 128;                 // query rows per CTA
-constexpr int BN = 128;                 // keys per block
-constexpr int kSoftmaxThreads = 256;
+constexpr int BM = 128;                  // rows per Q tile
+constexpr int NT = 2;                    // Q tiles per CTA
+constexpr int ROWS = BM * NT;            // query rows per CTA (work item)
+constexpr int BN = 64;                   // keys per block
 constexpr int kVWarp = 10;
-constexpr int kThreads = 64 + kSoftmaxThreads + 32;
-constexpr int kHalf = 128 * 128;        // one 64-dim half of a 128-row tile (16 KB)
-constexpr int kTile = 2 * kHalf;        // 32 KB
-constexpr int kStages = 2;
+constexpr int kThreads = 11 * 32;
+constexpr int kStages = 3;
+constexpr int kQHalf = BM * 128;         // one 64-dim half of a Q tile (16 KB)
+constexpr int kQTile = 2 * kQHalf;       // 32 KB
+constexpr int kKVHalf = BN * 128;        // one 64-dim half of a K or V block (8 KB)
+constexpr int kKVTile = 2 * kKVHalf;     // 16 KB
+constexpr int kPTile = BM * BN * 2;      // P of one tile: 128 rows x 64 keys bf16 (16 KB)
 constexpr int kQOff = 0;
-constexpr int kKOff = kQOff + kTile;
-constexpr int kVOff = kKOff + kStages * kTile;
-constexpr int kPOff = kVOff + kStages * kTile;
-constexpr int kBarOff = kPOff + kTile;  // 192 KB
-constexpr int kSmemBytes = kBarOff + 4096 + 1024;
+constexpr int kKOff = kQOff + NT * kQTile;
+constexpr int kVOff = kKOff + kStages * kKVTile;
+constexpr int kPOff = kVOff + kStages * kKVTile;
+constexpr int kBarOff = kPOff + NT * kPTile;   // 192 KB
+constexpr int kSmemBytes = kBarOff + 512 + 1024;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO = 256;
-constexpr float kRescaleLog2 = 8.0f;    // keep a stale row max until it is 2^8 too small
+constexpr uint32_t kTileCols = 256;      // per tile: S0 [0,64), S1 [64,128), O [128,256)
+constexpr uint32_t kColO = 128;
+constexpr float kRescaleLog2 = 8.0f;     // keep a stale row max until it is 2^8 too small
 
 KUS_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
   asm volatile(
@@ -105,11 +109,9 @@ struct Bars {
   uint64_t q_full;
   uint64_t k_full[kStages], k_empty[kStages];
   uint64_t v_full[kStages], v_empty[kStages];
-  uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, pv_done;
+  uint64_t s_full[NT][2], s_empty[NT][2];
+  uint64_t p_full[NT], pv_done[NT];
   uint32_t tmem;
-  float red_max[2][2][BM];   // [block parity][key half][row]
-  float red_l[2][BM];
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -131,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ctx = b.ctx_len[req];
   const int start = ctx - n;
   const int rows_total = n * G;
-  const int last_row = min(row0 + BM, rows_total) - 1;
+  const int last_row = min(row0 + ROWS, rows_total) - 1;
   const int kv_end = start + last_row / G + 1;
   const int nblk = (kv_end + BN - 1) / BN;
   const int bps = (nblk + b.splits - 1) / b.splits;
@@ -146,12 +148,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_empty[i], kSoftmaxThreads);
+    for (int x = 0; x < NT; ++x) {
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&bars->s_full[x][i], 1);
+        mbar_init(&bars->s_empty[x][i], BM);
+      }
+      mbar_init(&bars->p_full[x], BM);
+      mbar_init(&bars->pv_done[x], 1);
     }
-    mbar_init(&bars->p_full, kSoftmaxThreads);
-    mbar_init(&bars->pv_done, 1);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(&bars->tmem, kTmemCols);
@@ -169,11 +173,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one_sync() && nb > 0) {
       if (!is_v) {
         prefetch_tmap(&tmQ);
-        mbar_arrive_expect_tx(&bars->q_full, kTile);
-        const int tok0 = qs + row0 / G;
+        mbar_arrive_expect_tx(&bars->q_full, NT * kQTile);
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
-          tma_load_3d(sbase + kQOff + h * kHalf, &tmQ, &bars->q_full, 64 * h, kh * G, tok0);
+        for (int x = 0; x < NT; ++x) {
+          const int tok0 = qs + (row0 + x * BM) / G;
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(sbase + kQOff + x * kQTile + h * kQHalf, &tmQ, &bars->q_full, 64 * h, kh * G, tok0);
+        }
       }
       prefetch_tmap(&tmKV);
       const int* table = b.page_table + (size_t)req * b.max_pages;
@@ -185,14 +192,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t region = sbase + (is_v ? kVOff : kKOff);
       bool ok = true;
       for (int i = 0; i < nb && ok; ++i) {
-        const int s = i & 1;
-        const uint32_t ph = (uint32_t)(i >> 1) & 1u;
+        const int s = i % kStages;
+        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, kErrWaitEmpty)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], kTile);
-        const uint32_t dst = region + s * kTile;
+        mbar_arrive_expect_tx(&full[s], kKVTile);
+        const uint32_t dst = region + s * kKVTile;
         const int key_blk = (blk0 + i) * BN;
         for (int j = 0; j * box < BN; ++j) {
           const int key0 = key_blk + j * box;
@@ -203,12 +210,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int slot0 = in ? kv_page_slot(g, key0) : 0;
           const int row = kv_slot(g, page, layer) * rows_per_slot + v_rows + slot0;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) tma_load_3d(dst + h * kHalf + j * box * 128, &tmKV, &full[s], 64 * h, kh, row);
+          for (int h = 0; h < 2; ++h)
+            tma_load_3d(dst + h * kKVHalf + j * box * 128, &tmKV, &full[s], 64 * h, kh, row);
         }
       }
       // drain: the last uses of each stage must be consumed before exit
       for (int i = max(0, nb - kStages); i < nb && ok; ++i)
-        if (!mbar_wait(&empty[i & 1], (uint32_t)(i >> 1) & 1u, kErrWaitEmpty)) ok = false;
+        if (!mbar_wait(&empty[i % kStages], (uint32_t)(i / kStages) & 1u, kErrWaitEmpty)) ok = false;
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
@@ -217,127 +225,131 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_pv = idesc_bf16_f32(BM, HD) | (1u << 16);   // B (V) MN-major
       bool ok = mbar_wait(&bars->q_full, 0, kErrWaitFull);
       tc_fence_after();
-      auto qk = [&](int i) -> bool {
-        const int s = i & 1;
-        const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-        if (!mbar_wait(&bars->k_full[s], ph, kErrWaitFull)) return false;
-        if (!mbar_wait(&bars->s_empty[s], ph ^ 1u, kErrWaitTmemEmpty)) return false;
+      // S_x(i) = Q_x K(i)^T into S buffer i & 1 of tile x
+      auto qk = [&](int i, int x) -> bool {
+        const int s = i % kStages;
+        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+        if (x == 0 && !mbar_wait(&bars->k_full[s], ph, kErrWaitFull)) return false;
+        const int sb = i & 1;
+        if (!mbar_wait(&bars->s_empty[x][sb], (((uint32_t)i >> 1) & 1u) ^ 1u, kErrWaitTmemEmpty)) return false;
         tc_fence_after();
-        const uint32_t d = tmem + (s ? kColS1 : kColS0);
-        const uint32_t kb = sbase + kKOff + s * kTile;
+        const uint32_t d = tmem + x * kTileCols + sb * BN;
+        const uint32_t kb = sbase + kKOff + s * kKVTile;
+        const uint32_t qb = sbase + kQOff + x * kQTile;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = umma_desc_sw128(sbase + kQOff + (kk >> 2) * kHalf) + (uint64_t)(2 * (kk & 3));
-          const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * kHalf) + (uint64_t)(2 * (kk & 3));
+          const uint64_t a = umma_desc_sw128(qb + (kk >> 2) * kQHalf) + (uint64_t)(2 * (kk & 3));
+          const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * kKVHalf) + (uint64_t)(2 * (kk & 3));
           umma_f16(d, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars->s_full[s]);
-        umma_commit(&bars->k_empty[s]);
+        umma_commit(&bars->s_full[x][sb]);
+        if (x == NT - 1) umma_commit(&bars->k_empty[s]);
         return true;
       };
-      if (ok) ok = qk(0);
-      for (int i = 0; i < nb && ok; ++i) {
-        if (i + 1 < nb && !qk(i + 1)) break;
-        const int s = i & 1;
-        const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-        if (!mbar_wait(&bars->p_full, (uint32_t)i & 1u, kErrWaitFull)) break;
-        if (!mbar_wait(&bars->v_full[s], ph, kErrWaitFull)) break;
+      // O_x += P_x(i) V(i)
+      auto pv = [&](int i, int x) -> bool {
+        const int s = i % kStages;
+        const uint32_t ph = (uint32_t)(i / kStages) & 1u;
+        if (!mbar_wait(&bars->p_full[x], (uint32_t)i & 1u, kErrWaitFull)) return false;
+        if (x == 0 && !mbar_wait(&bars->v_full[s], ph, kErrWaitFull)) return false;
         tc_fence_after();
-        const uint32_t vb = sbase + kVOff + s * kTile;
+        const uint32_t vb = sbase + kVOff + s * kKVTile;
+        const uint32_t pb = sbase + kPOff + x * kPTile;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t a = umma_desc_sw128(sbase + kPOff + (kk >> 2) * kHalf) + (uint64_t)(2 * (kk & 3));
-          const uint64_t bd = umma_desc_sw128_mn(vb + kk * 16 * 128, kHalf, 1024);
-          umma_f16(tmem + kColO, a, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t a = umma_desc_sw128(pb) + (uint64_t)(2 * kk);
+          const uint64_t bd = umma_desc_sw128_mn(vb + kk * 16 * 128, kKVHalf, 1024);
+          umma_f16(tmem + x * kTileCols + kColO, a, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bars->pv_done);
-        umma_commit(&bars->v_empty[s]);
+        umma_commit(&bars->pv_done[x]);
+        if (x == NT - 1) umma_commit(&bars->v_empty[s]);
+        return true;
+      };
+      if (ok) ok = qk(0, 0) && qk(0, 1);
+      for (int i = 0; i < nb && ok; ++i) {
+        if (i + 1 < nb && !qk(i + 1, 0)) break;
+        if (!pv(i, 0)) break;
+        if (i + 1 < nb && !qk(i + 1, 1)) break;
+        if (!pv(i, 1)) break;
       }
     }
   } else {
     // ------------------------------------------- softmax + epilogue warps
+    const int x = (warp - 2) >> 2;          // tile of this warp group
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;     // keys (and O dims) 64*half .. 64*half+63
     const int r = quarter * 32 + lane;
-    const int R = row0 + r;
+    const int R = row0 + x * BM + r;
     const bool valid = R < rows_total;
     const int pos = start + (valid ? R / G : 0);
-    const int pos_min = start + row0 / G;  // no mask needed for blocks entirely at or below it
+    const int pos_min = start + (row0 + x * BM) / G;   // blocks entirely at or below it need no mask
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tcol = tmem + lane_off + x * kTileCols;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int i = 0; i < nb; ++i) {
-      const int s = i & 1;
-      const uint32_t ph = (uint32_t)(i >> 1) & 1u;
-      ok = __all_sync(0xffffffffu, ok && mbar_wait(&bars->s_full[s], ph, kErrWaitTmemFull));
+      const int sb = i & 1;
+      ok = __all_sync(0xffffffffu, ok && mbar_wait(&bars->s_full[x][sb], ((uint32_t)i >> 1) & 1u,
+                                                    kErrWaitTmemFull));
       tc_fence_after();
-      const uint32_t ts = tmem + lane_off + (s ? kColS1 : kColS0) + 64 * half;
-      const int key_base = (blk0 + i) * BN + 64 * half;
-      const bool diag = (blk0 + i) * BN + BN - 1 > pos_min;
-      // pass 1: masked max of the raw scores over this half row
-      float rmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      const int key_base = (blk0 + i) * BN;
+      const bool diag = key_base + BN - 1 > pos_min;
+      // the block's 64 scores of this row, masked, in registers
+      float sv[64];
+      {
         uint32_t v[32];
-        tmem_ld32(ts + 32 * c, v);
-        if (diag) {
+        tmem_ld32(tcol + sb * BN, v);
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            rmax = fmaxf(rmax, key_base + 32 * c + e <= pos ? __uint_as_float(v[e]) : -INFINITY);
-        } else {
+        for (int e = 0; e < 32; ++e) sv[e] = __uint_as_float(v[e]);
+        tmem_ld32(tcol + sb * BN + 32, v);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) rmax = fmaxf(rmax, __uint_as_float(v[e]));
-        }
+        for (int e = 0; e < 32; ++e) sv[32 + e] = __uint_as_float(v[e]);
       }
-      bars->red_max[s][half][r] = rmax;
-      named_barrier(1, kSoftmaxThreads);
-      rmax = fmaxf(rmax, bars->red_max[s][half ^ 1][r]) * scale_log2;
+      tc_fence_before();
+      mbar_arrive(&bars->s_empty[x][sb]);   // S buffer free for S(i + 2)
+      float rmax = -INFINITY;
+      if (diag) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+          if (key_base + e > pos) sv[e] = -INFINITY;
+          rmax = fmaxf(rmax, sv[e]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) rmax = fmaxf(rmax, sv[e]);
+      }
+      rmax *= scale_log2;
       const bool need = rmax > m_used + kRescaleLog2;
       const float m_new = need ? rmax : m_used;
       const float alpha = need ? exp2f(m_used - m_new) : 1.f;
       const float m_ref = m_new == -INFINITY ? 0.f : m_new;
-      // pass 2: P = exp2(S * scale - max) as bf16, half-row sum
       uint32_t pk[32];
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        tmem_ld32(ts + 32 * c, v);
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float p0 = exp2f(fmaf(__uint_as_float(v[e]), scale_log2, -m_ref));
-          float p1 = exp2f(fmaf(__uint_as_float(v[e + 1]), scale_log2, -m_ref));
-          if (diag) {
-            const int key = key_base + 32 * c + e;
-            p0 = key <= pos ? p0 : 0.f;
-            p1 = key + 1 <= pos ? p1 : 0.f;
-          }
-          sum += p0 + p1;
-          pk[16 * c + e / 2] = pack_bf16x2(p0, p1);
-        }
+      for (int e = 0; e < 64; e += 2) {
+        const float p0 = exp2f(fmaf(sv[e], scale_log2, -m_ref));
+        const float p1 = exp2f(fmaf(sv[e + 1], scale_log2, -m_ref));
+        sum += p0 + p1;
+        pk[e / 2] = pack_bf16x2(p0, p1);
       }
-      tc_fence_before();
-      mbar_arrive(&bars->s_empty[s]);
       if (i > 0) {
-        // P_{i-1} V_{i-1} finished: the P buffer is free and O is stable
-        ok = __all_sync(0xffffffffu, ok && mbar_wait(&bars->pv_done, (uint32_t)(i - 1) & 1u, kErrWaitTmemFull));
+        // P_x(i-1) V(i-1) finished: the P buffer is free and O is stable
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(&bars->pv_done[x], (uint32_t)(i - 1) & 1u, kErrWaitTmemFull));
         tc_fence_after();
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
-            const uint32_t to = tmem + lane_off + kColO + 64 * half + 32 * c;
-            tmem_ld32(to, o);
+            tmem_ld32(tcol + kColO + 32 * c, o);
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(to, o);
+            tmem_st32(tcol + kColO + 32 * c, o);
           }
         }
       }
       l = l * alpha + sum;
       m_used = m_new;
-      // P row r, keys 64*half.. : one 128-byte swizzle atom row of P half `half`
-      uint8_t* prow = smem + kPOff + half * kHalf + r * 128;
+      // P row r: 64 keys = one 128-byte swizzle-atom row of this tile's P
+      uint8_t* prow = smem + kPOff + x * kPTile + r * 128;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint4 u = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
@@ -345,25 +357,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
-      mbar_arrive(&bars->p_full);
+      mbar_arrive(&bars->p_full[x]);
     }
-    // epilogue: both halves' sums, then this half's 64 output dims
-    bars->red_l[half][r] = l;
-    named_barrier(1, kSoftmaxThreads);
-    l += bars->red_l[half ^ 1][r];
+    // epilogue
     if (nb > 0) {
-      ok = __all_sync(0xffffffffu, ok && mbar_wait(&bars->pv_done, (uint32_t)(nb - 1) & 1u, kErrWaitTmemFull));
+      ok = __all_sync(0xffffffffu, ok && mbar_wait(&bars->pv_done[x], (uint32_t)(nb - 1) & 1u, kErrWaitTmemFull));
       tc_fence_after();
     }
     const int tok = qs + (valid ? R / G : 0);
     const int head = kh * G + (valid ? R % G : 0);
     if (b.splits == 1) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = out + ((size_t)tok * nq + head) * HD + 64 * half;
+      __nv_bfloat16* dst = out + ((size_t)tok * nq + head) * HD;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        if (nb > 0) tmem_ld32(tmem + lane_off + kColO + 64 * half + 32 * c, o);
+        if (nb > 0) tmem_ld32(tcol + kColO + 32 * c, o);
         if (valid && nb > 0 && ok) {
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
@@ -378,11 +387,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
       const size_t idx = ((size_t)split * T + tok) * nq + head;
-      float* dst = sc.o_part + idx * HD + 64 * half;
+      float* dst = sc.o_part + idx * HD;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        if (nb > 0) tmem_ld32(tmem + lane_off + kColO + 64 * half + 32 * c, o);
+        if (nb > 0) tmem_ld32(tcol + kColO + 32 * c, o);
         if (valid) {
 #pragma unroll
           for (int e = 0; e < 32; e += 4) {
@@ -393,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (valid && half == 0) *reinterpret_cast<float2*>(sc.ml_part + idx * 2) = make_float2(m_used, l);
+      if (valid) *reinterpret_cast<float2*>(sc.ml_part + idx * 2) = make_float2(m_used, l);
     }
   }
   tc_fence_before();
@@ -401,27 +410,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-__global__ void combine_kernel(const AttnScratch sc, __nv_bfloat16* __restrict__ out, int T, int nq, int splits) {
+// Merge of the key splits: one warp per (token, head) row, lane l holding
+// dims 4l..4l+3; lane s reads split s's (max, sum), so every split's loads
+// are in flight at once.  splits <= 32.
+__global__ void __launch_bounds__(256) combine_kernel(const AttnScratch sc, __nv_bfloat16* __restrict__ out, int T,
+                                                      int nq, int splits) {
   pdl_wait();
   pdl_trigger();
-  const int tok = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
-  float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, sc.ml_part[(((size_t)s * T + tok) * nq + head) * 2]);
-  float L = 0.f, acc = 0.f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < splits; ++s) {
-      const size_t idx = ((size_t)s * T + tok) * nq + head;
-      const float w = exp2f(sc.ml_part[idx * 2] - M);
-      L += sc.ml_part[idx * 2 + 1] * w;
-      acc += sc.o_part[idx * HD + d] * w;
-    }
+  const int lane = threadIdx.x % 32;
+  const size_t plane = (size_t)T * nq;
+  const size_t row = (size_t)blockIdx.x * 8 + threadIdx.x / 32;   // token * nq + head
+  if (row >= plane) return;
+  float m = -INFINITY, l = 0.f;
+  if (lane < splits) {
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(sc.ml_part) + lane * plane + row);
+    m = ml.x;
+    l = ml.y;
   }
-  out[((size_t)tok * nq + head) * HD + d] = f2bf(L > 0.f ? acc / L : 0.f);
+  float M = m;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  const float w = M == -INFINITY ? 0.f : exp2f(m - M);
+  float L = l * w;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int s = 0; s < splits; ++s) {
+    const float ws = __shfl_sync(0xffffffffu, w, s);
+    const float4 o = __ldcg(reinterpret_cast<const float4*>(sc.o_part + (s * plane + row) * HD) + lane);
+    acc.x += ws * o.x;
+    acc.y += ws * o.y;
+    acc.z += ws * o.z;
+    acc.w += ws * o.w;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  uint2 u;
+  u.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+  u.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(out + row * HD + 4 * lane) = u;
 }
 
 }  // namespace fatc
 
-int attention_q_rows_per_tile() { return fatc::BM; }
+int attention_q_rows_per_tile() { return fatc::ROWS; }
+int attention_kv_block_keys() { return fatc::BN; }
 
 bool make_attn_q_map(CUtensorMap* map, const void* q, int tokens, int nq, int q_stride, int group) {
   auto fn = gemm_impl::get_encode_fn();
@@ -474,7 +507,8 @@ void paged_prefill_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, __
   launch_k(fatc::fa_kernel, dim3(b.n_items, g.kvh, b.splits), dim3(fatc::kThreads), fatc::kSmemBytes, s, tmQ, tmKV,
            out, g, layer, b, sc, T, nq, scale_log2);
   if (b.splits > 1)
-    launch_k(fatc::combine_kernel, dim3(T, nq), dim3(fatc::HD), 0, s, sc, out, T, nq, b.splits);
+    launch_k(fatc::combine_kernel, dim3((unsigned)(((size_t)T * nq + 7) / 8)), dim3(256), 0, s, sc, out, T, nq,
+             b.splits);
 }
 
 }  // namespace kus

@@ -110,7 +110,9 @@ struct AttnScratch {
   float* ml_part;         // [splits, T, nq, 2]
   float* dec_o;           // [dec_splits, n_dec, nq, hd]
   float* dec_ml;          // [dec_splits, n_dec, nq, 2]
+  int* dec_count;         // [n_dec * kvh] split arrivals; zero between launches (the merging CTA resets it)
 };
+constexpr int kDecCountSlots = 1024 * 64;   // dec_count entries a caller provides (n_dec * kvh bound)
 
 // q: [T, q_stride] bf16 (first nq*hd columns are the rotated queries);
 // out: [T, nq*hd] bf16.  Prefill tiles read Q and paged K/V through the
@@ -126,6 +128,7 @@ bool make_attn_q_map(CUtensorMap* map, const void* q, int tokens, int nq, int q_
 // decode_attention_block_keys() for decode).
 bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size, int max_rows);
 int decode_attention_block_keys();
+int attention_kv_block_keys();   // keys per prefill K/V block (its map's box rows)
 int attention_q_rows_per_tile();
 // Decode requests of the batch only (attention_decode.cu); paged_attention
 // calls it after the prefill tiles.

@@ -23,7 +23,30 @@ from .step import StepInput
 MAX_ENGINE_TOKENS = 16384
 ATTN_SPLIT_TOKENS = 512
 DEC_SPLIT_SLOTS = 1024          # dec_splits * n_dec bound (engine scratch)
-Q_TILE_ROWS = 128      # query rows per prefill attention tile (the kernel's BM)
+Q_TILE_ROWS = 256      # query rows per prefill attention work item (two 128-row tiles)
+
+
+def decode_splits(n_dec: int, max_ctx: int, nkv: int, num_sms: int) -> int:
+    """Key splits per decode request: at most one wave of CTAs (the decode
+    kernel keeps two per SM: about 100 KB of shared memory each), at least
+    256 keys per split (128 when there are fewer than 64 request-head
+    pairs), within the scratch."""
+    if n_dec == 0:
+        return 1
+    pairs = n_dec * nkv
+    want = (2 * num_sms) // pairs
+    min_keys = 128 if pairs < 64 else 256
+    return int(max(1, min(32, want, max_ctx // min_keys, DEC_SPLIT_SLOTS // n_dec)))
+
+
+def prefill_splits(T: int, n_items: int, max_ctx: int, nkv: int, num_sms: int) -> int:
+    """Key splits per prefill work item (small steps only): at most one wave
+    of CTAs (one per SM), and at least 2 * T keys per split, since the merge
+    traffic grows with the step's tokens times the splits."""
+    if n_items == 0 or T > ATTN_SPLIT_TOKENS:
+        return 1
+    want = num_sms // (n_items * nkv)
+    return int(max(1, min(16, want, max_ctx // max(128, 2 * T))))
 
 
 def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf: np.ndarray):
@@ -43,6 +66,13 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     n_items = int(tiles.sum())
     item_req = np.repeat(np.arange(B), tiles)
     item_first = np.arange(n_items) - np.repeat(np.cumsum(tiles) - tiles, tiles)
+    if n_items > 1:
+        # longest first: CTAs start in item order, so the items that see the
+        # most keys (the last query rows of the longest contexts) go first
+        # and the short causal items fill the tail of the grid
+        kv_end = starts[item_req] + (np.minimum((item_first + 1) * Q_TILE_ROWS, rows[item_req]) + group - 1) // group
+        order = np.argsort(-kv_end, kind="stable")
+        item_req, item_first = item_req[order], item_first[order]
     table = np.zeros((B, max_pages), dtype=np.int32)
     for i, p in enumerate(step.page_tables):
         if p:
@@ -186,22 +216,10 @@ class NativeRunner:
         self.eng.load_globals(g["embed"], g["final_norm"], g["lm_head"])
 
     def _dec_splits(self, n_dec: int, max_ctx: int) -> int:
-        """Key splits per decode request: enough CTAs to fill the GPU a few
-        times over, at least 256 keys per split (128 when there are fewer
-        than 64 request-head pairs), within the scratch."""
-        if n_dec == 0:
-            return 1
-        pairs = n_dec * self.shape.nkv
-        want = math.ceil(4 * self.num_sms / pairs)
-        min_keys = 128 if pairs < 64 else 256
-        return int(max(1, min(32, want, max_ctx // min_keys, DEC_SPLIT_SLOTS // n_dec)))
+        return decode_splits(n_dec, max_ctx, self.shape.nkv, self.num_sms)
 
     def _splits(self, T: int, n_items: int, max_ctx: int) -> int:
-        if T > ATTN_SPLIT_TOKENS:
-            return 1
-        ctas = n_items * self.shape.nkv
-        want = math.ceil(2 * self.num_sms / max(ctas, 1))
-        return int(max(1, min(16, want, max_ctx // 128)))
+        return prefill_splits(T, n_items, max_ctx, self.shape.nkv, self.num_sms)
 
     def step(self, step: StepInput, recv_from: Optional[Tuple[str, int]] = None,
              send_to: Optional[Tuple[str, int]] = None, last_stage: bool = True) -> Optional[List[int]]:
