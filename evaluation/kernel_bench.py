@@ -75,7 +75,7 @@ def bench_gemm(args, cublas=False):
 
 
 def bench_attention(args):
-    from kunserve_b200.engine.native_runner import decode_splits, pack_meta, prefill_splits
+    from kunserve_b200.engine.native_runner import pack_meta, prefill_splits
     from kunserve_b200.engine.step import StepInput
     from kunserve_b200.ops import native
     import numpy as np
@@ -84,7 +84,9 @@ def bench_attention(args):
     nq, nkv, hd, bs, L = args.nq, args.nkv, 128, 16, 1
     for B in args.batch:
         for ctx in args.ctx:
-            pages_per = math.ceil(ctx / bs)
+            # --long: request 0 has a longer context (a skewed batch)
+            ctxs = [max(ctx, args.long) if i == 0 else ctx for i in range(B)]
+            pages_per = math.ceil(max(ctxs) / bs)
             P = B * pages_per
             from kunserve_b200.kv.layout import KVLayout
             lay = KVLayout(P, L, bs, nkv, hd, 2)
@@ -93,31 +95,36 @@ def bench_attention(args):
             ql = args.qlen
             T = B * ql
             q = torch.randn(T, nq * hd, device="cuda").bfloat16()
-            step = StepInput(list(range(B)), [[0] * ql] * B, [ctx - ql] * B, tables, [int(ql > 1)] * B, 0, 1)
-            buf = np.zeros(2 * (T * (nq // nkv) // 64 + B + 1) + 4 * T + 6 * B + 64 + B * pages_per, dtype=np.int32)
-            n_int, T, _, n_items, _, n_dec = pack_meta(step, bs, nq // nkv, pages_per, buf)
-            dec = torch.from_numpy(buf[n_int - n_dec:n_int].copy()).cuda()
+            step = StepInput(list(range(B)), [[0] * ql] * B, [c - ql for c in ctxs], tables, [int(ql > 1)] * B, 0, 1)
+            buf = np.zeros(2 * (T * (nq // nkv) // 64 + B + 1) + 4 * T + 6 * B + 64 + B * pages_per + 4 * 1024,
+                           dtype=np.int32)
+            n_int, T, _, n_items, _, n_dec, n_units = pack_meta(step, bs, nq // nkv, pages_per, buf, nkv, 148)
+            o_dec = n_int - 4 * n_units - n_dec
+            dec = torch.from_numpy(buf[o_dec:o_dec + n_dec].copy()).cuda()
+            units = torch.from_numpy(buf[o_dec + n_dec:n_int].copy()).cuda()
             items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
             o = 2 * n_items + 4 * T
             q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
             ctxl = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
             tab = torch.tensor(tables, dtype=torch.int32, device="cuda")
-            splits = decode_splits(n_dec, ctx, nkv, 148) if n_dec else prefill_splits(T, n_items, ctx, nkv, 148)
-            if args.splits > 0:
+            # prefill: key splits per item; decode: work units in all
+            splits = n_units if n_dec else prefill_splits(T, n_items, ctx, nkv, 148)
+            if args.splits > 0 and not n_dec:
                 splits = args.splits
-            out = torch.empty(T, nq * hd, device="cuda", dtype=torch.bfloat16)
-            op = torch.empty(max(splits, 1) * T * nq * hd, device="cuda")
-            ml = torch.empty(max(splits, 1) * T * nq * 2, device="cuda")
             psplits = 1 if n_dec else splits
+            out = torch.empty(T, nq * hd, device="cuda", dtype=torch.bfloat16)
+            op = torch.empty(max(psplits * T, n_units) * nq * hd, device="cuda")
+            ml = torch.empty(max(psplits * T, n_units) * nq * 2, device="cuda")
             fn = lambda i: C.attention(q, nq * hd, out, pool, P, 1, L, L, bs, nkv, 0, q_start, ctxl, tab, items,
-                                       psplits, op, ml, nq, 1 / math.sqrt(hd), dec, splits if n_dec else 1, op, ml)
+                                       psplits, op, ml, nq, 1 / math.sqrt(hd), dec, units, op, ml)
             t = timeit(fn, args.warmup, args.iters)
-            kv_bytes = B * ctx * nkv * hd * 2 * 2
+            kv_bytes = sum(ctxs) * nkv * hd * 2 * 2
             # causal FLOPs: query i of a request sees (ctx - ql + i + 1) keys; QK^T and PV, 2 FLOP per MAC
-            keys = sum(ctx - ql + i + 1 for i in range(ql))
-            flops = 4.0 * B * keys * nq * hd
+            keys = sum(c - ql + i + 1 for c in ctxs for i in range(ql))
+            flops = 4.0 * keys * nq * hd
             print(json.dumps({"kernel": "paged_attention_" + ("decode" if ql == 1 else "prefill"), "B": B,
-                              "ctx": ctx, "qlen": ql, "nq": nq, "nkv": nkv, "splits": splits,
+                              "ctx": ctx, "long": ctxs[0] if ctxs[0] != ctx else None, "qlen": ql, "nq": nq, "nkv": nkv,
+                              "splits": splits,
                               "us": round(t * 1e6, 2), "TB_s": round(kv_bytes / t / 1e12, 3),
                               "bw_frac": round(kv_bytes / t / bw, 3), "TFLOP_s": round(flops / t / 1e12, 1),
                               "flop_frac": round(flops / t / fl, 3), "peaks": src}), flush=True)
@@ -156,6 +163,7 @@ def main():
     p.add_argument("--nq", type=int, default=32)
     p.add_argument("--nkv", type=int, default=8)
     p.add_argument("--splits", type=int, default=-1)
+    p.add_argument("--long", type=int, default=0, help="attention: context of request 0 (skewed batch)")
     p.add_argument("--qlen", type=int, default=1, help="query tokens per request (1 = decode)")
     p.add_argument("--chunks", type=int, nargs="+", default=[1024, 16384])
     p.add_argument("--chunk-bytes", type=int, default=65536)

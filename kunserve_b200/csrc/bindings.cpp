@@ -123,7 +123,7 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
                   int64_t Ls, int64_t L, int64_t block_size, int64_t nkv, int64_t layer, torch::Tensor q_start,
                   torch::Tensor ctx_len, torch::Tensor page_table, torch::Tensor items, int64_t splits,
                   torch::Tensor o_part, torch::Tensor ml_part, int64_t nq, double scale, torch::Tensor dec_reqs,
-                  int64_t dec_splits, torch::Tensor dec_o, torch::Tensor dec_ml) {
+                  torch::Tensor dec_units, torch::Tensor dec_o, torch::Tensor dec_ml) {
   c10::cuda::CUDAGuard g(q.device());
   KVGeom geo = make_geom(pool, P, N, Ls, L, block_size, nkv, 128);
   AttnBatch b;
@@ -136,7 +136,10 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
   b.splits = (int)splits;
   b.dec_reqs = dec_reqs.data_ptr<int>();
   b.n_dec = dec_reqs.numel();
-  b.dec_splits = (int)dec_splits;
+  TORCH_CHECK(dec_units.numel() % 4 == 0 && dec_units.is_contiguous(), "attention: dec_units is [n, 4]");
+  b.dec_units = dec_units.data_ptr<int>();
+  b.n_units = dec_units.numel() / 4;
+  TORCH_CHECK((int64_t)dec_o.numel() >= (int64_t)b.n_units * nq * 128, "attention: dec_o too small");
   // split-arrival counts of the decode kernel: one zeroed buffer per device,
   // returned to zero by every launch
   static torch::Tensor counts[64];
@@ -144,7 +147,7 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
   TORCH_CHECK(dev >= 0 && dev < 64, "attention: bad device");
   if (!counts[dev].defined())
     counts[dev] = torch::zeros({(int64_t)kDecCountSlots}, torch::TensorOptions().dtype(torch::kInt32).device(q.device()));
-  TORCH_CHECK((int64_t)dec_reqs.numel() * nkv <= kDecCountSlots, "attention: too many decode requests");
+  TORCH_CHECK((int64_t)b.n_units * nkv <= kDecCountSlots, "attention: too many decode units");
   AttnScratch sc{o_part.data_ptr<float>(), ml_part.data_ptr<float>(), dec_o.data_ptr<float>(),
                  dec_ml.data_ptr<float>(), counts[dev].data_ptr<int>()};
   CUtensorMap tq, tkv, tkv_dec;

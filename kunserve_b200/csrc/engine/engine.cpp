@@ -34,9 +34,6 @@ static void check_nccl(ncclResult_t r, const char* what) {
 
 static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
-// decode attention splits x decode requests per step (partials scratch)
-static constexpr int64_t kDecSplitSlots = 1024;
-
 // Byte layout of one layer segment: in_norm, post_norm, qkv, o, gu (interleaved), down.
 struct LayerLayout {
   size_t in_norm, post_norm, qkv, o, gu, down, total;
@@ -92,12 +89,12 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   attn_split_tokens_ = std::min<int64_t>(T, 512);
   attn_o_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * s.hd}, f32);
   attn_ml_ = torch::empty({(int64_t)attn_max_splits_ * attn_split_tokens_ * s.nq * 2}, f32);
-  dec_o_ = torch::empty({kDecSplitSlots * s.nq * s.hd}, f32);
-  dec_ml_ = torch::empty({kDecSplitSlots * s.nq * 2}, f32);
+  dec_o_ = torch::empty({(int64_t)kDecUnitSlots * s.nq * s.hd}, f32);
+  dec_ml_ = torch::empty({(int64_t)kDecUnitSlots * s.nq * 2}, f32);
   dec_count_ = torch::zeros({(int64_t)kDecCountSlots}, i32);
   const int64_t max_items = T * std::max(1, s.nq / s.nkv) / 64 + B + 1;
   const int64_t meta_ints = 2 * max_items + 4 * T + 5 * B + 1 +
-                            B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + 64;
+                            B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + 4 * kDecUnitSlots + 64;
   meta_dev_ = torch::empty({meta_ints}, i32);
   tokens_dev_ = torch::empty({B}, i32);
   err_host_ = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).pinned_memory(true));
@@ -321,7 +318,7 @@ void Engine::all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t st) {
 }
 
 std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, int64_t max_pages, int64_t n_items,
-                                     int64_t splits, int64_t n_dec, int64_t dec_splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
+                                     int64_t splits, int64_t n_dec, int64_t n_units, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
                                      bool first_stage, bool last_stage, int64_t sample_mode, int64_t step) {
   c10::cuda::CUDAGuard g(device_);
   char range_name[96];
@@ -334,13 +331,14 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   KUS_CHECK(splits >= 1 && splits <= attn_max_splits_, "bad attention split");
   KUS_CHECK(splits == 1 || T <= attn_split_tokens_, "split attention only for small steps");
   cudaStream_t st = at::cuda::getCurrentCUDAStream(device_);
-  KUS_CHECK(n_dec >= 0 && n_dec <= B && dec_splits >= 1 && dec_splits * n_dec <= kDecSplitSlots,
-            "bad decode attention split");
-  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 2 * B + n_dec;
+  KUS_CHECK(n_dec >= 0 && n_dec <= B && n_units >= n_dec && n_units <= kDecUnitSlots && (n_units > 0) == (n_dec > 0),
+            "bad decode attention units");
+  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 2 * B + n_dec + 4 * n_units;
   KUS_CHECK(meta.numel() >= n_meta && n_meta <= meta_dev_.numel(), "meta buffer too small");
   check_cuda(cudaMemcpyAsync(meta_dev_.data_ptr(), meta.data_ptr(), n_meta * 4, cudaMemcpyHostToDevice, st), "meta H2D");
   // meta layout (int32): items[2n] | tokens[T] | positions[T] | kv_page[T] | kv_slot[T] |
-  // q_start[B+1] | ctx_len[B] | last_idx[B] | page_table[B*max_pages] | temps[B] (f32) | seeds[B]
+  // q_start[B+1] | ctx_len[B] | last_idx[B] | page_table[B*max_pages] | temps[B] (f32) | seeds[B] |
+  // dec_reqs[n_dec] | dec_units[4*n_units]
   const int* m = meta_dev_.data_ptr<int>();
   const int2* items = reinterpret_cast<const int2*>(m);
   const int* tokens = m + 2 * n_items;
@@ -354,6 +352,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   const float* temps = reinterpret_cast<const float*>(table + B * max_pages);
   const unsigned* seeds = reinterpret_cast<const unsigned*>(temps + B);
   const int* dec_reqs = reinterpret_cast<const int*>(seeds + B);
+  const int* dec_units = dec_reqs + n_dec;
 
   KVGeom geo;
   geo.base = arena_->kv_base();
@@ -377,7 +376,8 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   ab.splits = (int)splits;
   ab.dec_reqs = dec_reqs;
   ab.n_dec = (int)n_dec;
-  ab.dec_splits = (int)dec_splits;
+  ab.dec_units = dec_units;
+  ab.n_units = (int)n_units;
   AttnScratch sc{attn_o_.data_ptr<float>(), attn_ml_.data_ptr<float>(), dec_o_.data_ptr<float>(),
                  dec_ml_.data_ptr<float>(), dec_count_.data_ptr<int>()};
 
@@ -434,7 +434,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
                 s_.max_pos, st, np ? part : nullptr, np, (long long)T * qkv_n_);
     paged_attention(m_attn_q_, m_attn_kv_, m_dec_kv_, qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
     if (sync_debug_) debug_check("attention", (int)T, (int)B, (int)n_dec, st);
-    launches_ += 3 + (splits > 1 ? 1 : 0);
+    launches_ += 2 + (n_items > 0 ? 1 + (splits > 1 ? 1 : 0) : 0) + (n_units > 0 ? 1 : 0);
     if (fused) {
       tp_push_gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, st);
       tp_reduce(h, W.post_norm, y, (int)T, st);

@@ -72,7 +72,7 @@ class Engine {
   // One step.  `meta` is a pinned int32 tensor laid out by the Python runner
   // (see native_runner.py); returns sampled ids on the last stage.
   std::vector<int64_t> forward(torch::Tensor meta, int64_t T, int64_t B, int64_t max_pages, int64_t n_items,
-                               int64_t splits, int64_t n_dec, int64_t dec_splits, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
+                               int64_t splits, int64_t n_dec, int64_t n_units, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
                                bool first_stage, bool last_stage, int64_t sample_mode, int64_t step);
   torch::Tensor hidden();                   // [max_tokens, H] residual stream (PP transfer)
   torch::Tensor logits();                   // [max_batch, V] fp32

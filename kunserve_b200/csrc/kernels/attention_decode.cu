@@ -1,7 +1,9 @@
 // Paged decode attention: one query token per request, on the tensor cores.
 //
-// One CTA serves (request, KV head, key split) for the whole GQA group of G
-// query heads.  The G query rows form the M side of mma.sync m16n8k16 tiles
+// One CTA serves (work unit, KV head) for the whole GQA group of G query
+// heads; a unit is a range of key blocks of one request (long contexts are
+// cut into several units, sized by the host so that the grid is about one
+// wave whatever the mix of context lengths).  The G query rows form the M side of mma.sync m16n8k16 tiles
 // (rows G..15 are zero), so S = Q K^T and O += P V each cost one MMA per 8
 // keys / 8 dims and every K/V byte feeds all G heads.
 //
@@ -13,9 +15,9 @@
 //              registers (the S accumulator layout is the A layout of P V),
 //              then the warps merge (max, sum, O) in shared memory
 //
-// With splits > 1 a CTA writes an unnormalized partial plus (max, sum); the
-// last of a (request, KV head)'s split CTAs to finish, found by an atomic
-// arrival count, merges them and writes the output rows.
+// A request cut into several units has each unit write an unnormalized
+// partial plus (max, sum); the last of its unit CTAs to finish (per KV head),
+// found by an atomic arrival count, merges them and writes the output rows.
 #include "../common.cuh"
 #include "kernels.h"
 
@@ -76,7 +78,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
   uint64_t* empty = full + kStages;
 
-  const int di = blockIdx.x, kh = blockIdx.y, split = blockIdx.z;
+  // work unit: (decode slot, first key block, blocks, first unit of the
+  // request << 8 | units of the request)
+  const int* unit = b.dec_units + 4 * blockIdx.x;
+  const int di = unit[0], kh = blockIdx.y;
+  const int u0 = unit[3] >> 8, n_units = unit[3] & 255;
   const int G = nq / g.kvh;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int req = b.dec_reqs[di];
@@ -84,9 +90,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   const int ctx = b.ctx_len[req];
   const int* table = b.page_table + (size_t)req * b.max_pages;
   const int nblk = (ctx + BK - 1) / BK;
-  const int per = (nblk + b.dec_splits - 1) / b.dec_splits;
-  const int blk0 = split * per;
-  const int nb = max(0, min(blk0 + per, nblk) - blk0);
+  const int blk0 = unit[1];
+  const int nb = max(0, min(unit[2], nblk - blk0));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -267,10 +272,10 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       }
     }
     const int head = kh * G + h;
-    if (b.dec_splits == 1) {
+    if (n_units == 1) {
       if (ok) out[(size_t)tok * nq * HD + (size_t)head * HD + d] = f2bf(L > 0.f ? A / L : 0.f);
     } else {
-      const size_t idx = ((size_t)split * b.n_dec + di) * nq + head;
+      const size_t idx = (size_t)blockIdx.x * nq + head;
       sc.dec_o[idx * HD + d] = A;
       if (d == 0) {
         sc.dec_ml[idx * 2] = M;
@@ -278,30 +283,30 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       }
     }
   }
-  if (b.dec_splits == 1) return;
-  // The last split CTA of this (request, KV head) to finish merges the
-  // partials of all splits (G x 128 values each, read from L2): no separate
-  // combine launch.  Every CTA arrives (waits are bounded), so the counter
-  // is back at zero after each launch.
+  if (n_units == 1) return;
+  // The last unit CTA of this (request, KV head) to finish merges the
+  // partials of all the request's units (G x 128 values each, read from L2):
+  // no separate combine launch.  Every CTA arrives (waits are bounded), so
+  // the counter is back at zero after each launch.
   __shared__ int last_s;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();   // publish this CTA's partial before counting it
-    int* cnt = sc.dec_count + di * g.kvh + kh;
-    const bool last = atomicAdd(cnt, 1) == b.dec_splits - 1;
+    int* cnt = sc.dec_count + u0 * g.kvh + kh;
+    const bool last = atomicAdd(cnt, 1) == n_units - 1;
     if (last) *cnt = 0;
     last_s = last;
   }
   __syncthreads();
   if (!last_s) return;
   __threadfence();
-  // one warp per head row of the group: lane s holds split s's (max, sum),
-  // lane l accumulates dims 4l..4l+3, all splits' loads in flight
-  const size_t plane = (size_t)b.n_dec * nq;
+  // one warp per head row of the group: lane s holds unit s's (max, sum),
+  // lane l accumulates dims 4l..4l+3, all units' loads in flight
+  const size_t plane = (size_t)nq;
   for (int h = warp; h < G; h += kWarps) {
-    const size_t row = (size_t)di * nq + kh * G + h;
+    const size_t row = (size_t)u0 * nq + kh * G + h;
     float m = -INFINITY, l = 0.f;
-    if (lane < b.dec_splits) {
+    if (lane < n_units) {
       const float2 ml = __ldcg(reinterpret_cast<const float2*>(sc.dec_ml) + lane * plane + row);
       m = ml.x;
       l = ml.y;
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
-    for (int sp = 0; sp < b.dec_splits; ++sp) {
+    for (int sp = 0; sp < n_units; ++sp) {
       const float ws = __shfl_sync(0xffffffffu, w, sp);
       const float4 o4 = __ldcg(reinterpret_cast<const float4*>(sc.dec_o + (sp * plane + row) * HD) + lane);
       acc.x += ws * o4.x;
@@ -338,14 +343,14 @@ int decode_attention_block_keys() { return dec::BK; }
 void paged_decode_attention(const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out,
                             const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int nq, float scale,
                             cudaStream_t s) {
-  if (b.n_dec <= 0) return;
+  if (b.n_units <= 0) return;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(dec::decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
     attr = true;
   }
   const float sl2 = scale * 1.4426950408889634f;
-  launch_k(dec::decode_attn_kernel, dim3(b.n_dec, g.kvh, b.dec_splits), dim3(dec::kThreads), dec::kSmemBytes, s, tmKV,
+  launch_k(dec::decode_attn_kernel, dim3(b.n_units, g.kvh), dim3(dec::kThreads), dec::kSmemBytes, s, tmKV,
            q, q_stride, out, g, layer, b, sc, nq, sl2);
 }
 

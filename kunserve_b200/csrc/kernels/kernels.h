@@ -102,17 +102,22 @@ struct AttnBatch {
   int splits;             // KV splits per item (>1: partials + combine)
   const int* dec_reqs;    // [n_dec] requests with one query token: decode kernel
   int n_dec;
-  int dec_splits;         // KV splits per decode request
+  // [n_units, 4] decode work units: (index into dec_reqs, first key block of
+  // 64 keys, blocks, first unit of the same request << 8 | its unit count);
+  // a request's units are consecutive, at most 32 per request
+  const int* dec_units;
+  int n_units;
 };
 
 struct AttnScratch {
   float* o_part;          // [splits, T, nq, hd]
   float* ml_part;         // [splits, T, nq, 2]
-  float* dec_o;           // [dec_splits, n_dec, nq, hd]
-  float* dec_ml;          // [dec_splits, n_dec, nq, 2]
-  int* dec_count;         // [n_dec * kvh] split arrivals; zero between launches (the merging CTA resets it)
+  float* dec_o;           // [n_units, nq, hd]
+  float* dec_ml;          // [n_units, nq, 2]
+  int* dec_count;         // [n_units * kvh] unit arrivals; zero between launches (the merging CTA resets it)
 };
-constexpr int kDecCountSlots = 1024 * 64;   // dec_count entries a caller provides (n_dec * kvh bound)
+constexpr int kDecUnitSlots = 1024;                    // n_units bound of the engine's scratch
+constexpr int kDecCountSlots = kDecUnitSlots * 64;     // dec_count entries a caller provides (n_units * kvh)
 
 // q: [T, q_stride] bf16 (first nq*hd columns are the rotated queries);
 // out: [T, nq*hd] bf16.  Prefill tiles read Q and paged K/V through the

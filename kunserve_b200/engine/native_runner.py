@@ -22,21 +22,42 @@ from .step import StepInput
 
 MAX_ENGINE_TOKENS = 16384
 ATTN_SPLIT_TOKENS = 512
-DEC_SPLIT_SLOTS = 1024          # dec_splits * n_dec bound (engine scratch)
+DEC_UNIT_SLOTS = 1024           # decode attention work units per step (engine scratch)
 Q_TILE_ROWS = 256      # query rows per prefill attention work item (two 128-row tiles)
 
 
-def decode_splits(n_dec: int, max_ctx: int, nkv: int, num_sms: int) -> int:
-    """Key splits per decode request: at most one wave of CTAs (the decode
-    kernel keeps two per SM: about 100 KB of shared memory each), at least
-    256 keys per split (128 when there are fewer than 64 request-head
-    pairs), within the scratch."""
-    if n_dec == 0:
-        return 1
-    pairs = n_dec * nkv
-    want = (2 * num_sms) // pairs
-    min_keys = 128 if pairs < 64 else 256
-    return int(max(1, min(32, want, max_ctx // min_keys, DEC_SPLIT_SLOTS // n_dec)))
+def decode_units(ctx: np.ndarray, nkv: int, num_sms: int) -> np.ndarray:
+    """Work units of the decode attention kernel for requests with contexts
+    ``ctx`` (decode-list order): int32 rows (decode index, first 64-key
+    block, blocks, first unit of the request << 8 | the request's units).
+
+    Each request is cut into units of about one CTA slot's share of the
+    whole batch's keys (the kernel keeps two CTAs per SM: about 100 KB of
+    shared memory each), so the grid stays near one wave even when one long
+    context sits among short ones; at least 256 keys per unit (128 when
+    there are fewer than 64 request-head pairs), at most 32 units per
+    request and ``DEC_UNIT_SLOTS`` in all."""
+    n = int(ctx.size)
+    if n == 0:
+        return np.zeros((0, 4), dtype=np.int32)
+    if n > DEC_UNIT_SLOTS:
+        raise ValueError(f"{n} decode requests exceed {DEC_UNIT_SLOTS} units")
+    blocks = (ctx.astype(np.int64) + 63) // 64
+    share = max(2 if n * nkv < 64 else 4, math.ceil(int(blocks.sum()) * nkv / (2 * num_sms)))
+    while True:
+        per = np.clip(blocks // share, 1, 32)
+        chunk = (blocks + per - 1) // per          # equal units within a request
+        per = (blocks + chunk - 1) // chunk        # no empty tail unit
+        if int(per.sum()) <= DEC_UNIT_SLOTS:
+            break
+        share *= 2
+    first = np.cumsum(per) - per
+    rep_first, rep_chunk = np.repeat(first, per), np.repeat(chunk, per)
+    j = np.arange(int(per.sum())) - rep_first
+    blk0 = j * rep_chunk
+    units = np.stack([np.repeat(np.arange(n), per), blk0, np.minimum(rep_chunk, np.repeat(blocks, per) - blk0),
+                      (rep_first << 8) | np.repeat(per, per)], axis=1)
+    return units.astype(np.int32)
 
 
 def prefill_splits(T: int, n_items: int, max_ctx: int, nkv: int, num_sms: int) -> int:
@@ -49,11 +70,13 @@ def prefill_splits(T: int, n_items: int, max_ctx: int, nkv: int, num_sms: int) -
     return int(max(1, min(16, want, max_ctx // max(128, 2 * T))))
 
 
-def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf: np.ndarray):
+def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf: np.ndarray, nkv: int,
+              num_sms: int):
     """Fill ``buf`` (int32) with the engine's step metadata; returns
-    ``(n_ints, T, B, n_items, max_ctx, n_dec)``.  Requests with one query
-    token go to the decode kernel (list at the end); the others become
-    ``Q_TILE_ROWS``-row query tiles (``items``) of the prefill kernel."""
+    ``(n_ints, T, B, n_items, max_prefill_ctx, n_dec, n_units)``.  Requests
+    with one query token go to the decode kernel (list and work units at the
+    end); the others become ``Q_TILE_ROWS``-row query tiles (``items``) of
+    the prefill kernel."""
     B = step.num_requests
     ql = np.fromiter((len(t) for t in step.input_tokens), dtype=np.int64, count=B)
     T = int(ql.sum())
@@ -106,7 +129,10 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     put(seeds.astype(np.uint32).view(np.int32))
     dec = np.nonzero(is_dec)[0].astype(np.int32)
     put(dec)
-    return o, T, B, n_items, int(ctx.max()) if B else 0, int(dec.size)
+    units = decode_units(ctx[dec], nkv, num_sms)
+    put(units)
+    pre_ctx = int(ctx[~is_dec].max()) if n_items else 0
+    return o, T, B, n_items, pre_ctx, int(dec.size), int(units.shape[0])
 
 
 class NativeRunner:
@@ -154,7 +180,7 @@ class NativeRunner:
             torch.cuda.synchronize()
         self.max_pages = math.ceil(sh.max_pos / layout.block_size)
         n = (2 * (sh.max_tokens * self.group // Q_TILE_ROWS + sh.max_batch + 1) + 4 * sh.max_tokens
-             + 6 * sh.max_batch + 1 + sh.max_batch * self.max_pages + 64)
+             + 6 * sh.max_batch + 1 + sh.max_batch * self.max_pages + 4 * DEC_UNIT_SLOTS + 64)
         self.meta = torch.empty(n, dtype=torch.int32, pin_memory=True)
         self.meta_np = self.meta.numpy()
         self.num_sms = C.num_sms()
@@ -215,18 +241,15 @@ class NativeRunner:
         g = w.globals
         self.eng.load_globals(g["embed"], g["final_norm"], g["lm_head"])
 
-    def _dec_splits(self, n_dec: int, max_ctx: int) -> int:
-        return decode_splits(n_dec, max_ctx, self.shape.nkv, self.num_sms)
-
     def _splits(self, T: int, n_items: int, max_ctx: int) -> int:
         return prefill_splits(T, n_items, max_ctx, self.shape.nkv, self.num_sms)
 
     def step(self, step: StepInput, recv_from: Optional[Tuple[str, int]] = None,
              send_to: Optional[Tuple[str, int]] = None, last_stage: bool = True) -> Optional[List[int]]:
         width = max([len(p) for p in step.page_tables] + [1])
-        n, T, B, n_items, max_ctx, n_dec = pack_meta(step, self.layout.block_size, self.group, width, self.meta_np)
+        n, T, B, n_items, max_ctx, n_dec, n_units = pack_meta(step, self.layout.block_size, self.group, width,
+                                                              self.meta_np, self.shape.nkv, self.num_sms)
         splits = self._splits(T, n_items, max_ctx) if n_items else 1
-        dec_splits = self._dec_splits(n_dec, max_ctx)
         first = recv_from is None
         if not first:
             buf = self.comm.recv((T, self.shape.hidden), torch.bfloat16, self.device, *recv_from)
@@ -238,7 +261,7 @@ class NativeRunner:
         if self._ev is None:
             self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         self._ev[0].record()
-        out = self.eng.forward(self.meta, T, B, width, n_items, splits, n_dec, dec_splits, step.layer_start,
+        out = self.eng.forward(self.meta, T, B, width, n_items, splits, n_dec, n_units, step.layer_start,
                                step.layer_end, step.fusion_size, first, last_stage, sample_mode, step.step_id)
         # the forward returned after its device work (it reads the sampled ids
         # back), so this bracket is the step's time on the GPU

@@ -204,9 +204,13 @@ def test_paged_attention(C, nq, nkv, splits):
     buf = np.zeros(4096, dtype=np.int32)
     G = nq // nkv
     width = max(len(t) for t in tables)
-    n_int, T2, B, n_items, _, n_dec = pack_meta(step, bs, G, width, buf)
+    n_int, T2, B, n_items, _, n_dec, n_units = pack_meta(step, bs, G, width, buf, nkv, 148)
+    if splits > 1:
+        assert n_units > n_dec   # the longer decode contexts are cut into several units
     items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
-    dec = torch.from_numpy(buf[n_int - n_dec:n_int].copy()).cuda()
+    o_dec = n_int - 4 * n_units - n_dec
+    dec = torch.from_numpy(buf[o_dec:o_dec + n_dec].copy()).cuda()
+    units = torch.from_numpy(buf[o_dec + n_dec:n_int].copy()).cuda()
     o = 2 * n_items + 4 * T
     q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
     ctx = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
@@ -217,10 +221,10 @@ def test_paged_attention(C, nq, nkv, splits):
     o_part = torch.empty(splits * T * nq * hd, device="cuda")
     ml = torch.empty(splits * T * nq * 2, device="cuda")
     layer = 1
-    dec_o = torch.empty(splits * 4 * nq * hd, device="cuda")
-    dec_ml = torch.empty(splits * 4 * nq * 2, device="cuda")
+    dec_o = torch.empty(max(n_units, 1) * nq * hd, device="cuda")
+    dec_ml = torch.empty(max(n_units, 1) * nq * 2, device="cuda")
     C.attention(q, nq * hd, out, pool, P, N, L, L, bs, nkv, layer, q_start, ctx, tab.cuda(), items, 1,
-                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, splits, dec_o, dec_ml)
+                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, units, dec_o, dec_ml)
     torch.cuda.synchronize()
     ref = _ref_attention(q, pool, lay, N, layer, tables, starts, qlens, nq, nkv, hd)
     assert _rel(out.view(T, nq, hd), ref) < 2e-2
@@ -252,9 +256,11 @@ def test_prefill_attention_long_chunks(C, nq, nkv, splits):
     step = StepInput(list(range(B)), [[0] * n for n in qlens], starts, tables, [1] * B, 0, 1)
     buf = np.zeros(16384, dtype=np.int32)
     width = max(len(t) for t in tables)
-    n_int, T2, B2, n_items, _, n_dec = pack_meta(step, bs, nq // nkv, width, buf)
+    n_int, T2, B2, n_items, _, n_dec, n_units = pack_meta(step, bs, nq // nkv, width, buf, nkv, 148)
     items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
-    dec = torch.from_numpy(buf[n_int - n_dec:n_int].copy()).cuda()
+    o_dec = n_int - 4 * n_units - n_dec
+    dec = torch.from_numpy(buf[o_dec:o_dec + n_dec].copy()).cuda()
+    units = torch.from_numpy(buf[o_dec + n_dec:n_int].copy()).cuda()
     o = 2 * n_items + 4 * T
     q_start = torch.from_numpy(buf[o:o + B + 1].copy()).cuda()
     ctx = torch.from_numpy(buf[o + B + 1:o + 2 * B + 1].copy()).cuda()
@@ -264,10 +270,10 @@ def test_prefill_attention_long_chunks(C, nq, nkv, splits):
     out = torch.empty(T, nq * hd, device="cuda", dtype=torch.bfloat16)
     o_part = torch.empty(splits * T * nq * hd, device="cuda")
     ml = torch.empty(splits * T * nq * 2, device="cuda")
-    dec_o = torch.empty(4 * nq * hd, device="cuda")
-    dec_ml = torch.empty(4 * nq * 2, device="cuda")
+    dec_o = torch.empty(max(n_units, 1) * nq * hd, device="cuda")
+    dec_ml = torch.empty(max(n_units, 1) * nq * 2, device="cuda")
     C.attention(q, nq * hd, out, pool, P, N, L, L, bs, nkv, 1, q_start, ctx, tab.cuda(), items, splits,
-                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, 1, dec_o, dec_ml)
+                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, units, dec_o, dec_ml)
     torch.cuda.synchronize()
     from kunserve_b200.ops import check_error
     check_error()
