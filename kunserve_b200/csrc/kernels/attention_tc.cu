@@ -124,8 +124,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + kBarOff);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int2 item = b.items[blockIdx.x];
-  const int kh = blockIdx.y, split = blockIdx.z;
+  // heads vary fastest in launch order, so the longest-first item order
+  // holds across the whole grid
+  const int2 item = b.items[blockIdx.y];
+  const int kh = blockIdx.x, split = blockIdx.z;
   const int G = nq / g.kvh;
   const int req = item.x, row0 = item.y;
   const int qs = b.q_start[req];
@@ -504,7 +506,7 @@ void paged_prefill_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, __
     attr = true;
   }
   const float scale_log2 = scale * 1.4426950408889634f;
-  launch_k(fatc::fa_kernel, dim3(b.n_items, g.kvh, b.splits), dim3(fatc::kThreads), fatc::kSmemBytes, s, tmQ, tmKV,
+  launch_k(fatc::fa_kernel, dim3(g.kvh, b.n_items, b.splits), dim3(fatc::kThreads), fatc::kSmemBytes, s, tmQ, tmKV,
            out, g, layer, b, sc, T, nq, scale_log2);
   if (b.splits > 1)
     launch_k(fatc::combine_kernel, dim3((unsigned)(((size_t)T * nq + 7) / 8)), dim3(256), 0, s, sc, out, T, nq,
