@@ -10,8 +10,9 @@
   column-parallel projections (qkv: N = (H + 2 kv)/tp ~ H/tp here; gate/up:
   N = 2F/tp) with K = H;
 * paged KV-block migration (blocks of 16 tokens x 8 KV heads x 128 dim, K and
-  V) and parameter restore (contiguous bytes) pulled by the copy kernel from
-  a peer's mapped memory, against NCCL send/recv of the same bytes.
+  V; 1k-256k blocks) and parameter restore (contiguous shards of 1-70 GB)
+  pulled by the copy kernel from a peer's mapped memory, against NCCL
+  send/recv of the same bytes.
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
         evaluation/multigpu_bench.py --what tp --tokens 1 16 256 4096 --hidden 4096
@@ -266,13 +267,47 @@ def bench_copy(args, C, dev, rank, world):
         del keep
 
 
+def bench_restore(args, C, dev, rank, world):
+    """Parameter restore: a contiguous shard pulled from a peer by the copy
+    kernel (2 MB chunks) against NCCL send/recv of the same buffers."""
+    chunk = 2 << 20
+    for gb in args.restore_gb:
+        nbytes = int(gb * (1 << 30)) // chunk * chunk
+        bases, keep = share(C, dev, nbytes, rank, world)
+        local = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+        peer = (rank + 1) % world
+        offs = torch.arange(nbytes // chunk, device=dev, dtype=torch.int64) * chunk
+
+        def pull():
+            C.copy_chunks(local.data_ptr(), bases[peer], offs, offs, chunk, 4 * 148)
+
+        def nccl():
+            # one buffer sends and receives (two shards would not fit at 70 GB):
+            # a timing baseline only, the received bytes are not used
+            ops = [dist.P2POp(dist.isend, local, peer), dist.P2POp(dist.irecv, local, (rank - 1) % world)]
+            for r in dist.batch_isend_irecv(ops):
+                r.wait()
+
+        it = max(2, min(args.iters, int(8 / max(gb, 0.5))))
+        tp_ = time_ms(pull, 1, it, dev)
+        tn = time_ms(nccl, 1, it, dev)
+        if rank == 0:
+            print(json.dumps({"kernel": "p2p_parameter_restore", "GB": round(nbytes / 1e9, 3),
+                              "p2p_ms": round(tp_, 2), "nccl_ms": round(tn, 2),
+                              "p2p_GB_s": round(nbytes / tp_ / 1e6, 1), "nccl_GB_s": round(nbytes / tn / 1e6, 1),
+                              "link_frac": round(nbytes / tp_ / 1e6 / 770, 3)}), flush=True)
+        del keep, local
+        torch.cuda.empty_cache()
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("--what", nargs="+", choices=["tp", "rs", "ag", "copy", "all"], default=["all"])
+    p.add_argument("--what", nargs="+", choices=["tp", "rs", "ag", "copy", "restore", "all"], default=["all"])
     p.add_argument("--check", action="store_true", help="compare the fused results with PyTorch first")
     p.add_argument("--tokens", type=int, nargs="+", default=[1, 16, 256, 4096])
     p.add_argument("--hidden", type=int, nargs="+", default=[4096, 5120, 8192])
-    p.add_argument("--blocks", type=int, nargs="+", default=[1024, 16384, 65536])
+    p.add_argument("--blocks", type=int, nargs="+", default=[1024, 16384, 65536, 262144])
+    p.add_argument("--restore-gb", type=float, nargs="+", default=[1, 8, 35, 70])
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--iters", type=int, default=10)
     a = p.parse_args()
@@ -294,6 +329,8 @@ def main():
             bench_ag(a, C, local, rank, world)
         if want & {"copy", "all"}:
             bench_copy(a, C, local, rank, world)
+        if want & {"restore", "all"}:
+            bench_restore(a, C, local, rank, world)
         check_error()
     finally:
         dist.barrier()

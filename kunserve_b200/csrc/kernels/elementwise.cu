@@ -6,6 +6,8 @@
 // head dims must be multiples of 8 elements (checked by the host wrappers).
 #include "../common.cuh"
 #include "kernels.h"
+#include "gemm.h"
+#include <algorithm>
 
 namespace kus {
 
@@ -287,29 +289,47 @@ void sample(const float* logits, int B, int V, int ld, const float* temp, const 
 // dst_base + dst_off[i] <- src_base + src_off[i], `chunk` bytes each (multiple
 // of 16).  src_base may be a peer GPU's buffer mapped into this context: the
 // kernel then pulls over NVLink with plain 16-byte loads.
-__global__ void copy_chunks_kernel(uint8_t* __restrict__ dst_base, const uint8_t* __restrict__ src_base,
-                                   const long long* __restrict__ dst_off, const long long* __restrict__ src_off,
-                                   int n, long long chunk) {
-  const long long vec_per_chunk = chunk / 16;
-  const long long total = vec_per_chunk * n;
-  for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < total;
-       v += (long long)gridDim.x * blockDim.x) {
-    const long long c = v / vec_per_chunk, k = v - c * vec_per_chunk;
-    const uint4* s = reinterpret_cast<const uint4*>(src_base + src_off[c]) + k;
-    uint4* d = reinterpret_cast<uint4*>(dst_base + dst_off[c]) + k;
-    *d = __ldcs(s);
+__global__ void __launch_bounds__(256) copy_chunks_kernel(uint8_t* __restrict__ dst_base,
+                                                          const uint8_t* __restrict__ src_base,
+                                                          const long long* __restrict__ dst_off,
+                                                          const long long* __restrict__ src_off, int n, int vpc,
+                                                          int parts, int per_part) {
+  // work item w: piece w % parts of chunk w / parts (one 32-bit division per
+  // piece, none per vector); four 16-byte loads in flight per thread
+  const int items = n * parts;
+  for (int w = blockIdx.x; w < items; w += gridDim.x) {
+    const int c = w / parts, piece = w - c * parts;
+    const int v0 = piece * per_part, v1 = min(vpc, v0 + per_part);
+    const uint4* s = reinterpret_cast<const uint4*>(src_base + src_off[c]);
+    uint4* d = reinterpret_cast<uint4*>(dst_base + dst_off[c]);
+    int k = v0 + threadIdx.x;
+    for (; k + 3 * 256 < v1; k += 4 * 256) {
+      const uint4 x0 = __ldcs(s + k), x1 = __ldcs(s + k + 256), x2 = __ldcs(s + k + 512), x3 = __ldcs(s + k + 768);
+      d[k] = x0;
+      d[k + 256] = x1;
+      d[k + 512] = x2;
+      d[k + 768] = x3;
+    }
+    for (; k < v1; k += 256) d[k] = __ldcs(s + k);
   }
 }
 
 void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off, const long long* src_off, int n,
                  long long chunk, int max_blocks, cudaStream_t s) {
-  if (n <= 0) return;
-  const long long vecs = chunk / 16 * n;
-  long long blocks = (vecs + 255) / 256;
-  if (blocks > max_blocks) blocks = max_blocks;
-  copy_chunks_kernel<<<(int)blocks, 256, 0, s>>>(reinterpret_cast<uint8_t*>(dst_base),
-                                                 reinterpret_cast<const uint8_t*>(src_base), dst_off, src_off, n,
-                                                 chunk);
+  if (n <= 0 || chunk <= 0) return;
+  const long long vpc = chunk / 16;
+  // cut large chunks into pieces of at least 16 KB until there are about
+  // four work items per SM
+  const long long want = 4LL * num_sms();
+  long long parts = n >= want ? 1 : (want + n - 1) / n;
+  parts = std::max(1LL, std::min(parts, vpc / 1024));
+  const long long per_part = (vpc + parts - 1) / parts;
+  parts = (vpc + per_part - 1) / per_part;
+  const long long items = (long long)n * parts;
+  const int blocks = (int)std::min<long long>(items, max_blocks);
+  copy_chunks_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<uint8_t*>(dst_base),
+                                            reinterpret_cast<const uint8_t*>(src_base), dst_off, src_off, n,
+                                            (int)vpc, (int)parts, (int)per_part);
 }
 
 // ------------------------------------- fused TP all-reduce: the reduce side

@@ -313,6 +313,22 @@ def test_copy_chunks(C):
         assert torch.equal(dst[d:d + 4096], src[s:s + 4096])
 
 
+@pytest.mark.parametrize("chunk,n", [(16 * 3001, 2), (4 << 20, 3), (65536, 700)])
+def test_copy_chunks_pieces(C, chunk, n):
+    """Few large chunks are cut into pieces across CTAs; odd vector counts."""
+    src = torch.randint(0, 255, (n * chunk,), device="cuda", dtype=torch.uint8)
+    dst = torch.zeros(n * chunk + 4096, device="cuda", dtype=torch.uint8)
+    perm = torch.randperm(n, device="cuda").to(torch.int64)
+    so = torch.arange(n, device="cuda", dtype=torch.int64) * chunk
+    do = perm * chunk + 16
+    C.copy_chunks(dst.data_ptr(), src.data_ptr(), do, so, chunk, 4 * 148)
+    torch.cuda.synchronize()
+    expect = torch.zeros_like(dst)
+    for i, p in enumerate(perm.tolist()):
+        expect[p * chunk + 16:(p + 1) * chunk + 16] = src[i * chunk:(i + 1) * chunk]
+    assert torch.equal(dst, expect)
+
+
 def test_embed(C):
     tab = torch.randn(100, 512, device="cuda").bfloat16()
     tok = torch.tensor([3, 99, 0], device="cuda", dtype=torch.int32)
