@@ -81,7 +81,7 @@ def bench_attention(args):
     import numpy as np
     C = native()
     bw, fl, src = peaks()
-    nq, nkv, hd, bs, L = args.nq, args.nkv, 128, 16, 1
+    nq, nkv, hd, bs, L = args.nq, args.nkv, 128, args.block_size, 1
     for B in args.batch:
         for ctx in args.ctx:
             # --long: request 0 has a longer context (a skewed batch)
@@ -96,10 +96,10 @@ def bench_attention(args):
             T = B * ql
             q = torch.randn(T, nq * hd, device="cuda").bfloat16()
             step = StepInput(list(range(B)), [[0] * ql] * B, [c - ql for c in ctxs], tables, [int(ql > 1)] * B, 0, 1)
-            buf = np.zeros(2 * (T * (nq // nkv) // 64 + B + 1) + 4 * T + 6 * B + 64 + B * pages_per + 4 * 1024,
+            buf = np.zeros(2 * (T * (nq // nkv) // 64 + B + 1) + 4 * T + 6 * B + 64 + B * pages_per + 8 * 1024,
                            dtype=np.int32)
             n_int, T, _, n_items, _, n_dec, n_units = pack_meta(step, bs, nq // nkv, pages_per, buf, nkv, 148)
-            o_dec = n_int - 4 * n_units - n_dec
+            o_dec = n_int - 8 * n_units - n_dec
             dec = torch.from_numpy(buf[o_dec:o_dec + n_dec].copy()).cuda()
             units = torch.from_numpy(buf[o_dec + n_dec:n_int].copy()).cuda()
             items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
@@ -164,6 +164,7 @@ def main():
     p.add_argument("--nkv", type=int, default=8)
     p.add_argument("--splits", type=int, default=-1)
     p.add_argument("--long", type=int, default=0, help="attention: context of request 0 (skewed batch)")
+    p.add_argument("--block-size", type=int, default=16, help="attention: tokens per KV page")
     p.add_argument("--qlen", type=int, default=1, help="query tokens per request (1 = decode)")
     p.add_argument("--chunks", type=int, nargs="+", default=[1024, 16384])
     p.add_argument("--chunk-bytes", type=int, default=65536)

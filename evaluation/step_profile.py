@@ -40,9 +40,10 @@ def main(argv=None):
     p.add_argument("--lens", type=int, nargs="+", default=[512, 2048])
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--iters", type=int, default=10)
+    p.add_argument("--block-size", type=int, default=64, help="tokens per KV page")
     a = p.parse_args(argv)
     mc = ModelConfig(a.model, dtype="bf16")
-    bs = 16
+    bs = args.block_size
     w = Worker(0, mc, CacheConfig(block_size=bs), ParallelConfig(), backend="native", device="cuda:0")
     span = max(a.ctx) + 1 if a.mode == "decode" else max(a.lens)
     pages_per = (span + bs - 1) // bs

@@ -136,9 +136,9 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
   b.splits = (int)splits;
   b.dec_reqs = dec_reqs.data_ptr<int>();
   b.n_dec = dec_reqs.numel();
-  TORCH_CHECK(dec_units.numel() % 4 == 0 && dec_units.is_contiguous(), "attention: dec_units is [n, 4]");
+  TORCH_CHECK(dec_units.numel() % kDecUnitInts == 0 && dec_units.is_contiguous(), "attention: dec_units is [n, 8]");
   b.dec_units = dec_units.data_ptr<int>();
-  b.n_units = dec_units.numel() / 4;
+  b.n_units = dec_units.numel() / kDecUnitInts;
   TORCH_CHECK((int64_t)dec_o.numel() >= (int64_t)b.n_units * nq * 128, "attention: dec_o too small");
   // split-arrival counts of the decode kernel: one zeroed buffer per device,
   // returned to zero by every launch

@@ -94,7 +94,7 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   dec_count_ = torch::zeros({(int64_t)kDecCountSlots}, i32);
   const int64_t max_items = T * std::max(1, s.nq / s.nkv) / 64 + B + 1;
   const int64_t meta_ints = 2 * max_items + 4 * T + 5 * B + 1 +
-                            B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + 4 * kDecUnitSlots + 64;
+                            B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + kDecUnitInts * kDecUnitSlots + 64;
   meta_dev_ = torch::empty({meta_ints}, i32);
   tokens_dev_ = torch::empty({B}, i32);
   err_host_ = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).pinned_memory(true));
@@ -333,12 +333,12 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   cudaStream_t st = at::cuda::getCurrentCUDAStream(device_);
   KUS_CHECK(n_dec >= 0 && n_dec <= B && n_units >= n_dec && n_units <= kDecUnitSlots && (n_units > 0) == (n_dec > 0),
             "bad decode attention units");
-  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 2 * B + n_dec + 4 * n_units;
+  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 2 * B + n_dec + kDecUnitInts * n_units;
   KUS_CHECK(meta.numel() >= n_meta && n_meta <= meta_dev_.numel(), "meta buffer too small");
   check_cuda(cudaMemcpyAsync(meta_dev_.data_ptr(), meta.data_ptr(), n_meta * 4, cudaMemcpyHostToDevice, st), "meta H2D");
   // meta layout (int32): items[2n] | tokens[T] | positions[T] | kv_page[T] | kv_slot[T] |
   // q_start[B+1] | ctx_len[B] | last_idx[B] | page_table[B*max_pages] | temps[B] (f32) | seeds[B] |
-  // dec_reqs[n_dec] | dec_units[4*n_units]
+  // dec_reqs[n_dec] | dec_units[8*n_units]
   const int* m = meta_dev_.data_ptr<int>();
   const int2* items = reinterpret_cast<const int2*>(m);
   const int* tokens = m + 2 * n_items;

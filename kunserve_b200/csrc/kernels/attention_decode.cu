@@ -78,20 +78,17 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
   uint64_t* empty = full + kStages;
 
-  // work unit: (decode slot, first key block, blocks, first unit of the
-  // request << 8 | units of the request)
-  const int* unit = b.dec_units + 4 * blockIdx.x;
-  const int di = unit[0], kh = blockIdx.y;
-  const int u0 = unit[3] >> 8, n_units = unit[3] & 255;
+  // work unit: one record of independent loads (no chain through the
+  // request's metadata before the first TMA can issue)
+  const int* unit = b.dec_units + kDecUnitInts * blockIdx.x;
+  const int tok = unit[0], ctx = unit[1], req = unit[2], blk0 = unit[3];
+  const int u0 = unit[5] >> 8, n_units = unit[5] & 255;
+  const int kh = blockIdx.y;
   const int G = nq / g.kvh;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int req = b.dec_reqs[di];
-  const int tok = b.q_start[req];
-  const int ctx = b.ctx_len[req];
   const int* table = b.page_table + (size_t)req * b.max_pages;
   const int nblk = (ctx + BK - 1) / BK;
-  const int blk0 = unit[1];
-  const int nb = max(0, min(unit[2], nblk - blk0));
+  const int nb = max(0, min(unit[4], nblk - blk0));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -101,9 +98,6 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     fence_barrier_init();
   }
   __syncthreads();
-  // q and the KV pages are written by the previous kernel (RoPE + KV append)
-  pdl_wait();
-  pdl_trigger();
 
   const int box = g.block_size < BK ? g.block_size : BK;
   const int rows_per_slot = 2 * g.block_size;
@@ -127,10 +121,17 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
   };
   int issued = 0;   // blocks issued (thread 0 only)
+  // The previous kernel (RoPE + KV append) writes q and this step's new key
+  // (position ctx - 1); blocks that end before it were written by earlier
+  // steps, so their loads start before the wait on that kernel.
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmKV);
-    for (; issued < nb && issued < kStages; ++issued) issue(issued);
+    for (; issued < nb && issued < kStages && (blk0 + issued + 1) * BK <= ctx - 1; ++issued) issue(issued);
   }
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0)
+    for (; issued < nb && issued < kStages; ++issued) issue(issued);
 
   // Q rows (G heads, zero padded to 16) into shared memory, then A fragments
   uint8_t* qs = smem + kQOff;

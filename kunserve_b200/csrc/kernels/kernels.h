@@ -102,9 +102,10 @@ struct AttnBatch {
   int splits;             // KV splits per item (>1: partials + combine)
   const int* dec_reqs;    // [n_dec] requests with one query token: decode kernel
   int n_dec;
-  // [n_units, 4] decode work units: (index into dec_reqs, first key block of
-  // 64 keys, blocks, first unit of the same request << 8 | its unit count);
-  // a request's units are consecutive, at most 32 per request
+  // [n_units, kDecUnitInts] decode work units: (query token row, context
+  // length, request (page-table row), first key block of 64 keys, blocks,
+  // first unit of the same request << 8 | its unit count, index into
+  // dec_reqs, 0); a request's units are consecutive, at most 32 per request
   const int* dec_units;
   int n_units;
 };
@@ -117,6 +118,7 @@ struct AttnScratch {
   int* dec_count;         // [n_units * kvh] unit arrivals; zero between launches (the merging CTA resets it)
 };
 constexpr int kDecUnitSlots = 1024;                    // n_units bound of the engine's scratch
+constexpr int kDecUnitInts = 8;                        // ints per decode work unit
 constexpr int kDecCountSlots = kDecUnitSlots * 64;     // dec_count entries a caller provides (n_units * kvh)
 
 // q: [T, q_stride] bf16 (first nq*hd columns are the rotated queries);

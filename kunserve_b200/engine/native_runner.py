@@ -23,6 +23,7 @@ from .step import StepInput
 MAX_ENGINE_TOKENS = 16384
 ATTN_SPLIT_TOKENS = 512
 DEC_UNIT_SLOTS = 1024           # decode attention work units per step (engine scratch)
+DEC_UNIT_INTS = 8               # ints per decode work unit in the metadata
 Q_TILE_ROWS = 256      # query rows per prefill attention work item (two 128-row tiles)
 
 
@@ -75,8 +76,8 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     """Fill ``buf`` (int32) with the engine's step metadata; returns
     ``(n_ints, T, B, n_items, max_prefill_ctx, n_dec, n_units)``.  Requests
     with one query token go to the decode kernel (list and work units at the
-    end); the others become ``Q_TILE_ROWS``-row query tiles (``items``) of
-    the prefill kernel."""
+    end, ``DEC_UNIT_INTS`` ints per unit); the others become
+    ``Q_TILE_ROWS``-row query tiles (``items``) of the prefill kernel."""
     B = step.num_requests
     ql = np.fromiter((len(t) for t in step.input_tokens), dtype=np.int64, count=B)
     T = int(ql.sum())
@@ -130,7 +131,16 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     dec = np.nonzero(is_dec)[0].astype(np.int32)
     put(dec)
     units = decode_units(ctx[dec], nkv, num_sms)
-    put(units)
+    # kernel records: (token row, context, request, first block, blocks,
+    # first unit << 8 | units, decode index, 0)
+    rec = np.zeros((units.shape[0], DEC_UNIT_INTS), dtype=np.int32)
+    di = units[:, 0]
+    rec[:, 0] = q_start[dec[di]]
+    rec[:, 1] = ctx[dec[di]]
+    rec[:, 2] = dec[di]
+    rec[:, 3:6] = units[:, 1:4]
+    rec[:, 6] = di
+    put(rec)
     pre_ctx = int(ctx[~is_dec].max()) if n_items else 0
     return o, T, B, n_items, pre_ctx, int(dec.size), int(units.shape[0])
 
@@ -180,7 +190,7 @@ class NativeRunner:
             torch.cuda.synchronize()
         self.max_pages = math.ceil(sh.max_pos / layout.block_size)
         n = (2 * (sh.max_tokens * self.group // Q_TILE_ROWS + sh.max_batch + 1) + 4 * sh.max_tokens
-             + 6 * sh.max_batch + 1 + sh.max_batch * self.max_pages + 4 * DEC_UNIT_SLOTS + 64)
+             + 6 * sh.max_batch + 1 + sh.max_batch * self.max_pages + DEC_UNIT_INTS * DEC_UNIT_SLOTS + 64)
         self.meta = torch.empty(n, dtype=torch.int32, pin_memory=True)
         self.meta_np = self.meta.numpy()
         self.num_sms = C.num_sms()

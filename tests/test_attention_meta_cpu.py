@@ -81,10 +81,15 @@ def test_pack_meta_orders_items_longest_first_and_lists_units():
     # keys seen by each item's last row, non-increasing
     ends = [starts[r] + min(row0 + Q_TILE_ROWS, qlens[r] * G) // G for r, row0 in items]
     assert ends == sorted(ends, reverse=True)
-    o_dec = n - 4 * n_units - n_dec
+    o_dec = n - 8 * n_units - n_dec
     assert buf[o_dec:o_dec + n_dec].tolist() == [2, 3]
-    units = buf[o_dec + n_dec:n].reshape(n_units, 4)
-    _check_cover(units, [301, 5001])
+    rec = buf[o_dec + n_dec:n].reshape(n_units, 8)
+    _check_cover(rec[:, [6, 3, 4, 5]], [301, 5001])
+    # token row, context and request of each unit's decode request
+    q_start = np.cumsum([0] + qlens)
+    for r in rec:
+        req = [2, 3][r[6]]
+        assert (r[0], r[1], r[2], r[7]) == (q_start[req], starts[req] + 1, req, 0)
 
 
 def test_prefill_splits_stay_within_one_wave():

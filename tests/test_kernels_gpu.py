@@ -208,7 +208,7 @@ def test_paged_attention(C, nq, nkv, splits):
     if splits > 1:
         assert n_units > n_dec   # the longer decode contexts are cut into several units
     items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
-    o_dec = n_int - 4 * n_units - n_dec
+    o_dec = n_int - 8 * n_units - n_dec
     dec = torch.from_numpy(buf[o_dec:o_dec + n_dec].copy()).cuda()
     units = torch.from_numpy(buf[o_dec + n_dec:n_int].copy()).cuda()
     o = 2 * n_items + 4 * T
@@ -258,7 +258,7 @@ def test_prefill_attention_long_chunks(C, nq, nkv, splits):
     width = max(len(t) for t in tables)
     n_int, T2, B2, n_items, _, n_dec, n_units = pack_meta(step, bs, nq // nkv, width, buf, nkv, 148)
     items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
-    o_dec = n_int - 4 * n_units - n_dec
+    o_dec = n_int - 8 * n_units - n_dec
     dec = torch.from_numpy(buf[o_dec:o_dec + n_dec].copy()).cuda()
     units = torch.from_numpy(buf[o_dec + n_dec:n_int].copy()).cuda()
     o = 2 * n_items + 4 * T
