@@ -43,7 +43,7 @@ def main(argv=None):
     p.add_argument("--block-size", type=int, default=64, help="tokens per KV page")
     a = p.parse_args(argv)
     mc = ModelConfig(a.model, dtype="bf16")
-    bs = args.block_size
+    bs = a.block_size
     w = Worker(0, mc, CacheConfig(block_size=bs), ParallelConfig(), backend="native", device="cuda:0")
     span = max(a.ctx) + 1 if a.mode == "decode" else max(a.lens)
     pages_per = (span + bs - 1) // bs

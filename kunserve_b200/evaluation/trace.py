@@ -30,6 +30,16 @@ class Burst:
     factor: float        # rate multiplier inside the window
 
 
+def periodic_bursts(start: float, length: float, period: float, factor: float, duration: float) -> List[Burst]:
+    """Bursts of ``length`` seconds every ``period`` seconds from ``start``:
+    the offered load is bursty at the period's scale but stationary over
+    longer windows (mean rate x (1 + (factor - 1) * length / period))."""
+    if period <= 0:
+        return [Burst(start, length, factor)]
+    n = max(0, int(math.ceil((duration - start) / period)))
+    return [Burst(start + k * period, length, factor) for k in range(n)]
+
+
 def _rate_at(t: float, rate: float, bursts: Sequence[Burst]) -> float:
     r = rate
     for b in bursts:

@@ -5,6 +5,20 @@ from kunserve_b200.evaluation.trace import Burst, arrivals, build_trace, load_pa
 from kunserve_b200.utils.metrics import SLO, calculate_metrics, goodput, summarize
 
 
+def test_periodic_bursts_make_a_stationary_load():
+    from kunserve_b200.evaluation.trace import periodic_bursts
+    b = periodic_bursts(0.0, 1.0, 2.0, 5.0, 600.0)
+    assert len(b) == 300 and b[1].start == 2.0 and b[-1].start == 598.0
+    t = arrivals(600, 5.0, "poisson", seed=3, bursts=b)
+    # the mean over any 20 s window is close to the whole trace's mean
+    mean = t.size / 600
+    for s0 in (0, 100, 333, 500):
+        assert abs(((t >= s0) & (t < s0 + 20)).sum() / 20 - mean) < 0.3 * mean
+    on = sum(((t >= x.start) & (t < x.start + 1.0)).sum() for x in b[:100])
+    off = sum(((t >= x.start + 1.0) & (t < x.start + 2.0)).sum() for x in b[:100])
+    assert on > 3 * off
+
+
 def test_poisson_rate_and_burst():
     t = arrivals(400, 5.0, "poisson", seed=1, bursts=[Burst(100, 100, 4.0)])
     base = ((t < 100).sum() + (t >= 200).sum()) / 300
