@@ -98,7 +98,9 @@ def bench_attention(args):
             step = StepInput(list(range(B)), [[0] * ql] * B, [c - ql for c in ctxs], tables, [int(ql > 1)] * B, 0, 1)
             buf = np.zeros(2 * (T * (nq // nkv) // 64 + B + 1) + 4 * T + 6 * B + 64 + B * pages_per + 8 * 1024,
                            dtype=np.int32)
-            n_int, T, _, n_items, _, n_dec, n_units = pack_meta(step, bs, nq // nkv, pages_per, buf, nkv, 148)
+            hg_max = C.decode_attention_heads(bs, nkv) if args.dec_heads <= 0 else args.dec_heads
+            n_int, T, _, n_items, _, n_dec, n_units, hg = pack_meta(step, bs, nq // nkv, pages_per, buf, nkv, 148,
+                                                                    hg_max, 16 if args.dec_heads <= 0 else 0)
             o_dec = n_int - 8 * n_units - n_dec
             dec = torch.from_numpy(buf[o_dec:o_dec + n_dec].copy()).cuda()
             units = torch.from_numpy(buf[o_dec + n_dec:n_int].copy()).cuda()
@@ -116,14 +118,14 @@ def bench_attention(args):
             op = torch.empty(max(psplits * T, n_units) * nq * hd, device="cuda")
             ml = torch.empty(max(psplits * T, n_units) * nq * 2, device="cuda")
             fn = lambda i: C.attention(q, nq * hd, out, pool, P, 1, L, L, bs, nkv, 0, q_start, ctxl, tab, items,
-                                       psplits, op, ml, nq, 1 / math.sqrt(hd), dec, units, op, ml)
+                                       psplits, op, ml, nq, 1 / math.sqrt(hd), dec, units, op, ml, hg)
             t = timeit(fn, args.warmup, args.iters)
             kv_bytes = sum(ctxs) * nkv * hd * 2 * 2
             # causal FLOPs: query i of a request sees (ctx - ql + i + 1) keys; QK^T and PV, 2 FLOP per MAC
             keys = sum(c - ql + i + 1 for c in ctxs for i in range(ql))
             flops = 4.0 * keys * nq * hd
             print(json.dumps({"kernel": "paged_attention_" + ("decode" if ql == 1 else "prefill"), "B": B,
-                              "ctx": ctx, "long": ctxs[0] if ctxs[0] != ctx else None, "qlen": ql, "nq": nq, "nkv": nkv,
+                              "ctx": ctx, "long": ctxs[0] if ctxs[0] != ctx else None, "dec_heads": hg, "qlen": ql, "nq": nq, "nkv": nkv,
                               "splits": splits,
                               "us": round(t * 1e6, 2), "TB_s": round(kv_bytes / t / 1e12, 3),
                               "bw_frac": round(kv_bytes / t / bw, 3), "TFLOP_s": round(flops / t / 1e12, 1),
@@ -165,6 +167,7 @@ def main():
     p.add_argument("--splits", type=int, default=-1)
     p.add_argument("--long", type=int, default=0, help="attention: context of request 0 (skewed batch)")
     p.add_argument("--block-size", type=int, default=16, help="attention: tokens per KV page")
+    p.add_argument("--dec-heads", type=int, default=0, help="attention: KV heads per decode CTA (0: engine rule)")
     p.add_argument("--qlen", type=int, default=1, help="query tokens per request (1 = decode)")
     p.add_argument("--chunks", type=int, nargs="+", default=[1024, 16384])
     p.add_argument("--chunk-bytes", type=int, default=65536)

@@ -123,7 +123,7 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
                   int64_t Ls, int64_t L, int64_t block_size, int64_t nkv, int64_t layer, torch::Tensor q_start,
                   torch::Tensor ctx_len, torch::Tensor page_table, torch::Tensor items, int64_t splits,
                   torch::Tensor o_part, torch::Tensor ml_part, int64_t nq, double scale, torch::Tensor dec_reqs,
-                  torch::Tensor dec_units, torch::Tensor dec_o, torch::Tensor dec_ml) {
+                  torch::Tensor dec_units, torch::Tensor dec_o, torch::Tensor dec_ml, int64_t dec_heads) {
   c10::cuda::CUDAGuard g(q.device());
   KVGeom geo = make_geom(pool, P, N, Ls, L, block_size, nkv, 128);
   AttnBatch b;
@@ -139,6 +139,10 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
   TORCH_CHECK(dec_units.numel() % kDecUnitInts == 0 && dec_units.is_contiguous(), "attention: dec_units is [n, 8]");
   b.dec_units = dec_units.data_ptr<int>();
   b.n_units = dec_units.numel() / kDecUnitInts;
+  TORCH_CHECK((dec_heads == 1 || dec_heads == 2 || dec_heads == 4) && nkv % dec_heads == 0 &&
+                  dec_heads <= decode_attention_heads((int)block_size, (int)nkv),
+              "attention: bad decode head group");
+  b.dec_heads = (int)dec_heads;
   TORCH_CHECK((int64_t)dec_o.numel() >= (int64_t)b.n_units * nq * 128, "attention: dec_o too small");
   // split-arrival counts of the decode kernel: one zeroed buffer per device,
   // returned to zero by every launch
@@ -158,7 +162,7 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
                                attention_kv_block_keys()),
               "attention kv tensor map");
   TORCH_CHECK(make_attn_kv_map(&tkv_dec, pool.data_ptr(), pool_bytes, (int)nkv, (int)block_size,
-                               decode_attention_block_keys()),
+                               decode_attention_box_rows((int)block_size, (int)dec_heads), (int)dec_heads),
               "decode attention kv tensor map");
   paged_attention(tq, tkv, tkv_dec, bp(q), (int)q_stride, bp(out), geo, (int)layer, b, sc, q.size(0), (int)nq,
                   (float)scale, at::cuda::getCurrentCUDAStream());
@@ -404,6 +408,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nccl_unique_id", &nccl_unique_id);
   m.def("error_flag", &read_error_flag, py::arg("reset") = true);
   m.def("attention_q_rows_per_tile", &attention_q_rows_per_tile);
+  m.def("decode_attention_heads", &decode_attention_heads);
   m.def("tp_gemm_reduce_scatter", &tp_gemm_reduce_scatter_op);
   m.def("tp_allgather_gemm", &tp_allgather_gemm_op);
   m.def("tp_signal", &tp_signal_op);

@@ -155,9 +155,14 @@ void Engine::init_memory(int64_t num_pages) {
   KUS_CHECK(make_attn_kv_map(&m_attn_kv_, arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv, s_.block_size,
                              attention_kv_block_keys()),
             "tmap attention kv");
-  KUS_CHECK(make_attn_kv_map(&m_dec_kv_, arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv, s_.block_size,
-                             decode_attention_block_keys()),
-            "tmap decode attention kv");
+  // decode maps for 1, 2 and 4 KV heads per CTA, up to the page size's most
+  for (int i = 0, hg = 1; i < 3; ++i, hg *= 2) {
+    m_dec_ok_[i] = hg <= decode_attention_heads(s_.block_size, s_.nkv) && s_.nkv % hg == 0;
+    if (m_dec_ok_[i])
+      KUS_CHECK(make_attn_kv_map(&m_dec_kv_[i], arena_->kv_base(), (long long)arena_->kv_va_bytes(), s_.nkv,
+                                 s_.block_size, decode_attention_box_rows(s_.block_size, hg), hg),
+                "tmap decode attention kv");
+  }
 }
 
 void Engine::build_layer_maps(int l) {
@@ -318,7 +323,7 @@ void Engine::all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t st) {
 }
 
 std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, int64_t max_pages, int64_t n_items,
-                                     int64_t splits, int64_t n_dec, int64_t n_units, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
+                                     int64_t splits, int64_t n_dec, int64_t n_units, int64_t dec_heads, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
                                      bool first_stage, bool last_stage, int64_t sample_mode, int64_t step) {
   c10::cuda::CUDAGuard g(device_);
   char range_name[96];
@@ -378,6 +383,9 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   ab.n_dec = (int)n_dec;
   ab.dec_units = dec_units;
   ab.n_units = (int)n_units;
+  const int dec_map = dec_heads == 4 ? 2 : dec_heads == 2 ? 1 : 0;
+  KUS_CHECK((dec_heads == 1 || dec_heads == 2 || dec_heads == 4) && m_dec_ok_[dec_map], "bad decode head group");
+  ab.dec_heads = (int)dec_heads;
   AttnScratch sc{attn_o_.data_ptr<float>(), attn_ml_.data_ptr<float>(), dec_o_.data_ptr<float>(),
                  dec_ml_.data_ptr<float>(), dec_count_.data_ptr<int>()};
 
@@ -432,7 +440,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     if (np == 0) gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
     rope_append(qkv, positions, kv_page, kv_slot, cos_sin_.data_ptr<float>(), geo, ll, (int)T, s_.nq, s_.nkv,
                 s_.max_pos, st, np ? part : nullptr, np, (long long)T * qkv_n_);
-    paged_attention(m_attn_q_, m_attn_kv_, m_dec_kv_, qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
+    paged_attention(m_attn_q_, m_attn_kv_, m_dec_kv_[dec_map], qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
     if (sync_debug_) debug_check("attention", (int)T, (int)B, (int)n_dec, st);
     launches_ += 2 + (n_items > 0 ? 1 + (splits > 1 ? 1 : 0) : 0) + (n_units > 0 ? 1 : 0);
     if (fused) {

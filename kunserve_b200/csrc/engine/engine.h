@@ -72,7 +72,7 @@ class Engine {
   // One step.  `meta` is a pinned int32 tensor laid out by the Python runner
   // (see native_runner.py); returns sampled ids on the last stage.
   std::vector<int64_t> forward(torch::Tensor meta, int64_t T, int64_t B, int64_t max_pages, int64_t n_items,
-                               int64_t splits, int64_t n_dec, int64_t n_units, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
+                               int64_t splits, int64_t n_dec, int64_t n_units, int64_t dec_heads, int64_t layer_start, int64_t layer_end, int64_t fusion_size,
                                bool first_stage, bool last_stage, int64_t sample_mode, int64_t step);
   torch::Tensor hidden();                   // [max_tokens, H] residual stream (PP transfer)
   torch::Tensor logits();                   // [max_batch, V] fp32
@@ -128,7 +128,8 @@ class Engine {
   // activation TMA descriptors per token-box height (16, 32, 64, 128 rows)
   CUtensorMap m_y_[4], m_attn_[4], m_act_[4], m_ylast_[4];
   // prefill attention: queries in qkv_ and the whole reserved KV range
-  CUtensorMap m_attn_q_, m_attn_kv_, m_dec_kv_;
+  CUtensorMap m_attn_q_, m_attn_kv_, m_dec_kv_[3];   // decode maps for 1, 2, 4 KV heads per CTA
+  bool m_dec_ok_[3] = {false, false, false};
   int64_t attn_split_tokens_ = 0;
   int attn_max_splits_ = 16;
   ncclComm_t tp_comm_ = nullptr;

@@ -1,23 +1,29 @@
 // Paged decode attention: one query token per request, on the tensor cores.
 //
-// One CTA serves (work unit, KV head) for the whole GQA group of G query
-// heads; a unit is a range of key blocks of one request (long contexts are
-// cut into several units, sized by the host so that the grid is about one
-// wave whatever the mix of context lengths).  The G query rows form the M side of mma.sync m16n8k16 tiles
-// (rows G..15 are zero), so S = Q K^T and O += P V each cost one MMA per 8
-// keys / 8 dims and every K/V byte feeds all G heads.
+// One CTA serves (work unit, group of HG KV heads) for the GQA groups of
+// those heads; a unit is a range of key blocks of one request (long contexts
+// are cut into several units, sized by the host so that the grid is about
+// one wave whatever the mix of context lengths).  A head's G query rows form
+// the M side of mma.sync m16n8k16 tiles (rows G..15 are zero), so S = Q K^T
+// and O += P V each cost one MMA per 8 keys / 8 dims and every K/V byte
+// feeds all G heads.
 //
-//   thread 0   TMA producer: blocks of 64 keys, one box per page and 64-dim
-//              half for K and for V (128-byte swizzle), into a three-stage
-//              ring; mbarrier waits are bounded (common.cuh)
-//   4 warps    warp w takes keys 16w..16w+15 of every block: K fragments by
-//              ldmatrix, V fragments by ldmatrix.trans, online softmax in
-//              registers (the S accumulator layout is the A layout of P V),
-//              then the warps merge (max, sum, O) in shared memory
+//   thread 0   TMA producer: stages of 64 / HG keys of the HG heads, one box
+//              (64 dims x HG heads x page rows) per page, 64-dim half and
+//              K / V (128-byte swizzle), into a three-stage ring.  HG grows
+//              as pages shrink (decode_attention_heads) so that a box stays
+//              8 KB: 2 KB boxes held the kernel near half of HBM bandwidth.
+//              mbarrier waits are bounded (common.cuh)
+//   4 warps    warp w takes head w % HG and 16 keys of every stage: Q
+//              fragments straight from global memory, K by ldmatrix, V by
+//              ldmatrix.trans, online softmax in registers (the S
+//              accumulator layout is the A layout of P V), then the warps of
+//              each head merge (max, sum, O) in shared memory
 //
 // A request cut into several units has each unit write an unnormalized
-// partial plus (max, sum); the last of its unit CTAs to finish (per KV head),
-// found by an atomic arrival count, merges them and writes the output rows.
+// partial plus (max, sum); the last of its unit CTAs to finish (per head
+// group), found by an atomic arrival count, merges them and writes the
+// output rows.
 #include "../common.cuh"
 #include "kernels.h"
 
@@ -32,8 +38,7 @@ constexpr int kStages = 3;
 constexpr int kHalf = BK * 128;           // one 64-dim half of a block (8 KB)
 constexpr int kTile = 2 * kHalf;          // K or V of one block (16 KB)
 constexpr int kStageBytes = 2 * kTile;    // K and V
-constexpr int kQOff = kStages * kStageBytes;
-constexpr int kBarOff = kQOff + 16 * 256;
+constexpr int kBarOff = kStages * kStageBytes;
 constexpr int kSmemBytes = kBarOff + 64 + 1024;
 
 KUS_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
@@ -60,18 +65,24 @@ KUS_DEVICE void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uin
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Byte offset of 16-byte chunk `ch` (0..15 over the 128 dims) of key row `r`
-// in a block tile written by TMA with 128-byte swizzle: [half][row][128 B].
+// Byte offset of 16-byte chunk `ch` (0..15 over the 128 dims) of tile row
+// `r` in a stage written by TMA with 128-byte swizzle: [half][row][128 B].
+// A tile row is one (key, head) pair: row = key * HG + head.
 KUS_DEVICE uint32_t kv_swz(int r, int ch) {
   return (uint32_t)((ch >> 3) * kHalf + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
-// Q tile: 16 rows of 256 B, chunks XOR-swizzled by row.
-KUS_DEVICE uint32_t q_swz(int r, int ch) { return (uint32_t)(r * 256 + ((ch ^ (r & 7)) << 4)); }
 
+// HG KV heads per CTA (1, 2 or 4): each stage holds 64 / HG keys of all HG
+// heads, so one TMA box (64 dims x HG heads x page rows) is 8 KB even with
+// 16-token pages.  Warp w takes head w % HG and keys 16 (w / HG) .. +15 of
+// every stage.
+template <int HG>
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ CUtensorMap tmKV,
                                                                const __nv_bfloat16* __restrict__ q, int q_stride,
                                                                __nv_bfloat16* __restrict__ out, KVGeom g, int layer,
                                                                AttnBatch b, AttnScratch sc, int nq, float scale_log2) {
+  constexpr int KPS = BK / HG;             // keys per stage
+  constexpr int kSub = kWarps / HG;        // warps per head
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -83,12 +94,15 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   const int* unit = b.dec_units + kDecUnitInts * blockIdx.x;
   const int tok = unit[0], ctx = unit[1], req = unit[2], blk0 = unit[3];
   const int u0 = unit[5] >> 8, n_units = unit[5] & 255;
-  const int kh = blockIdx.y;
+  const int kh0 = blockIdx.y * HG;
   const int G = nq / g.kvh;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int wh = warp % HG, wk = warp / HG;   // this warp's head in the group and key quarter
   const int* table = b.page_table + (size_t)req * b.max_pages;
   const int nblk = (ctx + BK - 1) / BK;
   const int nb = max(0, min(unit[4], nblk - blk0));
+  const int key_lo = blk0 * BK;
+  const int nst = nb > 0 ? (min((blk0 + nb) * BK, ctx) - key_lo + KPS - 1) / KPS : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -99,14 +113,14 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
   __syncthreads();
 
-  const int box = g.block_size < BK ? g.block_size : BK;
+  const int box = g.block_size < KPS ? g.block_size : KPS;
   const int rows_per_slot = 2 * g.block_size;
-  auto issue = [&](int i) {   // thread 0: K and V of block i into stage i % kStages
+  auto issue = [&](int i) {   // thread 0: K and V of stage i into ring slot i % kStages
     const int s = i % kStages;
     mbar_arrive_expect_tx(&full[s], kStageBytes);
-    const int key_blk = (blk0 + i) * BK;
-    for (int j = 0; j * box < BK; ++j) {
-      const int key0 = key_blk + j * box;
+    const int key_st = key_lo + i * KPS;
+    for (int j = 0; j * box < KPS; ++j) {
+      const int key0 = key_st + j * box;
       // keys past the context read the request's first page: finite
       // values that the mask turns into p = 0
       const bool in = key0 < ctx;
@@ -116,43 +130,45 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
       for (int kv = 0; kv < 2; ++kv)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          tma_load_3d(sbase + s * kStageBytes + kv * kTile + h * kHalf + j * box * 128, &tmKV, &full[s], 64 * h, kh,
-                      row + kv * g.block_size);
+          tma_load_3d(sbase + s * kStageBytes + kv * kTile + h * kHalf + j * box * HG * 128, &tmKV, &full[s], 64 * h,
+                      kh0, row + kv * g.block_size);
     }
   };
-  int issued = 0;   // blocks issued (thread 0 only)
+  int issued = 0;   // stages issued (thread 0 only)
   // The previous kernel (RoPE + KV append) writes q and this step's new key
-  // (position ctx - 1); blocks that end before it were written by earlier
+  // (position ctx - 1); stages that end before it were written by earlier
   // steps, so their loads start before the wait on that kernel.
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmKV);
-    for (; issued < nb && issued < kStages && (blk0 + issued + 1) * BK <= ctx - 1; ++issued) issue(issued);
+    for (; issued < nst && issued < kStages && key_lo + (issued + 1) * KPS <= ctx - 1; ++issued) issue(issued);
   }
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x == 0)
-    for (; issued < nb && issued < kStages; ++issued) issue(issued);
+    for (; issued < nst && issued < kStages; ++issued) issue(issued);
 
-  // Q rows (G heads, zero padded to 16) into shared memory, then A fragments
-  uint8_t* qs = smem + kQOff;
-  for (int c = threadIdx.x; c < 16 * 16; c += kThreads) {
-    const int r = c >> 4, ch = c & 15;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < G) v = *reinterpret_cast<const uint4*>(q + (size_t)tok * q_stride + (size_t)(kh * G + r) * HD + ch * 8);
-    *reinterpret_cast<uint4*>(qs + q_swz(r, ch)) = v;
-  }
-  __syncthreads();
+  // A fragments of this warp's head: its G query rows (zero padded to 16),
+  // loaded straight from global memory in the m16n8k16 A layout
   uint32_t qf[8][4];
+  {
+    const int r0 = lane >> 2, c0 = 2 * (lane & 3);
+    const __nv_bfloat16* qh = q + (size_t)tok * q_stride + (size_t)(kh0 + wh) * G * HD;
 #pragma unroll
-  for (int ks = 0; ks < 8; ++ks)
-    ldsm_x4(sbase + kQOff + q_swz(lane & 15, ks * 2 + (lane >> 4)), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+    for (int ks = 0; ks < 8; ++ks) {
+      const int c = ks * 16 + c0;
+      qf[ks][0] = r0 < G ? *reinterpret_cast<const uint32_t*>(qh + (size_t)r0 * HD + c) : 0u;
+      qf[ks][1] = r0 + 8 < G ? *reinterpret_cast<const uint32_t*>(qh + (size_t)(r0 + 8) * HD + c) : 0u;
+      qf[ks][2] = r0 < G ? *reinterpret_cast<const uint32_t*>(qh + (size_t)r0 * HD + c + 8) : 0u;
+      qf[ks][3] = r0 + 8 < G ? *reinterpret_cast<const uint32_t*>(qh + (size_t)(r0 + 8) * HD + c + 8) : 0u;
+    }
+  }
 
   float o[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
   bool ok = true;
-  for (int i = 0; i < nb; ++i) {
+  for (int i = 0; i < nst; ++i) {
     const int s = i % kStages;
     const uint32_t ph = (uint32_t)(i / kStages) & 1u;
     ok = __all_sync(0xffffffffu, ok && mbar_wait(&full[s], ph, kErrWaitFull));
@@ -161,14 +177,14 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     float sfr[2][4] = {};
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
-      const int key = warp * 16 + ((lane >> 4) << 3) + (lane & 7);
+      const int key = wk * 16 + ((lane >> 4) << 3) + (lane & 7);
       uint32_t b0, b1, b2, b3;
-      ldsm_x4(kt + kv_swz(key, ks * 2 + ((lane >> 3) & 1)), b0, b1, b2, b3);
+      ldsm_x4(kt + kv_swz(key * HG + wh, ks * 2 + ((lane >> 3) & 1)), b0, b1, b2, b3);
       mma16816(sfr[0], qf[ks], b0, b1);
       mma16816(sfr[1], qf[ks], b2, b3);
     }
     // online softmax over the warp's 16 keys (rows lane/4 and lane/4 + 8)
-    const int key_base = (blk0 + i) * BK + warp * 16 + 2 * (lane & 3);
+    const int key_base = key_lo + i * KPS + wk * 16 + 2 * (lane & 3);
     float mx_lo = -INFINITY, mx_hi = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
@@ -214,21 +230,21 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     // O += P V over the warp's 16 keys
 #pragma unroll
     for (int dp = 0; dp < 8; ++dp) {
-      const int key = warp * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int key = wk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
       uint32_t b0, b1, b2, b3;
-      ldsm_x4_t(vt + kv_swz(key, dp * 2 + (lane >> 4)), b0, b1, b2, b3);
+      ldsm_x4_t(vt + kv_swz(key * HG + wh, dp * 2 + (lane >> 4)), b0, b1, b2, b3);
       mma16816(o[2 * dp], pa, b0, b1);
       mma16816(o[2 * dp + 1], pa, b2, b3);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (threadIdx.x == 0 && i + kStages < nb && ok) {
-      // refill this stage once every warp released it
+    if (threadIdx.x == 0 && i + kStages < nst && ok) {
+      // refill this slot once every warp released it
       if (mbar_wait(&empty[s], ph, kErrWaitEmpty)) issue(issued++);
     }
   }
   if (threadIdx.x == 0 && !ok) {
-    // after a timed-out wait the last issued blocks may still be in flight:
+    // after a timed-out wait the last issued stages may still be in flight:
     // let them land (bounded) before the shared memory is reused
     for (int i = max(0, issued - kStages); i < issued; ++i)
       mbar_wait(&full[i % kStages], (uint32_t)(i / kStages) & 1u, kErrWaitFull);
@@ -258,21 +274,24 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     o_s[(warp * 16 + r_lo + 8) * HD + d + 1] = o[dt][3];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * HD; i += kThreads) {
-    const int h = i / HD, d = i % HD;
+  // merge the warps of each head; rows of the group are q heads kh0*G ..
+  for (int i = threadIdx.x; i < HG * G * HD; i += kThreads) {
+    const int hr = i / HD, d = i % HD;
+    const int h = hr / G, r = hr % G;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, m_s[w * 16 + h]);
+    for (int j = 0; j < kSub; ++j) M = fmaxf(M, m_s[(h + HG * j) * 16 + r]);
     float L = 0.f, A = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float f = exp2f(m_s[w * 16 + h] - M);
-        L += l_s[w * 16 + h] * f;
-        A += o_s[(w * 16 + h) * HD + d] * f;
+      for (int j = 0; j < kSub; ++j) {
+        const int w = h + HG * j;
+        const float f = exp2f(m_s[w * 16 + r] - M);
+        L += l_s[w * 16 + r] * f;
+        A += o_s[(w * 16 + r) * HD + d] * f;
       }
     }
-    const int head = kh * G + h;
+    const int head = kh0 * G + hr;
     if (n_units == 1) {
       if (ok) out[(size_t)tok * nq * HD + (size_t)head * HD + d] = f2bf(L > 0.f ? A / L : 0.f);
     } else {
@@ -285,15 +304,15 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
   }
   if (n_units == 1) return;
-  // The last unit CTA of this (request, KV head) to finish merges the
-  // partials of all the request's units (G x 128 values each, read from L2):
-  // no separate combine launch.  Every CTA arrives (waits are bounded), so
-  // the counter is back at zero after each launch.
+  // The last unit CTA of this (request, head group) to finish merges the
+  // partials of all the request's units (HG x G x 128 values each, read from
+  // L2): no separate combine launch.  Every CTA arrives (waits are bounded),
+  // so the counter is back at zero after each launch.
   __shared__ int last_s;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();   // publish this CTA's partial before counting it
-    int* cnt = sc.dec_count + u0 * g.kvh + kh;
+    int* cnt = sc.dec_count + u0 * g.kvh + blockIdx.y;
     const bool last = atomicAdd(cnt, 1) == n_units - 1;
     if (last) *cnt = 0;
     last_s = last;
@@ -301,11 +320,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   __syncthreads();
   if (!last_s) return;
   __threadfence();
-  // one warp per head row of the group: lane s holds unit s's (max, sum),
+  // one warp per query row of the group: lane s holds unit s's (max, sum),
   // lane l accumulates dims 4l..4l+3, all units' loads in flight
   const size_t plane = (size_t)nq;
-  for (int h = warp; h < G; h += kWarps) {
-    const size_t row = (size_t)u0 * nq + kh * G + h;
+  for (int hr = warp; hr < HG * G; hr += kWarps) {
+    const size_t row = (size_t)u0 * nq + kh0 * G + hr;
     float m = -INFINITY, l = 0.f;
     if (lane < n_units) {
       const float2 ml = __ldcg(reinterpret_cast<const float2*>(sc.dec_ml) + lane * plane + row);
@@ -333,7 +352,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     uint2 u;
     u.x = pack_bf16x2(acc.x * inv, acc.y * inv);
     u.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(out + (size_t)tok * nq * HD + (size_t)(kh * G + h) * HD + 4 * lane) = u;
+    *reinterpret_cast<uint2*>(out + (size_t)tok * nq * HD + (size_t)(kh0 * G + hr) * HD + 4 * lane) = u;
   }
 }
 
@@ -341,18 +360,43 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
 
 int decode_attention_block_keys() { return dec::BK; }
 
+int decode_attention_heads(int block_size, int kvh) {
+  // enough heads per CTA for 8 KB boxes (64 rows of 128 B), dividing kvh
+  const int want = block_size >= dec::BK ? 1 : dec::BK / block_size;
+  for (int hg = 4; hg > 1; hg /= 2)
+    if (hg <= want && kvh % hg == 0) return hg;
+  return 1;
+}
+
+int decode_attention_box_rows(int block_size, int heads) {
+  const int kps = dec::BK / heads;
+  return block_size < kps ? block_size : kps;
+}
+
+template <int HG>
+static void launch_decode(const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out,
+                          const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int nq, float sl2,
+                          cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(dec::decode_attn_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
+    attr = true;
+  }
+  launch_k(dec::decode_attn_kernel<HG>, dim3(b.n_units, g.kvh / HG), dim3(dec::kThreads), dec::kSmemBytes, s, tmKV,
+           q, q_stride, out, g, layer, b, sc, nq, sl2);
+}
+
 void paged_decode_attention(const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out,
                             const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int nq, float scale,
                             cudaStream_t s) {
   if (b.n_units <= 0) return;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(dec::decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
-    attr = true;
-  }
   const float sl2 = scale * 1.4426950408889634f;
-  launch_k(dec::decode_attn_kernel, dim3(b.n_units, g.kvh), dim3(dec::kThreads), dec::kSmemBytes, s, tmKV,
-           q, q_stride, out, g, layer, b, sc, nq, sl2);
+  // the tensor map was built for this head count
+  switch (b.dec_heads) {
+    case 4: launch_decode<4>(tmKV, q, q_stride, out, g, layer, b, sc, nq, sl2, s); break;
+    case 2: launch_decode<2>(tmKV, q, q_stride, out, g, layer, b, sc, nq, sl2, s); break;
+    default: launch_decode<1>(tmKV, q, q_stride, out, g, layer, b, sc, nq, sl2, s); break;
+  }
 }
 
 }  // namespace kus

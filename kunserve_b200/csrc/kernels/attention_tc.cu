@@ -470,14 +470,15 @@ bool make_attn_q_map(CUtensorMap* map, const void* q, int tokens, int nq, int q_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size, int max_rows) {
+bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size, int max_rows,
+                      int heads) {
   auto fn = gemm_impl::get_encode_fn();
   const long long row_bytes = (long long)kvh * fatc::HD * 2;
   const int box_rows = block_size < max_rows ? block_size : max_rows;
-  if (!fn || box_rows <= 0 || max_rows % box_rows) return false;
+  if (!fn || box_rows <= 0 || max_rows % box_rows || heads <= 0 || kvh % heads) return false;
   cuuint64_t dims[3] = {(cuuint64_t)fatc::HD, (cuuint64_t)kvh, (cuuint64_t)(bytes / row_bytes)};
   cuuint64_t strides[2] = {(cuuint64_t)fatc::HD * 2, (cuuint64_t)row_bytes};
-  cuuint32_t box[3] = {64, 1, (cuuint32_t)box_rows};
+  cuuint32_t box[3] = {64, (cuuint32_t)heads, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -108,6 +108,7 @@ struct AttnBatch {
   // dec_reqs, 0); a request's units are consecutive, at most 32 per request
   const int* dec_units;
   int n_units;
+  int dec_heads = 1;      // KV heads per decode CTA (1, 2 or 4; the decode map is built for it)
 };
 
 struct AttnScratch {
@@ -133,8 +134,13 @@ bool make_attn_q_map(CUtensorMap* map, const void* q, int tokens, int nq, int q_
 // 3-D map over a KV pool viewed as [rows][kvh][128 dims], one row per token
 // slot; boxes of min(block_size, max_rows) rows (128 for prefill tiles,
 // decode_attention_block_keys() for decode).
-bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size, int max_rows);
+bool make_attn_kv_map(CUtensorMap* map, const void* base, long long bytes, int kvh, int block_size, int max_rows,
+                      int heads = 1);
 int decode_attention_block_keys();
+// Most KV heads per decode CTA for a page size (1, 2 or 4, dividing kvh:
+// enough for 8 KB TMA boxes), and the decode map's box rows for a head count
+int decode_attention_heads(int block_size, int kvh);
+int decode_attention_box_rows(int block_size, int heads);
 int attention_kv_block_keys();   // keys per prefill K/V block (its map's box rows)
 int attention_q_rows_per_tile();
 // Decode requests of the batch only (attention_decode.cu); paged_attention

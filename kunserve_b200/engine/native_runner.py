@@ -24,6 +24,10 @@ MAX_ENGINE_TOKENS = 16384
 ATTN_SPLIT_TOKENS = 512
 DEC_UNIT_SLOTS = 1024           # decode attention work units per step (engine scratch)
 DEC_UNIT_INTS = 8               # ints per decode work unit in the metadata
+# decode CTAs cover several KV heads (larger TMA boxes with small pages) only
+# when the batch holds at least this many 64-key blocks x KV heads per SM:
+# below it the grid would be too small to hide the kernel's latency
+DEC_WIDE_MIN_BLOCKS_PER_SM = 16
 Q_TILE_ROWS = 256      # query rows per prefill attention work item (two 128-row tiles)
 
 
@@ -31,6 +35,7 @@ def decode_units(ctx: np.ndarray, nkv: int, num_sms: int) -> np.ndarray:
     """Work units of the decode attention kernel for requests with contexts
     ``ctx`` (decode-list order): int32 rows (decode index, first 64-key
     block, blocks, first unit of the request << 8 | the request's units).
+    ``nkv`` is the number of decode CTAs per unit (KV heads / heads per CTA).
 
     Each request is cut into units of about one CTA slot's share of the
     whole batch's keys (the kernel keeps two CTAs per SM: about 100 KB of
@@ -72,9 +77,11 @@ def prefill_splits(T: int, n_items: int, max_ctx: int, nkv: int, num_sms: int) -
 
 
 def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf: np.ndarray, nkv: int,
-              num_sms: int):
+              num_sms: int, hg_max: int = 1, wide_min_blocks: int = DEC_WIDE_MIN_BLOCKS_PER_SM):
     """Fill ``buf`` (int32) with the engine's step metadata; returns
-    ``(n_ints, T, B, n_items, max_prefill_ctx, n_dec, n_units)``.  Requests
+    ``(n_ints, T, B, n_items, max_prefill_ctx, n_dec, n_units, dec_heads)``;
+    ``dec_heads`` (KV heads per decode CTA, up to ``hg_max``) is chosen from
+    the batch's decode work.  Requests
     with one query token go to the decode kernel (list and work units at the
     end, ``DEC_UNIT_INTS`` ints per unit); the others become
     ``Q_TILE_ROWS``-row query tiles (``items``) of the prefill kernel."""
@@ -130,7 +137,10 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     put(seeds.astype(np.uint32).view(np.int32))
     dec = np.nonzero(is_dec)[0].astype(np.int32)
     put(dec)
-    units = decode_units(ctx[dec], nkv, num_sms)
+    hg = 1
+    if dec.size and hg_max > 1 and int(((ctx[dec] + 63) // 64).sum()) * nkv >= wide_min_blocks * num_sms:
+        hg = hg_max
+    units = decode_units(ctx[dec], nkv // hg, num_sms)
     # kernel records: (token row, context, request, first block, blocks,
     # first unit << 8 | units, decode index, 0)
     rec = np.zeros((units.shape[0], DEC_UNIT_INTS), dtype=np.int32)
@@ -142,7 +152,7 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     rec[:, 6] = di
     put(rec)
     pre_ctx = int(ctx[~is_dec].max()) if n_items else 0
-    return o, T, B, n_items, pre_ctx, int(dec.size), int(units.shape[0])
+    return o, T, B, n_items, pre_ctx, int(dec.size), int(units.shape[0]), hg
 
 
 class NativeRunner:
@@ -194,6 +204,8 @@ class NativeRunner:
         self.meta = torch.empty(n, dtype=torch.int32, pin_memory=True)
         self.meta_np = self.meta.numpy()
         self.num_sms = C.num_sms()
+        # most KV heads one decode CTA may cover with this page size
+        self.dec_hg_max = C.decode_attention_heads(layout.block_size, sh.nkv)
         self.ext_pages = 0
         self.fusion_size = 1
         self.gpu_ms = 0.0      # device time inside forward(), summed over steps
@@ -257,8 +269,9 @@ class NativeRunner:
     def step(self, step: StepInput, recv_from: Optional[Tuple[str, int]] = None,
              send_to: Optional[Tuple[str, int]] = None, last_stage: bool = True) -> Optional[List[int]]:
         width = max([len(p) for p in step.page_tables] + [1])
-        n, T, B, n_items, max_ctx, n_dec, n_units = pack_meta(step, self.layout.block_size, self.group, width,
-                                                              self.meta_np, self.shape.nkv, self.num_sms)
+        n, T, B, n_items, max_ctx, n_dec, n_units, dec_heads = pack_meta(
+            step, self.layout.block_size, self.group, width, self.meta_np, self.shape.nkv, self.num_sms,
+            self.dec_hg_max)
         splits = self._splits(T, n_items, max_ctx) if n_items else 1
         first = recv_from is None
         if not first:
@@ -271,7 +284,7 @@ class NativeRunner:
         if self._ev is None:
             self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         self._ev[0].record()
-        out = self.eng.forward(self.meta, T, B, width, n_items, splits, n_dec, n_units, step.layer_start,
+        out = self.eng.forward(self.meta, T, B, width, n_items, splits, n_dec, n_units, dec_heads, step.layer_start,
                                step.layer_end, step.fusion_size, first, last_stage, sample_mode, step.step_id)
         # the forward returned after its device work (it reads the sampled ids
         # back), so this bracket is the step's time on the GPU

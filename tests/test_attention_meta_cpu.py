@@ -73,7 +73,8 @@ def test_pack_meta_orders_items_longest_first_and_lists_units():
     step = StepInput(list(range(4)), [[0] * n for n in qlens], starts, tables, [1, 1, 0, 0], 0, 1)
     buf = np.zeros(20000, dtype=np.int32)
     width = max(len(t) for t in tables)
-    n, T, B, n_items, pre_ctx, n_dec, n_units = pack_meta(step, bs, G, width, buf, 8, 148)
+    n, T, B, n_items, pre_ctx, n_dec, n_units, hg = pack_meta(step, bs, G, width, buf, 8, 148)
+    assert hg == 1
     assert (T, B, n_dec) == (702, 4, 2)
     assert pre_ctx == 1100   # decode contexts do not count for prefill splits
     items = buf[:2 * n_items].reshape(n_items, 2)
@@ -90,6 +91,18 @@ def test_pack_meta_orders_items_longest_first_and_lists_units():
     for r in rec:
         req = [2, 3][r[6]]
         assert (r[0], r[1], r[2], r[7]) == (q_start[req], starts[req] + 1, req, 0)
+
+
+def test_wide_decode_ctas_only_for_large_batches():
+    bs, G = 16, 4
+    for n, ctx, want in ((2, 300, 1), (64, 2048, 4)):
+        tables = [list(range(k * 200, k * 200 + (ctx + bs - 1) // bs)) for k in range(n)]
+        step = StepInput(list(range(n)), [[0]] * n, [ctx - 1] * n, tables, [0] * n, 0, 1)
+        buf = np.zeros(40000, dtype=np.int32)
+        *_, n_units, hg = pack_meta(step, bs, G, max(len(t) for t in tables), buf, 8, 148, hg_max=4)
+        assert hg == want
+        units = decode_units(np.full(n, ctx), 8 // hg, 148)
+        assert n_units == len(units)
 
 
 def test_prefill_splits_stay_within_one_wave():

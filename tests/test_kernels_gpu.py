@@ -180,7 +180,10 @@ def _ref_attention(q, pool, lay, N, layer, tables, starts, qlens, nq, nkv, hd):
 
 @pytest.mark.parametrize("nq,nkv", [(4, 2), (8, 1), (4, 4)])
 @pytest.mark.parametrize("splits", [1, 3])
-def test_paged_attention(C, nq, nkv, splits):
+@pytest.mark.parametrize("wide", [False, True])
+def test_paged_attention(C, nq, nkv, splits, wide):
+    """Mixed prefill + decode batch; decode contexts cut into several units
+    (splits=3); decode CTAs over one or several KV heads (wide)."""
     import numpy as np
     from kunserve_b200.engine.native_runner import pack_meta
     from kunserve_b200.engine.step import StepInput
@@ -204,7 +207,9 @@ def test_paged_attention(C, nq, nkv, splits):
     buf = np.zeros(4096, dtype=np.int32)
     G = nq // nkv
     width = max(len(t) for t in tables)
-    n_int, T2, B, n_items, _, n_dec, n_units = pack_meta(step, bs, G, width, buf, nkv, 148)
+    hg_max = C.decode_attention_heads(bs, nkv) if wide else 1
+    n_int, T2, B, n_items, _, n_dec, n_units, hg = pack_meta(step, bs, G, width, buf, nkv, 148, hg_max, 0)
+    assert hg == hg_max
     if splits > 1:
         assert n_units > n_dec   # the longer decode contexts are cut into several units
     items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
@@ -224,7 +229,7 @@ def test_paged_attention(C, nq, nkv, splits):
     dec_o = torch.empty(max(n_units, 1) * nq * hd, device="cuda")
     dec_ml = torch.empty(max(n_units, 1) * nq * 2, device="cuda")
     C.attention(q, nq * hd, out, pool, P, N, L, L, bs, nkv, layer, q_start, ctx, tab.cuda(), items, 1,
-                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, units, dec_o, dec_ml)
+                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, units, dec_o, dec_ml, hg)
     torch.cuda.synchronize()
     ref = _ref_attention(q, pool, lay, N, layer, tables, starts, qlens, nq, nkv, hd)
     assert _rel(out.view(T, nq, hd), ref) < 2e-2
@@ -256,7 +261,7 @@ def test_prefill_attention_long_chunks(C, nq, nkv, splits):
     step = StepInput(list(range(B)), [[0] * n for n in qlens], starts, tables, [1] * B, 0, 1)
     buf = np.zeros(16384, dtype=np.int32)
     width = max(len(t) for t in tables)
-    n_int, T2, B2, n_items, _, n_dec, n_units = pack_meta(step, bs, nq // nkv, width, buf, nkv, 148)
+    n_int, T2, B2, n_items, _, n_dec, n_units, hg = pack_meta(step, bs, nq // nkv, width, buf, nkv, 148)
     items = torch.from_numpy(buf[:2 * n_items].reshape(n_items, 2).copy()).cuda()
     o_dec = n_int - 8 * n_units - n_dec
     dec = torch.from_numpy(buf[o_dec:o_dec + n_dec].copy()).cuda()
@@ -273,7 +278,7 @@ def test_prefill_attention_long_chunks(C, nq, nkv, splits):
     dec_o = torch.empty(max(n_units, 1) * nq * hd, device="cuda")
     dec_ml = torch.empty(max(n_units, 1) * nq * 2, device="cuda")
     C.attention(q, nq * hd, out, pool, P, N, L, L, bs, nkv, 1, q_start, ctx, tab.cuda(), items, splits,
-                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, units, dec_o, dec_ml)
+                o_part, ml, nq, 1.0 / math.sqrt(hd), dec, units, dec_o, dec_ml, hg)
     torch.cuda.synchronize()
     from kunserve_b200.ops import check_error
     check_error()
