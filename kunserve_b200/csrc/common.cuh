@@ -9,6 +9,7 @@
 // GPU.
 #pragma once
 #include <cstdint>
+#include <mutex>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -82,6 +83,35 @@ inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
   cfg.attrs = attr;
   cfg.numAttrs = pdl_flag() ? 1 : 0;
   cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) belongs to the current
+// device's context, so a process that drives several GPUs needs it once per
+// (kernel, device).  Returns the cudaError_t of the first call on a device.
+inline int ensure_smem_attr(const void* kern, int bytes) {
+  constexpr int kMaxDev = 64;
+  constexpr int kSlots = 256;
+  static std::mutex mu;
+  static const void* keys[kSlots] = {};
+  static uint64_t done[kSlots] = {};   // bit d: set on device d
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev)
+    return (int)cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  std::lock_guard<std::mutex> lock(mu);
+  int slot = -1;
+  for (int i = 0; i < kSlots; ++i) {
+    if (keys[i] == kern || keys[i] == nullptr) {
+      slot = i;
+      break;
+    }
+  }
+  if (slot >= 0 && keys[slot] == kern && (done[slot] >> dev & 1ull)) return 0;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && slot >= 0) {
+    keys[slot] = kern;
+    done[slot] |= 1ull << dev;
+  }
+  return (int)e;
 }
 
 KUS_DEVICE uint32_t smem_u32(const void* p) {

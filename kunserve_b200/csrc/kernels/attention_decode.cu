@@ -377,11 +377,7 @@ template <int HG>
 static void launch_decode(const CUtensorMap& tmKV, const __nv_bfloat16* q, int q_stride, __nv_bfloat16* out,
                           const KVGeom& g, int layer, const AttnBatch& b, const AttnScratch& sc, int nq, float sl2,
                           cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(dec::decode_attn_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
-    attr = true;
-  }
+  ensure_smem_attr(reinterpret_cast<const void*>(dec::decode_attn_kernel<HG>), dec::kSmemBytes);
   launch_k(dec::decode_attn_kernel<HG>, dim3(b.n_units, g.kvh / HG), dim3(dec::kThreads), dec::kSmemBytes, s, tmKV,
            q, q_stride, out, g, layer, b, sc, nq, sl2);
 }

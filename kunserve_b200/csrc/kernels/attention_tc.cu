@@ -501,11 +501,7 @@ void paged_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, const CUte
 void paged_prefill_attention(const CUtensorMap& tmQ, const CUtensorMap& tmKV, __nv_bfloat16* out, const KVGeom& g,
                              int layer, const AttnBatch& b, const AttnScratch& sc, int T, int nq, float scale,
                              cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(fatc::fa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::kSmemBytes);
-    attr = true;
-  }
+  ensure_smem_attr(reinterpret_cast<const void*>(fatc::fa_kernel), fatc::kSmemBytes);
   const float scale_log2 = scale * 1.4426950408889634f;
   launch_k(fatc::fa_kernel, dim3(g.kvh, b.n_items, b.splits), dim3(fatc::kThreads), fatc::kSmemBytes, s, tmQ, tmKV,
            out, g, layer, b, sc, T, nq, scale_log2);

@@ -41,6 +41,8 @@ extern "C" int kus_gemm_bf16_noalloc(const void* A, int lda, const void* B, int 
   if (M <= 0 || N <= 0 || K <= 0 || K % 8 || lda % 8 || ldb % 8 || ldc % 8 || lda < K || ldb < K || ldc < N)
     return KUS_NOALLOC_ERR_ARGS;
   if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)C) & 15u) return KUS_NOALLOC_ERR_ALIGN;
+  // an earlier, unrelated failure must not be reported as this call's
+  (void)cudaGetLastError();
   void* scratch = nullptr;
   int rc = noalloc::scratch_for_current_device(&scratch);
   if (rc) return rc;
@@ -61,4 +63,16 @@ extern "C" int kus_gemm_bf16_noalloc(const void* A, int lda, const void* B, int 
     return KUS_NOALLOC_ERR_TMAP;
   run_gemm(p, stream);
   return (int)cudaGetLastError();
+}
+
+extern "C" long long kus_noalloc_error_flag(int reset) {
+  int code = 0, info = 0;
+  if (cudaMemcpyFromSymbol(&code, kus::g_kus_error, sizeof(int)) != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&info, kus::g_kus_error_info, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(kus::g_kus_error, &zero, sizeof(int)) != cudaSuccess) return -1;
+    if (cudaMemcpyToSymbol(kus::g_kus_error_info, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return (long long)code | ((long long)info << 8);
 }

@@ -33,8 +33,18 @@
 // different streams, or from different host threads without ordering)
 // race on it; order them on one stream.
 //
-// Returns 0 on success, a negative KUS_NOALLOC_ERR_* code for a rejected
-// argument, or a positive cudaError_t from the CUDA runtime.
+// Errors: the call returns 0 on success, a negative KUS_NOALLOC_ERR_* code
+// for a rejected argument, or a positive cudaError_t from the CUDA runtime
+// for its own launch (a pending, non-sticky error left by earlier CUDA work
+// of the calling thread is cleared on entry so that it is not reported as
+// this call's).  The kernel's pipeline waits are bounded: a wait that runs
+// out, or a wait that starts after any kernel of this library in this
+// process has already recorded an error, gives up and leaves C incomplete.
+// So after synchronizing `stream`, read the library's device error flag
+// with kus_noalloc_error_flag(): a nonzero value means C is not valid.
+// Passing reset = 1 clears the flag (do so only with no kernel of this
+// library running on the device).  That function copies 8 bytes from the
+// device synchronously and allocates nothing.
 #pragma once
 #include <cuda_runtime.h>
 
@@ -56,6 +66,12 @@ extern "C" {
 __attribute__((visibility("default"))) int kus_gemm_bf16_noalloc(const void* A, int lda, const void* B, int ldb,
                                                                  void* C, int ldc, int M, int N, int K,
                                                                  cudaStream_t stream);
+
+/* The current device's library error flag: 0 when no kernel of this library
+   recorded an error, else (code | info << 8); code 1-4 is a pipeline wait that
+   gave up, 5 a peer flag, 6 a bounds check.  Returns -1 when the flag cannot
+   be read (the CUDA error is then pending for cudaGetLastError). */
+__attribute__((visibility("default"))) long long kus_noalloc_error_flag(int reset);
 
 #ifdef __cplusplus
 }

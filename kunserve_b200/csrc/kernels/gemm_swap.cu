@@ -332,11 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int BNT, int EPI>
 void launch_swap(const GemmPlan& p, cudaStream_t s) {
   using C = SCfg<BNT>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(gemm_swap_kernel<BNT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    attr = true;
-  }
+  ensure_smem_attr(reinterpret_cast<const void*>(gemm_swap_kernel<BNT, EPI>), C::kSmemBytes);
   launch_k(gemm_swap_kernel<BNT, EPI>, dim3(p.grid), dim3(kThreads), C::kSmemBytes, s, p.tmA, p.tmB, p.args);
 }
 

@@ -584,11 +584,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 template <int BN, int EPI, int GW = 0>
 void launch(const GemmPlan& p, cudaStream_t stream) {
   using C = Cfg<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemm_kernel<BN, EPI, GW>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-    attr_set = true;
-  }
+  ensure_smem_attr(reinterpret_cast<const void*>(gemm_kernel<BN, EPI, GW>), C::kSmemBytes);
   launch_k(gemm_kernel<BN, EPI, GW>, dim3(p.grid), dim3(kThreads + 32 * GW), C::kSmemBytes, stream, p.tmA, p.tmB,
            p.args);
 }
@@ -613,14 +609,18 @@ void launch_bn(const GemmPlan& p, cudaStream_t s) {
 
 using namespace gemm_impl;
 
+// SM count of the current device (cached per device).
 int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  static int n[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
   }
-  return n;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev];
 }
 
 bool make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,

@@ -331,9 +331,17 @@ class NativeRunner:
             self._fd_server.close()
             self._fd_server = None
 
-    def _pull(self, dst_base: int, member: int, src_base: int, dst: List[int], src: List[int], chunk: int) -> None:
+    def _pull(self, dst_base: int, dst_extent: int, src_base: int, src_extent: int, dst: List[int], src: List[int],
+              chunk: int) -> None:
+        """Copy ``chunk``-byte pieces ``src[i] -> dst[i]`` between two mapped
+        ranges (either may be a peer GPU's memory).  Every piece is checked
+        against its range's extent first: the copy kernel itself does not
+        know the extents, and a bad plan would write past the KV pool or a
+        peer's mapping."""
         if not dst:
             return
+        _check_extent("destination", dst, chunk, dst_extent)
+        _check_extent("source", src, chunk, src_extent)
         d = torch.tensor(dst, dtype=torch.int64, device=self.device)
         s = torch.tensor(src, dtype=torch.int64, device=self.device)
         self.eng.copy_chunks(dst_base, src_base, d, s, chunk, 4 * self.num_sms)
@@ -354,8 +362,8 @@ class NativeRunner:
             for l in restored:
                 nb = self.eng.layer_segment_bytes(l)
                 offs = list(range(0, nb, chunk))
-                src = self.peer_maps[keepers[l]].layers[l]
-                self._pull(self.eng.layer_ptr(l), keepers[l], src, offs, offs, chunk)
+                peer = self.peer_maps[keepers[l]]
+                self._pull(self.eng.layer_ptr(l), nb, peer.layers[l], peer.layer_bytes[l], offs, offs, chunk)
                 moved += nb
             torch.cuda.synchronize(self.device)
         elif self.comm is not None and n > 1:
@@ -406,19 +414,24 @@ class NativeRunner:
         ptr = self.eng.kv_base_ptr()
         return _u8_view(ptr, n, self.device)
 
+    def pool_extent(self) -> int:
+        """Bytes of the KV pool that pages may address now (base + extend)."""
+        return self.layout.base_bytes + self.ext_pages * self.layout.extend_page_bytes(self.fusion_size)
+
     def local_copy(self, src: List[int], dst: List[int], chunk: int) -> None:
-        d = torch.tensor(dst, dtype=torch.int64, device=self.device)
-        s = torch.tensor(src, dtype=torch.int64, device=self.device)
+        ext = self.pool_extent()
         base = self.eng.kv_base_ptr()
-        self.eng.copy_chunks(base, base, d, s, chunk, 4 * self.num_sms)
+        self._pull(base, ext, base, ext, dst, src, chunk)
         torch.cuda.synchronize(self.device)
 
     def kv_exchange(self, plan_send, plan_recv, chunk, my_rank, n, peer_src=None) -> int:
         if self.peer_maps and peer_src is not None:
             total = 0
             base = self.eng.kv_base_ptr()
+            ext = self.pool_extent()
             for j, dst in plan_recv.items():
-                self._pull(base, j, self.peer_maps[j].kv, dst, peer_src[j], chunk)
+                peer = self.peer_maps[j]
+                self._pull(base, ext, peer.kv, peer.kv_bytes, dst, peer_src[j], chunk)
                 total += len(dst) * chunk
             torch.cuda.synchronize(self.device)
             return total
@@ -433,15 +446,15 @@ class NativeRunner:
         total = 0
         for j, offs in plan_recv.items():
             if offs:
-                dst = torch.tensor(offs, dtype=torch.int64, device=self.device)
-                self._scatter(got[self._kvex(j)], dst, chunk)
+                self._scatter(got[self._kvex(j)], offs, chunk)
                 total += len(offs) * chunk
         torch.cuda.synchronize(self.device)
         return total
 
-    def _scatter(self, buf: torch.Tensor, dst_offs: torch.Tensor, chunk: int) -> None:
-        src = torch.arange(dst_offs.numel(), dtype=torch.int64, device=self.device) * chunk
-        self.eng.copy_chunks(self.eng.kv_base_ptr(), buf.data_ptr(), dst_offs, src, chunk, 4 * self.num_sms)
+    def _scatter(self, buf: torch.Tensor, dst_offs: List[int], chunk: int) -> None:
+        src = [i * chunk for i in range(len(dst_offs))]
+        self._pull(self.eng.kv_base_ptr(), self.pool_extent(), buf.data_ptr(), buf.numel() * buf.element_size(),
+                   list(dst_offs), src, chunk)
 
     def kv_restore(self, my_rank, n, home, fusion_pages, dp_pages, chunk) -> int:
         from ..kv import copy_plan
@@ -449,9 +462,14 @@ class NativeRunner:
             if my_rank != home:
                 return 0          # the home instance pulls
             base = self.eng.kv_base_ptr()
+            ext = self.pool_extent()
             for j in range(n):
                 src, dst = copy_plan.restore_plan(self.layout, n, j, fusion_pages[j], dp_pages)
-                self._pull(base, j, base if j == home else self.peer_maps[j].kv, dst, src, chunk)
+                if j == home:
+                    self._pull(base, ext, base, ext, dst, src, chunk)
+                else:
+                    peer = self.peer_maps[j]
+                    self._pull(base, ext, peer.kv, peer.kv_bytes, dst, src, chunk)
             torch.cuda.synchronize(self.device)
             return len(dp_pages) * chunk * n
         pool = self.pool_bytes()
@@ -465,13 +483,11 @@ class NativeRunner:
         got = self.comm.exchange("kvex", {}, recvs, self.device)
         for j in range(n):
             src, dst = copy_plan.restore_plan(self.layout, n, j, fusion_pages[j], dp_pages)
-            d = torch.tensor(dst, dtype=torch.int64, device=self.device)
             if j == home:
-                s = torch.tensor(src, dtype=torch.int64, device=self.device)
-                base = self.eng.kv_base_ptr()
-                self.eng.copy_chunks(base, base, d, s, chunk, 4 * self.num_sms)
+                base, ext = self.eng.kv_base_ptr(), self.pool_extent()
+                self._pull(base, ext, base, ext, dst, src, chunk)
             else:
-                self._scatter(got[self._kvex(j)], d, chunk)
+                self._scatter(got[self._kvex(j)], dst, chunk)
         torch.cuda.synchronize(self.device)
         return len(dp_pages) * chunk * n
 
@@ -493,6 +509,12 @@ class NativeRunner:
         off = self.layout.kv_offset(page_id, local_layer, fusion_size)
         n = self.layout.layer_stride // 2
         return self.pool_bytes()[off:off + n].view(torch.bfloat16).clone().cpu()
+
+
+def _check_extent(what: str, offs: List[int], chunk: int, extent: int) -> None:
+    lo, hi = min(offs), max(offs)
+    if lo < 0 or hi + chunk > extent:
+        raise ValueError(f"copy plan {what} [{lo}, {hi + chunk}) outside its {extent}-byte range")
 
 
 def _u8_view(ptr: int, nbytes: int, device) -> torch.Tensor:

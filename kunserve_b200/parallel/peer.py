@@ -77,3 +77,6 @@ class PeerMemory:
                 os.close(fd)
         self.kv = self.maps[0].ptr()
         self.layers = [m.ptr() for m in self.maps[1:]]
+        # mapped extents: copies that read the peer are checked against them
+        self.kv_bytes = int(sizes[0])
+        self.layer_bytes = [int(x) for x in sizes[1:]]

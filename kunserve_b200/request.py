@@ -7,8 +7,10 @@ Parity: ``kunserve/request.py`` — ``SamplingParams`` (:17-165),
 
 Differences by design:
 
-* Sampling parameters reach the device: temperature, top-k and top-p are
-  applied by the sampling kernel (the reference always decodes greedily).
+* Sampling parameters reach the engine (the reference always decodes
+  greedily): greedy and temperature sampling run in the sampling kernel;
+  a batch with top-k or top-p is sampled on the host path in torch from the
+  engine's fp32 logits.
 * ``start_position()`` is the RoPE position of the first input token of the
   next step (prefill chunk start, or ``len(prompt) + len(generated) - 1`` for
   a decode step).  The reference passes ``input_len + output_len`` for decode

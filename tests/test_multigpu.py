@@ -157,8 +157,9 @@ def test_balloon_cycle_two_gpus(p2p):
 
 def test_fused_reduce_scatter_and_allgather_gemm_two_gpus():
     """GEMM + reduce-scatter (row blocks pushed to their owners) and
-    all-gather + GEMM (A shards read by TMA from the owning GPU) against
-    PyTorch on 2 ranks (the sweep's --check mode asserts the numbers)."""
+    all-gather + GEMM (gather warps copy the peers' A shards with plain loads
+    into a local buffer; TMA reads only this GPU's memory) against PyTorch on
+    2 ranks (the sweep's --check mode asserts the numbers)."""
     _need2()
     import os
     import subprocess

@@ -28,6 +28,10 @@ def lib():
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                    ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    flag = so.kus_noalloc_error_flag
+    flag.restype = ctypes.c_longlong
+    flag.argtypes = [ctypes.c_int]
+    fn.error_flag = flag
     return C, fn
 
 
@@ -62,6 +66,9 @@ def test_noalloc_gemm_matches_regular_entry_point(lib, shapes):
     free2, _ = torch.cuda.mem_get_info()
     assert torch.cuda.memory_allocated() == alloc0
     assert free2 == free1, "the second call changed free device memory"
+    # the library's device error flag, read through the C API: zero means
+    # both calls' outputs are complete
+    assert fn.error_flag(0) == 0
     for A, B, ref, out in cases:
         assert _rel(out, ref) < 1e-2
         assert _rel(out, A.float() @ B.float().t()) < 1e-2
