@@ -71,11 +71,7 @@ def build_instances(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: S
     port = free_port()
     handles = {}
     for rank in range(world):
-        _, g, i, st, t = topo.coords(rank)
-        pc = ParallelConfig(tensor_parallel_size=ec.tp, tensor_parallel_rank=t, pipeline_parallel_size=ec.pp,
-                            pipeline_parallel_rank=st, group_parallel_size=ec.group_size * ec.pp,
-                            group_parallel_rank=i * ec.pp + st, replica_size=ec.group_size, replica_rank=i,
-                            global_rank=rank, global_size=world)
+        pc = rank_parallel_config(topo, rank)
         if actor_kind == "local":
             handles[rank] = LocalActor(Worker(rank, mc, cc, pc, backend=backend, device=devices[rank], seed=seed))
         elif actor_kind == "process":
@@ -89,6 +85,24 @@ def build_instances(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: S
     if actor_kind == "process":
         for h in handles.values():
             h.wait_ready()
+    return instances_from_handles(cfg, mc, cc, sc, topo, handles, server_id, tokenizer, output_callback)
+
+
+def rank_parallel_config(topo: Topology, rank: int) -> ParallelConfig:
+    """The parallel coordinates of one global rank."""
+    _, g, i, st, t = topo.coords(rank)
+    return ParallelConfig(tensor_parallel_size=topo.tp, tensor_parallel_rank=t, pipeline_parallel_size=topo.pp,
+                          pipeline_parallel_rank=st, group_parallel_size=topo.group_size * topo.pp,
+                          group_parallel_rank=i * topo.pp + st, replica_size=topo.group_size, replica_rank=i,
+                          global_rank=rank, global_size=topo.world_size)
+
+
+def instances_from_handles(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: SchedConfig, topo: Topology,
+                           handles, server_id: int = 0, tokenizer=None,
+                           output_callback=None) -> List[List[InstanceEngine]]:
+    """Instance engines (grouped by balloon group) over worker handles
+    indexed by global rank."""
+    ec = cfg.engine_config
     groups = []
     for g in range(ec.ngroups):
         insts = []
@@ -101,6 +115,65 @@ def build_instances(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: S
             insts.append(inst)
         groups.append(insts)
     return groups
+
+
+class LaunchedRank:
+    """One rank of a job that an external launcher started: its worker and the
+    socket it serves the worker on."""
+
+    def __init__(self, worker, listener, ports, authkey):
+        self.worker, self.listener, self.ports, self.authkey = worker, listener, ports, authkey
+
+    def serve(self) -> None:
+        """Serve this rank's worker to the front end until it lets go."""
+        from .runtime.actors import serve_connection
+        serve_connection(self.worker, self.listener)
+
+
+def join_launched_job(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, rank: int, device: str,
+                      seed: int = 0, backend: str = "native") -> LaunchedRank:
+    """A rank of a serving job whose processes an external launcher started
+    (``torchrun``: one rank per GPU, the default ``torch.distributed`` group
+    already joined).  Builds the five communicators and this rank's
+    ``Worker``, opens a local socket for it and shares every rank's port; the
+    front end (a separate process, so that scheduling never competes with a
+    worker's step for the interpreter) then reaches all workers with
+    ``connect_launched_job``.  Call ``serve()`` afterwards."""
+    import secrets
+    from multiprocessing.connection import Listener
+
+    import torch.distributed as dist
+
+    from .parallel.comm import Communicator
+
+    ec = cfg.engine_config
+    topo = Topology(1, ec.ngroups, ec.group_size, ec.pp, ec.tp)
+    world = dist.get_world_size()
+    if topo.world_size != world:
+        raise ValueError(f"the job has {world} ranks but the topology needs {topo.world_size}")
+    comm = Communicator(topo, rank, "nccl" if device.startswith("cuda") else "gloo")
+    worker = Worker(rank, mc, cc, rank_parallel_config(topo, rank), backend=backend, device=device, comm=comm,
+                    seed=seed)
+    key = [secrets.token_bytes(16) if rank == 0 else None]
+    dist.broadcast_object_list(key, src=0)
+    listener = Listener(("127.0.0.1", 0), authkey=key[0])
+    ports = [None] * world
+    dist.all_gather_object(ports, listener.address[1])
+    return LaunchedRank(worker, listener, ports, key[0])
+
+
+def connect_launched_job(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: SchedConfig, ports, authkey,
+                         server_id: int = 0, tokenizer=None, output_callback=None):
+    """Front end of a launched job: ``ConnActor`` handles on every rank's
+    worker and the instance engines over them.  Returns ``(instance groups,
+    handles by rank)``."""
+    from .runtime.actors import ConnActor
+
+    ec = cfg.engine_config
+    topo = Topology(1, ec.ngroups, ec.group_size, ec.pp, ec.tp)
+    handles = {r: ConnActor(("127.0.0.1", p), authkey) for r, p in enumerate(ports)}
+    groups = instances_from_handles(cfg, mc, cc, sc, topo, handles, server_id, tokenizer, output_callback)
+    return groups, handles
 
 
 async def setup_kunserve(cfg: KunServeConfig, model_config: Optional[ModelConfig] = None, **kw):

@@ -21,8 +21,11 @@ FSM_INTERVAL_S = 0.1
 
 
 class Coordinator:
-    def __init__(self, groups: List[GroupEngine], strategy: str = "round-robin", enable_balloon: bool = False):
+    def __init__(self, groups: List[GroupEngine], strategy: str = "round-robin", enable_balloon: bool = False,
+                 load_interval: float = LOAD_INTERVAL_S, fsm_interval: float = FSM_INTERVAL_S):
         self.groups = groups
+        self.load_interval = load_interval
+        self.fsm_interval = fsm_interval
         self.strategy = strategy
         self.enable_balloon = enable_balloon
         self._rr = 0
@@ -61,7 +64,7 @@ class Coordinator:
     async def collect_loop(self) -> None:
         while True:
             self.collect_instance_loads()
-            await asyncio.sleep(LOAD_INTERVAL_S)
+            await asyncio.sleep(self.load_interval)
 
     async def monitor_engine_events(self) -> None:
         while True:
@@ -71,7 +74,7 @@ class Coordinator:
                 _, event = await g.get_event()
                 if event is not None:
                     await g.handle_event(event)
-            await asyncio.sleep(FSM_INTERVAL_S)
+            await asyncio.sleep(self.fsm_interval)
 
     def start(self) -> None:
         self._tasks.append(asyncio.create_task(self.collect_loop()))

@@ -384,6 +384,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("tp_fused", &Engine::tp_fused)
       .def("set_tp_fused", &Engine::set_tp_fused)
       .def("set_tp_fused_max_tokens", &Engine::set_tp_fused_max_tokens)
+      .def("set_library_mode", &Engine::set_library_mode,
+           "GEMMs through ATen/cuBLAS with unfused epilogues and NCCL all-reduce (the comparison baseline)")
+      .def("library_mode", &Engine::library_mode)
       .def("launches", &Engine::launches)
       .def("reset_launches", &Engine::reset_launches);
   py::class_<SharedBuffer>(m, "SharedBuffer")

@@ -247,14 +247,50 @@ torch::Tensor Engine::logits() { return logits_; }
 
 bool make_wmap(WMap* m, const void* w, int rows, int cols, bool with128) {
   m->has128 = with128;
+  m->ptr = w;
+  m->rows = rows;
+  m->cols = cols;
   if (!make_tmap_bf16(&m->b256, w, rows, cols, cols, 256)) return false;
   return !with128 || make_tmap_bf16(&m->b128, w, rows, cols, cols, 128);
 }
 
 static const CUtensorMap& pick(const WMap& m, const GemmPlan& p) { return p.bn == 128 ? m.b128 : m.b256; }
 
-void Engine::gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, int epi, void* out, int ldc,
-                  const __nv_bfloat16* res, cudaStream_t st) {
+void Engine::lib_gemm(const __nv_bfloat16* A, const WMap& mB, int M, int N, int K, int epi, void* out, int ldc,
+                      const __nv_bfloat16* res) {
+  auto bf = torch::TensorOptions().dtype(torch::kBFloat16).device(torch::kCUDA, device_);
+  auto a = torch::from_blob(const_cast<__nv_bfloat16*>(A), {M, K}, {K, 1}, bf);
+  auto w = torch::from_blob(const_cast<void*>(mB.ptr), {N, K}, {mB.cols, 1}, bf);
+  KUS_CHECK(mB.rows == N && mB.cols == K, "library GEMM shape");
+  if (epi == EPI_BF16) {
+    auto c = torch::from_blob(out, {M, N}, {ldc, 1}, bf);
+    at::mm_out(c, a, w.t());
+  } else if (epi == EPI_ADD) {
+    KUS_CHECK(res == out, "library GEMM adds the residual in place");
+    auto c = torch::from_blob(out, {M, N}, {ldc, 1}, bf);
+    c.addmm_(a, w.t());
+  } else if (epi == EPI_F32) {
+    auto c = torch::from_blob(out, {M, N}, {ldc, 1}, bf.dtype(torch::kFloat32));
+    c.copy_(at::mm(a, w.t()));
+  } else if (epi == EPI_SILU) {
+    if (!lib_gu_.defined()) lib_gu_ = torch::empty({s_.max_tokens, 2 * (int64_t)f_pad_}, bf);
+    auto g = lib_gu_.narrow(0, 0, M);
+    at::mm_out(g, a, w.t());
+    silu_mul_interleaved(reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out),
+                         M, N / 2, at::cuda::getCurrentCUDAStream(device_));
+    ++launches_;
+  } else {
+    KUS_CHECK(false, "library GEMM epilogue");
+  }
+}
+
+void Engine::gemm(const CUtensorMap* mA, const __nv_bfloat16* A, const WMap& mB, int M, int N, int K, int epi,
+                  void* out, int ldc, const __nv_bfloat16* res, cudaStream_t st) {
+  if (lib_) {
+    lib_gemm(A, mB, M, N, K, epi, out, ldc, res);
+    if (sync_debug_) debug_check("library gemm", M, N, K, st);
+    return;
+  }
   const int bn = mB.has128 ? 0 : 256;
   GemmPlan p = plan_gemm(M, N, K, epi, bn, true);
   if (plan_workspace_floats(p) > (size_t)gemm_ws_.numel() || plan_counters(p) >= counters_.numel())
@@ -275,7 +311,7 @@ void Engine::gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, in
 }
 
 int Engine::gemm_partials(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, cudaStream_t st) {
-  if (!parts_ || s_.tp > 1 || M > 128) return 0;
+  if (!parts_ || lib_ || s_.tp > 1 || M > 128) return 0;
   GemmPlan p = plan_gemm(M, N, K, EPI_F32, mB.has128 ? 0 : 256, false);
   if (!p.swap) return 0;
   const long long stride = (long long)M * N;
@@ -410,7 +446,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   if (first_stage) {
     embed(tokens, reinterpret_cast<const __nv_bfloat16*>(embed_.data_ptr()), h, (int)T, H, s_.vocab, st);
     ++launches_;
-    set_pdl(pdl_);
+    set_pdl(pdl_ && !lib_);
     armed = true;
   }
   bool pending = false;   // tmp holds an all-reduced partial still to be added to h
@@ -418,7 +454,8 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   float* part = part_ws_.data_ptr<float>();
   bool y_ready = false;   // the fused all-reduce already produced this layer's normed input
   // the push epilogue wins at decode sizes; NCCL's ring wins for large steps
-  const bool fused = tp && fused_ && T <= fused_max_tokens_;
+  const bool fused = tp && fused_ && !lib_ && T <= fused_max_tokens_;
+  if (lib_) armed = true;   // the library baseline launches without PDL
   for (int64_t l = layer_start; l < layer_end; ++l) {
     for (int d : dropped) KUS_CHECK(d != l, "step touches a dropped layer");
     const LayerW& W = layers_[l];
@@ -431,13 +468,13 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
               pend_parts ? part : nullptr, pend_parts, (long long)T * H);
     pend_parts = 0;
     if (!armed) {
-      set_pdl(pdl_);
+      set_pdl(pdl_ && !lib_);
       armed = true;
     }
     y_ready = false;
     // decode-sized steps: split-K partial slots, summed by RoPE + KV append
     int np = gemm_partials(m_y_, W.m_qkv, (int)T, qkv_n_, H, st);
-    if (np == 0) gemm(m_y_, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
+    if (np == 0) gemm(m_y_, y, W.m_qkv, (int)T, qkv_n_, H, EPI_BF16, qkv, qkv_n_, nullptr, st);
     rope_append(qkv, positions, kv_page, kv_slot, cos_sin_.data_ptr<float>(), geo, ll, (int)T, s_.nq, s_.nkv,
                 s_.max_pos, st, np ? part : nullptr, np, (long long)T * qkv_n_);
     paged_attention(m_attn_q_, m_attn_kv_, m_dec_kv_[dec_map], qkv, qkv_n_, attn, geo, ll, ab, sc, (int)T, s_.nq, scale, st);
@@ -447,18 +484,18 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
       tp_push_gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, st);
       tp_reduce(h, W.post_norm, y, (int)T, st);
     } else if (tp) {
-      gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_BF16, tmp, H, nullptr, st);
+      gemm(m_attn_, attn, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_BF16, tmp, H, nullptr, st);
       all_reduce(tmp, T * H, st);
       rmsnorm(h, tmp, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
     } else if ((np = gemm_partials(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, st)) > 0) {
       // residual add of the partial slots fused into the post-attention norm
       rmsnorm(h, nullptr, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st, part, np, (long long)T * H);
     } else {
-      gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_ADD, h, H, h, st);
+      gemm(m_attn_, attn, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_ADD, h, H, h, st);
       rmsnorm(h, nullptr, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
     }
     ++launches_;
-    gemm(m_y_, W.m_gu, (int)T, 2 * f_pad_, H, EPI_SILU, act, f_pad_, nullptr, st);
+    gemm(m_y_, y, W.m_gu, (int)T, 2 * f_pad_, H, EPI_SILU, act, f_pad_, nullptr, st);
     if (fused) {
       tp_push_gemm(m_act_, W.m_down, (int)T, H, f_pad_, st);
       const bool next = l + 1 < layer_end;
@@ -466,7 +503,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
       y_ready = next;
       pending = false;
     } else if (tp) {
-      gemm(m_act_, W.m_down, (int)T, H, f_pad_, EPI_BF16, tmp, H, nullptr, st);
+      gemm(m_act_, act, W.m_down, (int)T, H, f_pad_, EPI_BF16, tmp, H, nullptr, st);
       all_reduce(tmp, T * H, st);
       pending = true;
     } else {
@@ -474,7 +511,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
       // the next pipeline stage finishes its last layer in place
       const bool hand_off = l + 1 == layer_end && !last_stage;
       pend_parts = hand_off ? 0 : gemm_partials(m_act_, W.m_down, (int)T, H, f_pad_, st);
-      if (pend_parts == 0) gemm(m_act_, W.m_down, (int)T, H, f_pad_, EPI_ADD, h, H, h, st);
+      if (pend_parts == 0) gemm(m_act_, act, W.m_down, (int)T, H, f_pad_, EPI_ADD, h, H, h, st);
       pending = false;
     }
   }
@@ -488,7 +525,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   rmsnorm(h, nullptr, reinterpret_cast<const __nv_bfloat16*>(final_norm_.data_ptr()), yl, last_idx, (int)B, H,
           (float)s_.eps, st, pend_parts ? part : nullptr, pend_parts, (long long)T * H);
   ++launches_;
-  gemm(m_ylast_, m_lm_head_, (int)B, s_.vocab, H, EPI_F32, logits_.data_ptr(), s_.vocab, nullptr, st);
+  gemm(m_ylast_, yl, m_lm_head_, (int)B, s_.vocab, H, EPI_F32, logits_.data_ptr(), s_.vocab, nullptr, st);
   if (sample_mode == 1) {   // caller samples from logits(); still surface device errors
     read_error_async(err_host_.data_ptr<int>(), st);
     check_cuda(cudaStreamSynchronize(st), "step sync");

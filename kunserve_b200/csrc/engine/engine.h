@@ -38,6 +38,8 @@ struct EngineShape {
 struct WMap {
   CUtensorMap b256, b128;
   bool has128 = false;
+  const void* ptr = nullptr;   // the weight itself (library baseline GEMMs)
+  int rows = 0, cols = 0;
 };
 
 // Maps for a [rows, cols] row-major bf16 weight (128-row ones if asked).
@@ -107,10 +109,21 @@ class Engine {
   int64_t launches() const { return launches_; }
   void reset_launches() { launches_ = 0; }
 
+  // Library baseline: every GEMM through ATen (cuBLAS) with unfused
+  // epilogues, NCCL for the TP all-reduce, no programmatic dependent launch.
+  // The comparison arm for the hand-written kernels and fused collectives
+  // (attention, norms, RoPE and sampling stay this library's kernels).
+  void set_library_mode(bool on) { lib_ = on; }
+  bool library_mode() const { return lib_; }
+
  private:
   void build_layer_maps(int l);
-  void gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, int epi, void* out, int ldc,
-            const __nv_bfloat16* res, cudaStream_t s);
+  void gemm(const CUtensorMap* mA, const __nv_bfloat16* A, const WMap& mB, int M, int N, int K, int epi, void* out,
+            int ldc, const __nv_bfloat16* res, cudaStream_t s);
+  void lib_gemm(const __nv_bfloat16* A, const WMap& mB, int M, int N, int K, int epi, void* out, int ldc,
+                const __nv_bfloat16* res);
+  bool lib_ = false;
+  torch::Tensor lib_gu_;   // [max_tokens, 2F] gate/up GEMM output of the library baseline
   void all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t s);
 
   EngineShape s_;

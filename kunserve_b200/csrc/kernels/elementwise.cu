@@ -440,6 +440,34 @@ __global__ void add_inplace_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfl
   }
 }
 
+// act[t, j] = silu(gu[t, g(j)]) * gu[t, g(j) + 128] with g(j) = (j / 128) * 256 + j % 128:
+// the library baseline's unfused SiLU * up over the engine's gate/up layout
+// (weights interleaved per 128 rows, so a plain GEMM's columns interleave
+// the same way).  Eight features per thread.
+__global__ void silu_mul_interleaved_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ act,
+                                            int T, int F) {
+  const int f8 = F / 8;
+  const long long n = (long long)T * f8;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(i / f8), j = (int)(i % f8) * 8;
+    const long long g = (long long)t * 2 * F + (j / 128) * 256 + j % 128;
+    float a[8], b[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(gu + g), a);
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(gu + g + 128), b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = a[k] / (1.0f + __expf(-a[k])) * b[k];
+    *reinterpret_cast<uint4*>(act + (long long)t * F + j) = pack_bf16x8(a);
+  }
+}
+
+void silu_mul_interleaved(const __nv_bfloat16* gu, __nv_bfloat16* act, int T, int F, cudaStream_t s) {
+  const long long n = (long long)T * (F / 8);
+  if (n <= 0) return;
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 8 * 148) blocks = 8 * 148;
+  silu_mul_interleaved_kernel<<<blocks, 256, 0, s>>>(gu, act, T, F);
+}
+
 void add_inplace(__nv_bfloat16* x, const __nv_bfloat16* y, long long n, cudaStream_t s) {
   if (n <= 0) return;
   long long n8 = n / 8;

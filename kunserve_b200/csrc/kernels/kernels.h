@@ -80,6 +80,9 @@ void sample(const float* logits, int B, int V, int ld, const float* temp, const 
 void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off, const long long* src_off, int n,
                  long long chunk, int max_blocks, cudaStream_t s);
 void add_inplace(__nv_bfloat16* x, const __nv_bfloat16* y, long long n, cudaStream_t s);
+// act[T, F] = silu(gate) * up from a [T, 2F] GEMM output whose columns
+// interleave 128 gate and 128 up features (F a multiple of 128).
+void silu_mul_interleaved(const __nv_bfloat16* gu, __nv_bfloat16* act, int T, int F, cudaStream_t s);
 // Reduce side of the fused tensor-parallel all-reduce (see elementwise.cu).
 // Rows [row0, row0 + T) (row0 > 0: the reduce-scatter owner's block).
 void tp_reduce_rmsnorm(const __nv_bfloat16* rb, int R, long long slot_elems, __nv_bfloat16* h,

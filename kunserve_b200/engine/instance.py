@@ -102,13 +102,18 @@ class InstanceEngine(AdmissionMixin):
         self._last_requests = 0
         self.ttfts: List[float] = []
         self.tbts: List[float] = []
-        window = 30
-        self.sliding_window: Deque[float] = deque([0.0] * window, maxlen=window)
-        self.rate_window: Deque[float] = deque([0.0] * window, maxlen=window)
+        self.set_vote_window(30)
         self.step_log: List[Tuple[float, int, int]] = []   # (seconds, tokens, requests)
         self.event_log: List[Tuple[float, str, float]] = []  # (time, event, seconds)
+        self.restore_log: List[Tuple[float, float]] = []     # (bytes pulled by all workers, seconds)
         self._loop_task: Optional[asyncio.Task] = None
         # per VE scheduler: was its next batch prepared after its last step?
+
+    def set_vote_window(self, n: int) -> None:
+        """Samples of KV demand (one per load collection) behind the balloon
+        and restore votes; the reference keeps 30."""
+        self.sliding_window: Deque[float] = deque([0.0] * n, maxlen=n)
+        self.rate_window: Deque[float] = deque([0.0] * n, maxlen=n)
 
     # ------------------------------------------------------------ set-up
     def _new_scheduler(self) -> ColocatedScheduler:
@@ -202,6 +207,7 @@ class InstanceEngine(AdmissionMixin):
         self.stopped = False
         self.ttfts, self.tbts, self.step_log = [], [], []
         self.finished_tokens = self.finished_requests = 0
+        self.set_vote_window(len(self.sliding_window))
 
     async def stop_and_wait(self) -> None:
         self.stopped = True
@@ -791,6 +797,7 @@ class InstanceEngine(AdmissionMixin):
         moved = await asyncio.gather(*[aw(f) for f in futs])
         dt = time.perf_counter() - t0
         self.event_log.append((time.time(), "pmm_restore", dt))
+        self.restore_log.append((float(sum(moved)), dt))
         logger.info(f"parameters restored ({sum(moved) / 2**30:.2f} GiB pulled) in {dt:.3f}s")
 
     def restore_instance(self) -> None:

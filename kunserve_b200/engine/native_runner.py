@@ -211,9 +211,22 @@ class NativeRunner:
         self.gpu_ms = 0.0      # device time inside forward(), summed over steps
         self._ev = None
         self.peer_maps = {}
+        # KV and weight movement pulls over NVLink when peers are mapped;
+        # the library baseline moves them with NCCL instead
+        self.use_p2p = True
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.num_steps = 0
+
+    def set_library_mode(self, on: bool) -> None:
+        """Switch between this library's kernels (fused TP collectives, P2P
+        copies) and the comparison baseline: ATen/cuBLAS GEMMs, NCCL
+        all-reduce, NCCL send/recv for KV reshard and parameter restore."""
+        self.eng.set_library_mode(bool(on))
+        self.use_p2p = not on
+
+    def _p2p(self) -> bool:
+        return bool(self.peer_maps) and self.use_p2p
 
     def _init_tp_comm(self, dev: int) -> None:
         """NCCL communicator of the engine's in-layer all-reduce: TP rank 0
@@ -357,7 +370,7 @@ class NativeRunner:
         """Remap the dropped layers and pull their bytes from the keepers."""
         restored = self.eng.restore_layers()
         moved = 0.0
-        if n > 1 and self.peer_maps:
+        if n > 1 and self._p2p():
             chunk = 1 << 20
             for l in restored:
                 nb = self.eng.layer_segment_bytes(l)
@@ -425,7 +438,7 @@ class NativeRunner:
         torch.cuda.synchronize(self.device)
 
     def kv_exchange(self, plan_send, plan_recv, chunk, my_rank, n, peer_src=None) -> int:
-        if self.peer_maps and peer_src is not None:
+        if self._p2p() and peer_src is not None:
             total = 0
             base = self.eng.kv_base_ptr()
             ext = self.pool_extent()
@@ -458,7 +471,7 @@ class NativeRunner:
 
     def kv_restore(self, my_rank, n, home, fusion_pages, dp_pages, chunk) -> int:
         from ..kv import copy_plan
-        if self.peer_maps:
+        if self._p2p():
             if my_rank != home:
                 return 0          # the home instance pulls
             base = self.eng.kv_base_ptr()

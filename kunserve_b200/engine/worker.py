@@ -58,6 +58,7 @@ class Worker:
         self.fusion_size = 1
         self.dropped: List[int] = []
         self.step_times: List[float] = []
+        self.steps_done = 0
 
     def ready(self) -> bool:
         return True
@@ -128,6 +129,7 @@ class Worker:
                 self.comm.send(h, *send_to)
             out = self.runner.sample(h, step).tolist() if last_stage else None
         self.step_times.append(time.perf_counter() - t0)
+        self.steps_done += 1
         return out
 
     def export_memory(self) -> dict:
@@ -351,6 +353,43 @@ class Worker:
             return 0
         from ..ops import native
         return int(native().error_flag(True))
+
+    # ------------------------------------------------------ bench helpers
+    def set_library_mode(self, on: bool) -> bool:
+        """Native runner only: run the library baseline (cuBLAS GEMMs, NCCL
+        collectives and copies) instead of this library's kernels."""
+        if self.backend != "native":
+            return False
+        self.runner.set_library_mode(on)
+        return True
+
+    def mark(self, tag: str) -> None:
+        """Record a CUDA event named ``tag`` on this worker's stream (after
+        every step issued so far)."""
+        if not hasattr(self, "_marks"):
+            self._marks = {}
+        if self.device.type != "cuda":
+            self._marks[tag] = time.perf_counter()
+            return
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(self.device))
+        self._marks[tag] = ev
+
+    def mark_elapsed_ms(self, a: str, b: str) -> float:
+        """Device time between two marks (waits for the second)."""
+        ea, eb = self._marks[a], self._marks[b]
+        if isinstance(ea, float):
+            return (eb - ea) * 1000.0
+        eb.synchronize()
+        return float(ea.elapsed_time(eb))
+
+    def counters(self) -> Dict[str, float]:
+        """Launch, step, byte and device-time counters of the native runner."""
+        if self.backend != "native":
+            return {"launches": 0, "steps": self.steps_done, "gpu_ms": 0.0, "h2d": 0, "d2h": 0}
+        r = self.runner
+        return {"launches": int(r.eng.launches()), "steps": int(r.num_steps), "gpu_ms": float(r.gpu_ms),
+                "h2d": int(r.h2d_bytes), "d2h": int(r.d2h_bytes)}
 
     def last_logits(self, n: int) -> torch.Tensor:
         """fp32 logits of the last step's ``n`` rows (left by sample mode 1)."""

@@ -92,14 +92,30 @@ def lognormal_lengths(n: int, mean: float, sigma: float, lo: int, hi: int, rng) 
     return np.clip(np.round(rng.lognormal(mu, sigma, n)), lo, hi).astype(np.int64)
 
 
+def uniform_lengths(n: int, lo: int, hi: int, rng) -> np.ndarray:
+    """Integers uniform in [lo, hi] (both ends included)."""
+    return rng.integers(lo, hi + 1, n).astype(np.int64)
+
+
 def build_trace(duration: float, rate: float, dist: str = "poisson", cv: float = 1.0, seed: int = 42,
                 bursts: Sequence[Burst] = (), prompt_mean: float = 700, prompt_sigma: float = 1.0,
                 prompt_range=(16, 8192), output_mean: float = 250, output_sigma: float = 1.0,
-                output_range=(1, 2048), vocab: int = 32000, with_tokens: bool = True) -> List[TraceRequest]:
+                output_range=(1, 2048), vocab: int = 32000, with_tokens: bool = True,
+                lengths: str = "lognormal", backlog: int = 0) -> List[TraceRequest]:
+    """Seeded requests.  ``lengths="uniform"`` draws prompt and output lengths
+    uniformly from their ranges (the tiny-model configuration); otherwise
+    lognormal with the given means.  ``backlog`` requests arrive at time 0
+    before the arrival process starts (a burst already queued)."""
     ts = arrivals(duration, rate, dist, cv, seed, bursts)
+    if backlog:
+        ts = np.concatenate([np.zeros(backlog), ts])
     rng = np.random.default_rng(seed + 1)
-    pl = lognormal_lengths(ts.size, prompt_mean, prompt_sigma, *prompt_range, rng)
-    ol = lognormal_lengths(ts.size, output_mean, output_sigma, *output_range, rng)
+    if lengths == "uniform":
+        pl = uniform_lengths(ts.size, *prompt_range, rng)
+        ol = uniform_lengths(ts.size, *output_range, rng)
+    else:
+        pl = lognormal_lengths(ts.size, prompt_mean, prompt_sigma, *prompt_range, rng)
+        ol = lognormal_lengths(ts.size, output_mean, output_sigma, *output_range, rng)
     out = []
     for t, p, o in zip(ts, pl, ol):
         toks = rng.integers(0, vocab, int(p)).tolist() if with_tokens else None

@@ -10,7 +10,10 @@ three built-in kinds is used:
   GPU worker driven by its own engine);
 * ``thread``  — calls run in order on one dedicated thread;
 * ``process`` — the object is built in a child process (``spawn``), calls and
-  results travel over a pipe; one process per GPU or per CPU rank.
+  results travel over a pipe; one process per GPU or per CPU rank;
+* ``conn``    — the object lives in a process that an external launcher
+  started (a ``torchrun`` rank): that process serves it on a local socket
+  (``serve_connection``) and the front end holds a ``ConnActor``.
 
 Every future can be awaited (``asyncio.wrap_future``) or waited with
 ``get(futures, timeout=...)``.  A child process that dies fails all of its
@@ -88,9 +91,11 @@ class LocalActor(ActorHandle):
 class ThreadActor(ActorHandle):
     kind = "thread"
 
-    def __init__(self, obj, name: str = "actor"):
+    def __init__(self, obj, name: str = "actor", init: Optional[Callable[[], None]] = None):
+        """``init`` runs once on the actor's thread before any call (for
+        example ``torch.cuda.set_device``: the current device is per thread)."""
         object.__setattr__(self, "_obj", obj)
-        object.__setattr__(self, "_pool", cf.ThreadPoolExecutor(1, thread_name_prefix=name))
+        object.__setattr__(self, "_pool", cf.ThreadPoolExecutor(1, thread_name_prefix=name, initializer=init))
 
     def _submit(self, name, args, kwargs):
         return self._pool.submit(getattr(self._obj, name), *args, **kwargs)
@@ -111,6 +116,13 @@ def _process_main(conn, factory, fargs, fkwargs, env):
     except BaseException as e:  # noqa: BLE001
         conn.send(("__ready__", False, (repr(e), traceback.format_exc())))
         return
+    _serve_loop(obj, conn)
+
+
+def _serve_loop(obj, conn) -> None:
+    """Run ``(call_id, name, args, kwargs)`` messages against ``obj`` in
+    order and answer ``(call_id, ok, result or (repr, traceback))`` until the
+    peer sends ``None`` or goes away."""
     while True:
         try:
             msg = conn.recv()
@@ -126,32 +138,27 @@ def _process_main(conn, factory, fargs, fkwargs, env):
             conn.send((call_id, False, (repr(e), traceback.format_exc())))
 
 
-class ProcessActor(ActorHandle):
-    kind = "process"
+class _ConnectionActor(ActorHandle):
+    """Calls over a ``multiprocessing`` connection: a reader thread resolves
+    each call's future from the answers, and a closed connection fails every
+    pending call with ``ActorDiedError``."""
 
-    def __init__(self, factory: Callable, *args, env: Optional[Dict[str, str]] = None,
-                 ready_timeout: float = 600.0, wait_ready: bool = True, **kwargs):
-        ctx = mp.get_context("spawn")
-        parent, child = ctx.Pipe()
-        proc = ctx.Process(target=_process_main, args=(child, factory, args, kwargs, env), daemon=True)
-        proc.start()
-        child.close()
+    def _start(self, conn, proc=None, ready: bool = False) -> None:
         d = self.__dict__
-        d["_conn"], d["_proc"] = parent, proc
+        d["_conn"], d["_proc"] = conn, proc
         d["_pending"]: Dict[int, cf.Future] = {}
         d["_lock"] = threading.Lock()
         d["_next"] = 0
         d["_ready"] = cf.Future()
+        if ready:
+            d["_ready"].set_result(True)
         d["_dead"] = False
         t = threading.Thread(target=self._reader, daemon=True)
         d["_reader_thread"] = t
         t.start()
-        if wait_ready:
-            self._ready.result(timeout=ready_timeout)
 
-    def wait_ready(self, timeout: float = 600.0) -> None:
-        """Block until the object was built in the child (raises its error)."""
-        self._ready.result(timeout=timeout)
+    def _died(self) -> "ActorDiedError":
+        return ActorDiedError("actor connection closed")
 
     def _reader(self):
         while True:
@@ -174,7 +181,7 @@ class ProcessActor(ActorHandle):
             else:
                 fut.set_exception(RemoteError(*payload))
         self.__dict__["_dead"] = True
-        err = ActorDiedError(f"actor process {self._proc.pid} exited (code {self._proc.exitcode})")
+        err = self._died()
         if not self._ready.done():
             self._ready.set_exception(err)
         with self._lock:
@@ -200,6 +207,28 @@ class ProcessActor(ActorHandle):
             fut.set_exception(ActorDiedError(str(e)))
         return fut
 
+
+class ProcessActor(_ConnectionActor):
+    kind = "process"
+
+    def __init__(self, factory: Callable, *args, env: Optional[Dict[str, str]] = None,
+                 ready_timeout: float = 600.0, wait_ready: bool = True, **kwargs):
+        ctx = mp.get_context("spawn")
+        parent, child = ctx.Pipe()
+        proc = ctx.Process(target=_process_main, args=(child, factory, args, kwargs, env), daemon=True)
+        proc.start()
+        child.close()
+        self._start(parent, proc)
+        if wait_ready:
+            self._ready.result(timeout=ready_timeout)
+
+    def wait_ready(self, timeout: float = 600.0) -> None:
+        """Block until the object was built in the child (raises its error)."""
+        self._ready.result(timeout=timeout)
+
+    def _died(self) -> ActorDiedError:
+        return ActorDiedError(f"actor process {self._proc.pid} exited (code {self._proc.exitcode})")
+
     @property
     def pid(self) -> int:
         return self._proc.pid
@@ -216,6 +245,70 @@ class ProcessActor(ActorHandle):
         if self._proc.is_alive():
             self._proc.terminate()
             self._proc.join(timeout)
+
+
+class ConnActor(_ConnectionActor):
+    """Handle on an object served by another process of the same job (for
+    example a ``torchrun`` rank hosting its GPU worker) over a local socket;
+    see ``serve_connection``."""
+    kind = "conn"
+
+    def __init__(self, address, authkey: bytes, timeout: float = 60.0):
+        import time as _time
+        from multiprocessing.connection import Client
+
+        deadline = _time.time() + timeout
+        while True:
+            try:
+                conn = Client(address, authkey=authkey)
+                break
+            except ConnectionRefusedError:
+                if _time.time() > deadline:
+                    raise
+                _time.sleep(0.05)
+        self.__dict__["_address"] = address
+        self._start(conn, ready=True)
+
+    def _died(self) -> ActorDiedError:
+        return ActorDiedError(f"served actor at {self._address} closed its connection")
+
+    def kill(self, timeout: float = 10.0) -> None:
+        """Ask the serving process to stop serving (it then returns from
+        ``serve_connection``)."""
+        try:
+            self._conn.send(None)
+        except (OSError, BrokenPipeError):
+            pass
+        self._reader_thread.join(timeout)
+
+
+def serve_connection(obj, listener, accept_timeout: float = 900.0) -> None:
+    """Serve ``obj`` to one ``ConnActor`` that connects to ``listener``
+    (a ``multiprocessing.connection.Listener``) until it sends the stop
+    message or disconnects.  Calls run in arrival order on this thread.
+    Raises ``TimeoutError`` when nobody connects within ``accept_timeout``
+    seconds (the front end died before it connected)."""
+    connected = threading.Event()
+
+    def give_up():
+        if not connected.is_set():
+            listener.close()
+
+    timer = threading.Timer(accept_timeout, give_up)
+    timer.daemon = True
+    timer.start()
+    try:
+        conn = listener.accept()
+    except OSError as e:
+        raise TimeoutError(f"no front end connected within {accept_timeout:.0f} s") from e
+    finally:
+        connected.set()
+        timer.cancel()
+    try:
+        _serve_loop(obj, conn)
+    finally:
+        conn.close()
+        listener.close()
 
 
 def ray_available() -> bool:

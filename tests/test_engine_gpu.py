@@ -68,6 +68,34 @@ def test_engine_matches_torch_logits():
     check_error()
 
 
+def test_library_baseline_matches_torch_logits():
+    """The comparison baseline (ATen/cuBLAS GEMMs, unfused SiLU * up and
+    residual adds) computes the same model: prefill and a decode step."""
+    mc, nat, ref = _setup()
+    nat.set_library_mode(True)
+    prompts = [[(5 * i + 11 * j) % 32000 for j in range(n)] for i, n in enumerate((24, 9, 300))]
+    tables = [[0, 1], [2], list(range(3, 3 + 19))]
+    step = StepInput([0, 1, 2], prompts, [0, 0, 0], tables, [1, 1, 1], 0, 2, top_k=[5] * 3, top_p=[1.0] * 3,
+                     temperature=[0.0] * 3, seeds=[0, 1, 2])
+    nat.step(step)
+    lg = nat.eng.logits()[:3].clone()
+    want = ref.logits(ref.forward_hidden(step), step)
+    assert ((lg - want).norm() / want.norm()).item() < 3e-2
+    _argmax_agrees(lg, want)
+    nxt = want.argmax(-1).tolist()
+    step2 = StepInput([0, 1, 2], [[t] for t in nxt], [24, 9, 300], tables, [0, 0, 0], 0, 2, top_k=[5] * 3,
+                      top_p=[1.0] * 3, temperature=[0.0] * 3, seeds=[0, 1, 2], step_id=1)
+    nat.step(step2)
+    lg2 = nat.eng.logits()[:3].clone()
+    want2 = ref.logits(ref.forward_hidden(step2), step2)
+    assert ((lg2 - want2).norm() / want2.norm()).item() < 3e-2
+    _argmax_agrees(lg2, want2)
+    # the library path launches none of this library's GEMM kernels
+    nat.set_library_mode(False)
+    from kunserve_b200.ops import check_error
+    check_error()
+
+
 def test_engine_greedy_in_kernel_equals_argmax():
     mc, nat, ref = _setup()
     step = StepInput([0], [[1, 2, 3, 4]], [0], [[0]], [1], 0, 2, temperature=[0.0], seeds=[0])
