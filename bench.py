@@ -336,6 +336,7 @@ class Job:
 
     async def measure(self, label, via_api):
         """Fill, warm, timed window, drain.  Returns this run's summary."""
+        from kunserve_b200.runtime import aw
         from kunserve_b200.evaluation.trace import build_trace
         from kunserve_b200.request import Request, SamplingParams
         from kunserve_b200.utils.misc import EngineState
@@ -411,7 +412,7 @@ class Job:
 
         # ---- timed window
         t0 = time.time()
-        s0 = await self.gpu0_steps()
+        await aw(self.workers[0].arm_mark.remote("w1", a.steps))
         self.llm.coordinator.enable_balloon = any(len(g.instances) > 1 for g in self.groups)
         self.llm.coordinator.start()
         self.resume()
@@ -423,14 +424,19 @@ class Job:
                     await asyncio.sleep(delay)
                 submit(i, trace[i], t0 + trace[i].arrival)
         feeder = asyncio.create_task(feed())
-        while await self.gpu0_steps() - s0 < a.steps:
+        c1_gpu0 = None
+        while c1_gpu0 is None:
             self._check()
             await asyncio.sleep(0.0002)
-        await self.call_all("mark", "w1")
+            c1_gpu0 = await aw(self.workers[0].armed_counters.remote())
+        # GPU 0 marked the window's end inside its K-th step; the others mark
+        # theirs behind whatever they have in flight now
+        await asyncio.gather(*[aw(w.mark.remote("w1")) for w in self.workers[1:]])
         t1 = time.time()
         clock_info = clocks.stop(t0, t1) if self.on_gpu else None
         win_ms = max(await asyncio.gather(*[self._elapsed(w) for w in self.workers]))
         c1 = await self.call_all("counters")
+        c1[0] = c1_gpu0
         # token times of the requests still in flight at the window's end
         for inst in self.live():
             for r in list(inst.unaccepted_queue) + [r for s in inst.scheduler for r in s.all_requests()]:

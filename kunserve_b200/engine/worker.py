@@ -130,6 +130,12 @@ class Worker:
             out = self.runner.sample(h, step).tolist() if last_stage else None
         self.step_times.append(time.perf_counter() - t0)
         self.steps_done += 1
+        arm = getattr(self, "_armed", None)
+        if arm is not None and self.steps_done == arm[1]:
+            # the armed step: mark the end of a timed window right behind it
+            self._armed = None
+            self.mark(arm[0])
+            self._armed_counters = self.counters()
         return out
 
     def export_memory(self) -> dict:
@@ -374,6 +380,16 @@ class Worker:
         ev = torch.cuda.Event(enable_timing=True)
         ev.record(torch.cuda.current_stream(self.device))
         self._marks[tag] = ev
+
+    def arm_mark(self, tag: str, after_steps: int) -> None:
+        """Record mark ``tag`` (and snapshot the counters) right after this
+        worker's ``after_steps``-th step from now, inside that step's call."""
+        self._armed = (tag, self.steps_done + after_steps)
+        self._armed_counters = None
+
+    def armed_counters(self):
+        """Counters at the armed mark, or None while it has not fired."""
+        return getattr(self, "_armed_counters", None)
 
     def mark_elapsed_ms(self, a: str, b: str) -> float:
         """Device time between two marks (waits for the second)."""
