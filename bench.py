@@ -407,6 +407,7 @@ class Job:
         kv_used0 = min(inst.get_used_gpu_blocks() / max(inst.get_capacity_units(), 1) for inst in self.live())
         preempt0 = sum(inst.get_num_preemption() for inst in self.live())
         c0 = await self.call_all("counters")
+        ht0 = [dict(inst.host_time) for inst in self.instances]
         await self.call_all("mark", "w0")
         trans0 = [len(g.transitions) for g in self.groups]
 
@@ -437,6 +438,13 @@ class Job:
         win_ms = max(await asyncio.gather(*[self._elapsed(w) for w in self.workers]))
         c1 = await self.call_all("counters")
         c1[0] = c1_gpu0
+        ht = {k: round(sum(inst.host_time[k] - h[k] for inst, h in zip(self.instances, ht0)), 4)
+              for k in ht0[0]}
+        host_profile = {"frontend_s": ht,
+                        "gpu0": {"steps": c1[0]["steps"] - c0[0]["steps"],
+                                 "gpu_s": round((c1[0]["gpu_ms"] - c0[0]["gpu_ms"]) / 1000.0, 4),
+                                 "step_call_s": round(c1[0]["step_s"] - c0[0]["step_s"], 4),
+                                 "pack_s": round(c1[0]["pack_s"] - c0[0]["pack_s"], 4)}}
         # token times of the requests still in flight at the window's end
         for inst in self.live():
             for r in list(inst.unaccepted_queue) + [r for s in inst.scheduler for r in s.all_requests()]:
@@ -497,7 +505,7 @@ class Job:
             "restored_gb": round(sum(b for b, _ in restore) / 1e9, 3),
             "restore_gbps": round(sum(b for b, _ in restore) / 1e9 / max(sum(s for _, s in restore), 1e-9), 1)
             if restore else None,
-            "clocks": clock_info,
+            "clocks": clock_info, "host_profile": host_profile,
         }
 
     async def _elapsed(self, w):
@@ -513,9 +521,14 @@ async def run(job, args, pages):
     base = None
     if not args.no_baseline:
         await job.call_all("set_library_mode", True)
+        p2p = [inst.p2p_kv for inst in job.instances]
+        for inst in job.instances:
+            inst.p2p_kv = False      # NCCL exchange in exchange_batch_size batches, as the reference
         await job.warmup(args.warmup)
         base = await job.measure("library-baseline", via_api=False)
         await job.call_all("set_library_mode", False)
+        for inst, v in zip(job.instances, p2p):
+            inst.p2p_kv = v
     return native, e2e, base
 
 
@@ -669,7 +682,7 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
         "transitions_in_window": nat["transitions_in_window"], "transitions": nat["transitions"],
         "restored_gb": nat["restored_gb"], "restore_gbps": nat["restore_gbps"], "drain_s": nat["drain_s"],
         "gpu_launches": int(nat["launches"]), "forward_busy_frac": round(nat["fwd_busy"], 3),
-        "clocks": nat["clocks"],
+        "clocks": nat["clocks"], "host_profile": nat["host_profile"],
     }
     if base is not None:
         line["baseline"] = {"impl": "library baseline: ATen/cuBLAS GEMMs, NCCL all-reduce and NCCL KV/weight moves",

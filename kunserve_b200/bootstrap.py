@@ -43,15 +43,19 @@ def connect_to_ray_cluster(address: Optional[str] = None) -> bool:
     return True
 
 
-def make_worker_process(rank: int, world: int, port: int, topo: Topology, mc: ModelConfig, cc: CacheConfig,
+def make_worker_process(rank: int, world: int, rendezvous, topo: Topology, mc: ModelConfig, cc: CacheConfig,
                         pc: ParallelConfig, backend: str, device: str, seed: int, timeout_s: float = 120.0):
-    """Runs inside a worker process: joins the job and builds the Worker."""
+    """Runs inside a worker process: joins the job and builds the Worker.
+    ``rendezvous`` is a file path (workers on this node) or a TCP port."""
     from .parallel.comm import Communicator, init_default_group
 
     if device.startswith("cuda"):
         torch.cuda.set_device(torch.device(device))
     dist_backend = "nccl" if device.startswith("cuda") else "gloo"
-    init_default_group(dist_backend, rank, world, timeout_s=timeout_s, master_port=port)
+    if isinstance(rendezvous, str):
+        init_default_group(dist_backend, rank, world, timeout_s=timeout_s, init_file=rendezvous)
+    else:
+        init_default_group(dist_backend, rank, world, timeout_s=timeout_s, master_port=rendezvous)
     comm = Communicator(topo, rank, dist_backend)
     return Worker(rank, mc, cc, pc, backend=backend, device=device, comm=comm, seed=seed)
 
@@ -68,7 +72,13 @@ def build_instances(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: S
         devices = [f"cuda:{r % n}" for r in range(world)] if n else ["cpu"] * world
     if actor_kind == "auto":
         actor_kind = "ray" if ray_available() else ("local" if world == 1 else "process")
-    port = free_port()
+    # worker processes of one node meet through a fresh file (a TCP port
+    # picked here could be taken by someone else before rank 0 binds it);
+    # Ray actors may live on other nodes and use a port
+    import tempfile
+    import uuid
+    rendezvous = (free_port() if actor_kind == "ray"
+                  else os.path.join(tempfile.gettempdir(), f"kus-rdzv-{os.getpid()}-{uuid.uuid4().hex[:12]}"))
     handles = {}
     for rank in range(world):
         pc = rank_parallel_config(topo, rank)
@@ -77,11 +87,11 @@ def build_instances(cfg: KunServeConfig, mc: ModelConfig, cc: CacheConfig, sc: S
         elif actor_kind == "process":
             env = {"KUNSERVE_WORKER_RANK": str(rank)}
             # every rank must be spawned before any can finish joining the job
-            handles[rank] = ProcessActor(make_worker_process, rank, world, port, topo, mc, cc, pc, backend,
+            handles[rank] = ProcessActor(make_worker_process, rank, world, rendezvous, topo, mc, cc, pc, backend,
                                          devices[rank], seed, env=env, wait_ready=False)
         else:
-            handles[rank] = make_actor("ray", make_worker_process, rank, world, port, topo, mc, cc, pc, backend,
-                                       devices[rank], seed, num_gpus=1 if devices[rank] != "cpu" else 0)
+            handles[rank] = make_actor("ray", make_worker_process, rank, world, rendezvous, topo, mc, cc, pc,
+                                       backend, devices[rank], seed, num_gpus=1 if devices[rank] != "cpu" else 0)
     if actor_kind == "process":
         for h in handles.values():
             h.wait_ready()

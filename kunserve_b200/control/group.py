@@ -96,6 +96,8 @@ class GroupEngine:
                                                                  if j != i}))
                                        for i, w in enumerate(members)])
         self.p2p = True
+        for inst in self.instances:
+            inst.p2p_kv = True
         return True
 
     # ------------------------------------------------------------ votes
@@ -141,12 +143,16 @@ class GroupEngine:
             await self._trigger_restore()
 
     async def _trigger_restore(self) -> None:
+        """Reclaim the extend pages, pull the dropped parameters back while
+        the fused pipeline keeps serving (the reference restores before it
+        stops the engines, ``kunserve/llm_engine.py:546-570``), then stop
+        briefly to switch the block managers back to whole pages."""
         t0 = time.perf_counter()
         leader = self.leader
         await leader.reclaim_extra_blocks()
+        await leader.pmm_restore()
         self.state = EngineState.STOP
         await self.stop_all_engines()
-        await leader.pmm_restore()
         leader.restore_instance()
         self.state = EngineState.RESTORE
         self.start()

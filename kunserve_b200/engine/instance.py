@@ -91,6 +91,10 @@ class InstanceEngine(AdmissionMixin):
         self.is_restoring = False
         self.is_reclaiming_ex_blocks = False
         self.allocate_lock = asyncio.Lock()
+        self.p2p_kv = False         # KV moves as in-kernel pulls over mapped peer memory
+        # host seconds by phase (scheduling between steps, building step
+        # inputs, waiting for the workers' forward), for profiling the loop
+        self.host_time = {"schedule": 0.0, "build": 0.0, "forward": 0.0, "post": 0.0}
         self.num_gpu_blocks = 0
         self.block_size_in_bytes = 0
         self.step_counter = 0
@@ -251,12 +255,18 @@ class InstanceEngine(AdmissionMixin):
             seeds=[(p.seed if p.seed is not None else r.request_id) for p, r in zip(sp, requests)],
             step_id=self.step_counter)
 
-    async def _forward(self, requests: List[Request], fusion_exec: bool, kv_rank: int) -> List[int]:
+    async def _forward(self, requests: List[Request], fusion_exec: bool, kv_rank: int,
+                       restore: Optional[tuple] = None) -> List[int]:
+        tb = time.perf_counter()
         stage_layers = self.model_config.get_num_layers(self.parallel_config)
         chain = self._chain(fusion_exec, kv_rank)
         comm = "gp" if (fusion_exec and self.num_instances > 1) else "pp"
         steps = {inst: self._build_step(requests, inst, stage_layers, fusion_exec)
                  for inst in {c[0] for c in chain}}
+        if restore is not None:
+            home, n, tables, dp = restore
+            for inst, st in steps.items():
+                st.restore = (home, n, inst, tables, dp)
         self.step_counter += 1
         futs = []
         for k, (inst, stage) in enumerate(chain):
@@ -268,11 +278,14 @@ class InstanceEngine(AdmissionMixin):
             last = k + 1 == len(chain)
             for w in self.workers[inst * self.pp_size + stage]:
                 futs.append((last, w.step.remote(steps[inst], recv_from, send_to, last)))
+        tf = time.perf_counter()
+        self.host_time["build"] += tf - tb
         result = None
         for last, f in futs:
             out = await aw(f)
             if last and result is None:
                 result = out
+        self.host_time["forward"] += time.perf_counter() - tf
         return result
 
     async def _step(self, ve: int) -> None:
@@ -301,7 +314,9 @@ class InstanceEngine(AdmissionMixin):
             if self.is_reclaiming_ex_blocks:
                 await self.pack_blocks_into_base_region(pipe)
             async with self.allocate_lock:
+                t0 = time.perf_counter()
                 await self._get_next_batch(ve)
+                self.host_time["schedule"] += time.perf_counter() - t0
         finally:
             self.scheduler_running[ve] = False
 
@@ -327,10 +342,18 @@ class InstanceEngine(AdmissionMixin):
         batch = BatchedRequests(requests)
         t0 = time.time()
         batch.start_one_iteration(t0)
-        tokens = await self._forward(requests, fusion_exec, kv_rank)
-        t1 = time.time()
+        restore = None
         if restore_reqs:
-            await self._live_restore(kv_rank, restore_reqs, restore_pages)
+            n = self.num_instances
+            tables = [[p for r, dp in zip(restore_reqs, restore_pages)
+                       for p in self.block_managers[i].get_single_block_table(r.request_id)[:len(dp)]]
+                      for i in range(n)]
+            restore = (kv_rank, n, tables, [p for dp in restore_pages for p in dp])
+        tokens = await self._forward(requests, fusion_exec, kv_rank, restore)
+        t1 = time.time()
+        tp0 = time.perf_counter()
+        if restore_reqs:
+            self._finish_live_restore(kv_rank, restore_reqs, restore_pages)
         self.step_log.append((t1 - t0, batch.get_num_input_tokens(), len(requests)))
         texts = self._detok(tokens[:len(requests)])
         batch.finish_one_iteration(texts, tokens[:len(requests)], t1)
@@ -354,6 +377,7 @@ class InstanceEngine(AdmissionMixin):
                                           r.server_info, True, arrival_time=r.arrival_time))
         if outs and self.output_callback is not None:
             self.output_callback(outs)
+        self.host_time["post"] += time.perf_counter() - tp0
 
     def _detok(self, ids: Sequence[int]) -> List[str]:
         if self.tokenizer is None:
@@ -736,7 +760,9 @@ class InstanceEngine(AdmissionMixin):
         requests keep their place in their VE's running queue; what cannot be
         placed on the other members is recomputed instead."""
         remaining = list(requests)
-        cap = self.balloon_config.exchange_batch_size or len(remaining) or 1
+        # the NCCL exchange stages each batch in a scratch buffer, so batches
+        # are bounded; the P2P pulls copy page to page and take all at once
+        cap = (len(remaining) if self.p2p_kv else self.balloon_config.exchange_batch_size) or len(remaining) or 1
         while remaining:
             head, remaining = remaining[:cap], remaining[cap:]
             ok, fail = self.prepare_reshard_blocks(head)
@@ -789,12 +815,23 @@ class InstanceEngine(AdmissionMixin):
         self.is_reclaiming_ex_blocks = False
 
     async def pmm_restore(self) -> None:
+        """Restore every member's dropped parameters (reference
+        ``pmm_restore``, called before the engines stop,
+        ``kunserve/llm_engine.py:546-570``): the pulls run on side streams
+        while this instance's fused pipeline keeps serving, and this returns
+        once every byte landed."""
         n = self.num_instances
         t0 = time.perf_counter()
         futs = []
         for i in range(n):
-            futs.extend(self._call_instance(i, "pmm_restore", n, None, i))
+            futs.extend(self._call_instance(i, "pmm_restore_start", n, None, i))
         moved = await asyncio.gather(*[aw(f) for f in futs])
+        while True:
+            done = await asyncio.gather(*[aw(f) for i in range(n) for f in self._call_instance(i, "pmm_restore_done")])
+            if all(done):
+                break
+            await asyncio.sleep(0.0005)
+        await asyncio.gather(*[aw(f) for i in range(n) for f in self._call_instance(i, "pmm_restore_finish")])
         dt = time.perf_counter() - t0
         self.event_log.append((time.time(), "pmm_restore", dt))
         self.restore_log.append((float(sum(moved)), dt))
@@ -807,17 +844,11 @@ class InstanceEngine(AdmissionMixin):
         self.state = "restore"
         self.stopped = False
 
-    async def _live_restore(self, home: int, reqs: List[Request], pages: List[List[int]]) -> None:
-        n = self.num_instances
-        futs = []
+    def _finish_live_restore(self, home: int, reqs: List[Request], pages: List[List[int]]) -> None:
+        """Bookkeeping after a step that moved ``reqs`` home: their KV now
+        lives in ``pages`` on the home instance (every member copied its
+        layer slice inside the step)."""
         for r, dp in zip(reqs, pages):
-            tables = [self.block_managers[i].get_single_block_table(r.request_id)[:len(dp)] for i in range(n)]
-            for i in range(n):
-                for st in range(self.pp_size):
-                    for w in self.workers[i * self.pp_size + st]:
-                        futs.append(w.kv_restore.remote(i, n, home, tables, dp))
-            await asyncio.gather(*[aw(f) for f in futs])
-            futs = []
             for bm in self.block_managers:
                 if bm.is_allocated(r.request_id):
                     bm.free_request(r.request_id)

@@ -9,6 +9,7 @@ hidden buffer.
 import itertools
 import math
 import os
+import time
 from typing import List, Optional, Tuple
 
 import numpy as np
@@ -217,6 +218,7 @@ class NativeRunner:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.num_steps = 0
+        self.pack_s = 0.0      # host seconds spent packing step metadata
 
     def set_library_mode(self, on: bool) -> None:
         """Switch between this library's kernels (fused TP collectives, P2P
@@ -281,10 +283,12 @@ class NativeRunner:
 
     def step(self, step: StepInput, recv_from: Optional[Tuple[str, int]] = None,
              send_to: Optional[Tuple[str, int]] = None, last_stage: bool = True) -> Optional[List[int]]:
+        tp = time.perf_counter()
         width = max([len(p) for p in step.page_tables] + [1])
         n, T, B, n_items, max_ctx, n_dec, n_units, dec_heads = pack_meta(
             step, self.layout.block_size, self.group, width, self.meta_np, self.shape.nkv, self.num_sms,
             self.dec_hg_max)
+        self.pack_s += time.perf_counter() - tp
         splits = self._splits(T, n_items, max_ctx) if n_items else 1
         first = recv_from is None
         if not first:
@@ -345,7 +349,7 @@ class NativeRunner:
             self._fd_server = None
 
     def _pull(self, dst_base: int, dst_extent: int, src_base: int, src_extent: int, dst: List[int], src: List[int],
-              chunk: int) -> None:
+              chunk: int, max_blocks: Optional[int] = None) -> None:
         """Copy ``chunk``-byte pieces ``src[i] -> dst[i]`` between two mapped
         ranges (either may be a peer GPU's memory).  Every piece is checked
         against its range's extent first: the copy kernel itself does not
@@ -357,7 +361,7 @@ class NativeRunner:
         _check_extent("source", src, chunk, src_extent)
         d = torch.tensor(dst, dtype=torch.int64, device=self.device)
         s = torch.tensor(src, dtype=torch.int64, device=self.device)
-        self.eng.copy_chunks(dst_base, src_base, d, s, chunk, 4 * self.num_sms)
+        self.eng.copy_chunks(dst_base, src_base, d, s, chunk, max_blocks or 4 * self.num_sms)
 
     # ---------------------------------------------------------- balloon
     def drop_layers(self, layers: List[int], fusion_size: int) -> int:
@@ -367,23 +371,61 @@ class NativeRunner:
         return int(self.ext_pages)
 
     def restore_layers(self, dropped, keepers, my_rank, n) -> float:
-        """Remap the dropped layers and pull their bytes from the keepers."""
+        """Remap the dropped layers and pull their bytes from the keepers
+        (waits until they landed)."""
+        moved = self.restore_layers_start(keepers, my_rank, n)
+        self.restore_layers_wait()
+        return moved
+
+    def restore_layers_start(self, keepers, my_rank, n) -> float:
+        """Remap the dropped layers to their home addresses and start pulling
+        their bytes from the keepers over NVLink on a side stream with a CTA
+        budget (``KUNSERVE_RESTORE_CTAS``), so decode steps of the fused
+        pipeline keep running on the compute stream meanwhile: those steps
+        only touch the layers this rank kept, and the extend pages that lived
+        in the dropped layers' memory were reclaimed before.  The NCCL path
+        (library baseline, or no peer mappings) is a collective and completes
+        here.  Returns the bytes this rank receives."""
         restored = self.eng.restore_layers()
+        self.ext_pages = 0
+        self.fusion_size = 1
         moved = 0.0
         if n > 1 and self._p2p():
             chunk = 1 << 20
-            for l in restored:
-                nb = self.eng.layer_segment_bytes(l)
-                offs = list(range(0, nb, chunk))
-                peer = self.peer_maps[keepers[l]]
-                self._pull(self.eng.layer_ptr(l), nb, peer.layers[l], peer.layer_bytes[l], offs, offs, chunk)
-                moved += nb
-            torch.cuda.synchronize(self.device)
+            side = self._side_stream()
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            budget = int(os.environ.get("KUNSERVE_RESTORE_CTAS", str(self.num_sms)))
+            with torch.cuda.stream(side):
+                for l in restored:
+                    nb = self.eng.layer_segment_bytes(l)
+                    offs = list(range(0, nb, chunk))
+                    peer = self.peer_maps[keepers[l]]
+                    self._pull(self.eng.layer_ptr(l), nb, peer.layers[l], peer.layer_bytes[l], offs, offs, chunk,
+                               max_blocks=budget)
+                    moved += nb
+                self._restore_ev = torch.cuda.Event()
+                self._restore_ev.record(side)
         elif self.comm is not None and n > 1:
             moved = self._pull_layers(restored, keepers, my_rank, n)
-        self.ext_pages = 0
-        self.fusion_size = 1
         return moved
+
+    def restore_layers_done(self) -> bool:
+        ev = getattr(self, "_restore_ev", None)
+        return ev is None or ev.query()
+
+    def restore_layers_wait(self) -> None:
+        """Block until the restored layers' bytes landed; later work on the
+        compute stream is ordered after them."""
+        ev = getattr(self, "_restore_ev", None)
+        if ev is not None:
+            torch.cuda.current_stream(self.device).wait_event(ev)
+            ev.synchronize()
+            self._restore_ev = None
+
+    def _side_stream(self) -> torch.cuda.Stream:
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(self.device)
+        return self._side
 
     def _pull_layers(self, restored, keepers, my_rank, n) -> float:
         # NCCL baseline path: every rank sends the layers it kept
@@ -468,6 +510,29 @@ class NativeRunner:
         src = [i * chunk for i in range(len(dst_offs))]
         self._pull(self.eng.kv_base_ptr(), self.pool_extent(), buf.data_ptr(), buf.numel() * buf.element_size(),
                    list(dst_offs), src, chunk)
+
+    def push_restore(self, home: int, n: int, member: int, tables: List[List[int]], dp_pages: List[int],
+                     chunk: int) -> None:
+        """Live restore inside a step: copy this member's layer slice of the
+        pipeline requests that move home (``tables[member]``: their fusion
+        page ids here; ``tables[j]`` on member j) into their
+        new whole pages on the home member, right behind this step's layers
+        on the compute stream (stores into the home GPU's mapped pool over
+        NVLink; a local copy on the home member).  Waits for the copy, so the
+        step's result means the slice landed.  Without peer mappings, the
+        NCCL exchange of ``kv_restore`` runs instead (all members join it)."""
+        from ..kv import copy_plan
+        if not self._p2p():
+            self.kv_restore(member, n, home, tables, dp_pages, chunk)
+            return
+        src, dst = copy_plan.restore_plan(self.layout, n, member, tables[member], dp_pages)
+        ext = self.pool_extent()
+        if member == home:
+            self._pull(self.eng.kv_base_ptr(), ext, self.eng.kv_base_ptr(), ext, dst, src, chunk)
+        else:
+            peer = self.peer_maps[home]
+            self._pull(peer.kv, peer.kv_bytes, self.eng.kv_base_ptr(), ext, dst, src, chunk)
+        torch.cuda.current_stream(self.device).synchronize()
 
     def kv_restore(self, my_rank, n, home, fusion_pages, dp_pages, chunk) -> int:
         from ..kv import copy_plan

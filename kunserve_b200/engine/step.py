@@ -29,6 +29,12 @@ class StepInput:
     top_p: Optional[List[float]] = None
     seeds: Optional[List[int]] = None
     step_id: int = 0
+    # live restore inside the step (the reference pforward's pages_of_pp /
+    # pages_of_dp / receiver_rank): (home member, group size, this member,
+    # per-member fusion page ids, the home's new whole pages), concatenated
+    # over the requests that move home.  After its layers, each member copies
+    # its layer slice of those pages into the home member's pool.
+    restore: Optional[tuple] = None
 
     @property
     def num_requests(self) -> int:

@@ -59,6 +59,7 @@ class Worker:
         self.dropped: List[int] = []
         self.step_times: List[float] = []
         self.steps_done = 0
+        self.step_wall_s = 0.0
 
     def ready(self) -> bool:
         return True
@@ -119,6 +120,9 @@ class Worker:
         t0 = time.perf_counter()
         if self.backend == "native":
             out = self.runner.step(step, recv_from, send_to, last_stage)
+            if step.restore is not None:
+                home, n, member, tables, dp = step.restore
+                self.runner.push_restore(home, n, member, tables, dp, copy_plan.chunk_bytes(self.layout, n))
         else:
             hidden_in = None
             if recv_from is not None:
@@ -128,7 +132,11 @@ class Worker:
             if send_to is not None:
                 self.comm.send(h, *send_to)
             out = self.runner.sample(h, step).tolist() if last_stage else None
+            if step.restore is not None:
+                home, n, member, tables, dp = step.restore
+                self.kv_restore(member, n, home, tables, dp)
         self.step_times.append(time.perf_counter() - t0)
+        self.step_wall_s += self.step_times[-1]
         self.steps_done += 1
         arm = getattr(self, "_armed", None)
         if arm is not None and self.steps_done == arm[1]:
@@ -172,15 +180,36 @@ class Worker:
     def pmm_restore(self, num_group_instances: int, keepers: Optional[Dict[int, int]] = None,
                     my_group_rank: int = 0) -> float:
         """Take the extend region back and re-fetch the dropped layers from the
-        peers that kept them (``keepers[layer] = kvex index``).  Returns the
-        bytes moved."""
+        peers that kept them (``keepers[layer] = kvex index``); returns once
+        they landed.  Returns the bytes moved."""
+        moved = self.pmm_restore_start(num_group_instances, keepers, my_group_rank)
+        self.pmm_restore_finish()
+        return moved
+
+    def pmm_restore_done(self) -> bool:
+        """Whether the pulls that ``pmm_restore_start`` began have landed."""
+        return self.runner.restore_layers_done() if self.backend == "native" else True
+
+    def pmm_restore_finish(self) -> None:
+        if self.backend == "native":
+            self.runner.restore_layers_wait()
+        self.dropped = []
+        self.fusion_size = 1
+
+    def pmm_restore_start(self, num_group_instances: int, keepers: Optional[Dict[int, int]] = None,
+                          my_group_rank: int = 0) -> float:
+        """Start the parameter restore: with peer memory mapped the pulls run
+        on a side stream and this returns at once (poll ``pmm_restore_done``,
+        then ``pmm_restore_finish``); decode steps of the fused pipeline may
+        run meanwhile.  The NCCL/gloo path completes before returning.
+        Returns the bytes this rank receives."""
         n = num_group_instances
         L = self.shapes.num_layers
         ls = L // n
         if keepers is None:
             keepers = {l: l // ls for l in range(L)}
         if self.backend == "native":
-            return self.runner.restore_layers(self.dropped, keepers, my_group_rank, n)
+            return self.runner.restore_layers_start(keepers, my_group_rank, n)
         self.runner.pool.shrink_extend()
         moved = 0
         # every rank sends the layers it kept to every rank that dropped them
@@ -214,8 +243,6 @@ class Worker:
                     off += numel
                 self.runner.w.layers[l] = lw
                 moved += off * buf.element_size()
-        self.dropped = []
-        self.fusion_size = 1
         return float(moved)
 
     # -------------------------------------------------------- KV movement
@@ -402,10 +429,12 @@ class Worker:
     def counters(self) -> Dict[str, float]:
         """Launch, step, byte and device-time counters of the native runner."""
         if self.backend != "native":
-            return {"launches": 0, "steps": self.steps_done, "gpu_ms": 0.0, "h2d": 0, "d2h": 0}
+            return {"launches": 0, "steps": self.steps_done, "gpu_ms": 0.0, "h2d": 0, "d2h": 0, "pack_s": 0.0,
+                    "step_s": float(self.step_wall_s)}
         r = self.runner
-        return {"launches": int(r.eng.launches()), "steps": int(r.num_steps), "gpu_ms": float(r.gpu_ms),
-                "h2d": int(r.h2d_bytes), "d2h": int(r.d2h_bytes)}
+        return {"launches": int(r.eng.launches()), "steps": self.steps_done, "gpu_ms": float(r.gpu_ms),
+                "h2d": int(r.h2d_bytes), "d2h": int(r.d2h_bytes), "pack_s": float(r.pack_s),
+                "step_s": float(self.step_wall_s)}
 
     def last_logits(self, n: int) -> torch.Tensor:
         """fp32 logits of the last step's ``n`` rows (left by sample mode 1)."""

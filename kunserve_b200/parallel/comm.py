@@ -18,8 +18,16 @@ from .topology import COMMS, Topology
 
 
 def init_default_group(backend: str, rank: int, world_size: int, timeout_s: float = 120.0,
-                       master_addr: str = "127.0.0.1", master_port: Optional[int] = None) -> None:
+                       master_addr: str = "127.0.0.1", master_port: Optional[int] = None,
+                       init_file: Optional[str] = None) -> None:
+    """Join the job's default process group: through a shared file when
+    ``init_file`` is given (processes on one node; no port to race for),
+    else through ``master_addr:master_port``."""
     if dist.is_initialized():
+        return
+    if init_file is not None:
+        dist.init_process_group(backend, init_method=f"file://{init_file}", rank=rank, world_size=world_size,
+                                timeout=timedelta(seconds=timeout_s))
         return
     os.environ.setdefault("MASTER_ADDR", master_addr)
     if master_port is not None:
