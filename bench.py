@@ -474,6 +474,21 @@ class Job:
                 break
             await asyncio.sleep(0.01)
         drain_s = time.time() - t_drain
+        c2 = await self.call_all("counters")
+        restore_dev = [(y["restore_bytes"] - x["restore_bytes"], y["restore_s"] - x["restore_s"])
+                       for x, y in zip(c1, c2) if y["restore_bytes"] > x["restore_bytes"]]
+        # inter-token gaps while the parameters were being restored, against the
+        # fused pipeline's gaps in the second before the restore started
+        spans = [(t - dt, t) for inst in self.instances for t, name, dt in inst.event_log
+                 if name == "pmm_restore" and t >= t_drain]
+        gaps_in, gaps_before = [], []
+        for _, times, _ in recs.values():
+            for x, y in zip(times, times[1:]):
+                for r0, r1 in spans:
+                    if r0 <= y <= r1:
+                        gaps_in.append(y - x)
+                    elif r0 - 1.0 <= y < r0:
+                        gaps_before.append(y - x)
         self.llm.coordinator.stop()
         for t in tasks:
             t.cancel()
@@ -505,6 +520,13 @@ class Job:
             "restored_gb": round(sum(b for b, _ in restore) / 1e9, 3),
             "restore_gbps": round(sum(b for b, _ in restore) / 1e9 / max(sum(s for _, s in restore), 1e-9), 1)
             if restore else None,
+            "restore_device": {"gb_per_gpu": round(np.mean([b for b, _ in restore_dev]) / 1e9, 3),
+                               "gbps_per_gpu": round(np.mean([b / max(d, 1e-9) for b, d in restore_dev]) / 1e9, 1),
+                               "tbt_p50_during_s": round(pct(gaps_in, 50), 4),
+                               "tbt_p99_during_s": round(pct(gaps_in, 99), 4),
+                               "tbt_p50_before_s": round(pct(gaps_before, 50), 4),
+                               "tbt_p99_before_s": round(pct(gaps_before, 99), 4),
+                               "gaps_during": len(gaps_in)} if restore_dev else None,
             "clocks": clock_info, "host_profile": host_profile,
         }
 
@@ -520,15 +542,12 @@ async def run(job, args, pages):
     e2e = None if args.no_e2e else await job.measure("native-e2e", via_api=True)
     base = None
     if not args.no_baseline:
+        # same scheduler and balloon policy; only the kernels and the transport
+        # (NCCL collectives and send/recv instead of fused kernels and P2P pulls) differ
         await job.call_all("set_library_mode", True)
-        p2p = [inst.p2p_kv for inst in job.instances]
-        for inst in job.instances:
-            inst.p2p_kv = False      # NCCL exchange in exchange_batch_size batches, as the reference
         await job.warmup(args.warmup)
         base = await job.measure("library-baseline", via_api=False)
         await job.call_all("set_library_mode", False)
-        for inst, v in zip(job.instances, p2p):
-            inst.p2p_kv = v
     return native, e2e, base
 
 
@@ -680,7 +699,8 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
         "kv_used_at_start": nat["kv_used_at_start"], "fill_steps": nat["fill_steps"],
         "preemptions": nat["preemptions"], "tpot_samples": nat["tpot_samples"],
         "transitions_in_window": nat["transitions_in_window"], "transitions": nat["transitions"],
-        "restored_gb": nat["restored_gb"], "restore_gbps": nat["restore_gbps"], "drain_s": nat["drain_s"],
+        "restored_gb": nat["restored_gb"], "restore_gbps": nat["restore_gbps"],
+        "restore_device": nat["restore_device"], "drain_s": nat["drain_s"],
         "gpu_launches": int(nat["launches"]), "forward_busy_frac": round(nat["fwd_busy"], 3),
         "clocks": nat["clocks"], "host_profile": nat["host_profile"],
     }

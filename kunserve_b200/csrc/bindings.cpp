@@ -168,11 +168,13 @@ void attention_op(torch::Tensor q, int64_t q_stride, torch::Tensor out, torch::T
                   (float)scale, at::cuda::getCurrentCUDAStream());
 }
 
-void sample_op(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, int64_t step, torch::Tensor out) {
+void sample_op(torch::Tensor logits, torch::Tensor temps, torch::Tensor seeds, int64_t step, torch::Tensor out,
+               c10::optional<torch::Tensor> top_k, c10::optional<torch::Tensor> top_p) {
   c10::cuda::CUDAGuard g(logits.device());
   sample(logits.data_ptr<float>(), logits.size(0), logits.size(1), logits.size(1), temps.data_ptr<float>(),
          reinterpret_cast<const unsigned*>(seeds.data_ptr<int>()), (unsigned long long)step, out.data_ptr<int>(),
-         at::cuda::getCurrentCUDAStream());
+         at::cuda::getCurrentCUDAStream(), top_k ? top_k->data_ptr<int>() : nullptr,
+         top_p ? top_p->data_ptr<float>() : nullptr);
 }
 
 void embed_op(torch::Tensor tokens, torch::Tensor table, torch::Tensor out) {
@@ -403,7 +405,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm_op);
   m.def("rope_append", &rope_append_op);
   m.def("attention", &attention_op);
-  m.def("sample", &sample_op);
+  m.def("sample", &sample_op, py::arg("logits"), py::arg("temps"), py::arg("seeds"), py::arg("step"),
+        py::arg("out"), py::arg("top_k") = py::none(), py::arg("top_p") = py::none());
   m.def("embed", &embed_op);
   m.def("copy_chunks", &copy_chunks_op);
   m.def("tp_gemm_allreduce", &tp_gemm_allreduce_op);

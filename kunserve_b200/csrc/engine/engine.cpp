@@ -93,7 +93,7 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   dec_ml_ = torch::empty({(int64_t)kDecUnitSlots * s.nq * 2}, f32);
   dec_count_ = torch::zeros({(int64_t)kDecCountSlots}, i32);
   const int64_t max_items = T * std::max(1, s.nq / s.nkv) / 64 + B + 1;
-  const int64_t meta_ints = 2 * max_items + 4 * T + 5 * B + 1 +
+  const int64_t meta_ints = 2 * max_items + 4 * T + 7 * B + 1 +
                             B * (int64_t)((s.max_pos + s.block_size - 1) / s.block_size) + kDecUnitInts * kDecUnitSlots + 64;
   meta_dev_ = torch::empty({meta_ints}, i32);
   tokens_dev_ = torch::empty({B}, i32);
@@ -374,11 +374,12 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   cudaStream_t st = at::cuda::getCurrentCUDAStream(device_);
   KUS_CHECK(n_dec >= 0 && n_dec <= B && n_units >= n_dec && n_units <= kDecUnitSlots && (n_units > 0) == (n_dec > 0),
             "bad decode attention units");
-  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 2 * B + n_dec + kDecUnitInts * n_units;
+  const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 4 * B + n_dec + kDecUnitInts * n_units;
   KUS_CHECK(meta.numel() >= n_meta && n_meta <= meta_dev_.numel(), "meta buffer too small");
   check_cuda(cudaMemcpyAsync(meta_dev_.data_ptr(), meta.data_ptr(), n_meta * 4, cudaMemcpyHostToDevice, st), "meta H2D");
   // meta layout (int32): items[2n] | tokens[T] | positions[T] | kv_page[T] | kv_slot[T] |
   // q_start[B+1] | ctx_len[B] | last_idx[B] | page_table[B*max_pages] | temps[B] (f32) | seeds[B] |
+  // top_k[B] | top_p[B] (f32) |
   // dec_reqs[n_dec] | dec_units[8*n_units]
   const int* m = meta_dev_.data_ptr<int>();
   const int2* items = reinterpret_cast<const int2*>(m);
@@ -392,7 +393,9 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   const int* table = last_idx + B;
   const float* temps = reinterpret_cast<const float*>(table + B * max_pages);
   const unsigned* seeds = reinterpret_cast<const unsigned*>(temps + B);
-  const int* dec_reqs = reinterpret_cast<const int*>(seeds + B);
+  const int* top_k = reinterpret_cast<const int*>(seeds + B);
+  const float* top_p = reinterpret_cast<const float*>(top_k + B);
+  const int* dec_reqs = reinterpret_cast<const int*>(top_p + B);
   const int* dec_units = dec_reqs + n_dec;
 
   KVGeom geo;
@@ -533,7 +536,7 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     return out;
   }
   sample(logits_.data_ptr<float>(), (int)B, s_.vocab, s_.vocab, temps, seeds, (unsigned long long)step,
-         tokens_dev_.data_ptr<int>(), st);
+         tokens_dev_.data_ptr<int>(), st, top_k, top_p);
   ++launches_;
   check_cuda(cudaMemcpyAsync(tokens_host_.data_ptr(), tokens_dev_.data_ptr(), B * 4, cudaMemcpyDeviceToHost, st),
              "tokens D2H");

@@ -227,21 +227,120 @@ KUS_DEVICE uint64_t splitmix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
+// Order-preserving 32-bit key of a float: a > b  <=>  key(a) > key(b).
+KUS_DEVICE uint32_t order_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// Block-wide reductions over 1024 threads (32 warps).
+KUS_DEVICE float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = red[threadIdx.x & 31];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+KUS_DEVICE float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = red[threadIdx.x & 31];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Radix select, most significant byte first: the key K of the boundary
+// element when the row's keys are ordered from the largest down and each
+// element weighs one (top-k: the k-th largest) or its probability mass
+// exp((l - mx) / T) (top-p: the element at which the mass from the top
+// reaches `need`).  Only keys >= `floor` take part.  Four passes of a
+// 256-bin histogram in shared memory.
+template <bool MASS>
+KUS_DEVICE uint32_t radix_select(const float* __restrict__ row, int V, uint32_t floor, float need, float mx,
+                                 float invt, float* hist, uint32_t* shared_prefix, float* shared_need) {
+  uint32_t prefix = 0, mask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0.f;
+    __syncthreads();
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float l = row[i];
+      const uint32_t key = order_key(l);
+      if (key >= floor && (key & mask) == prefix)
+        atomicAdd(&hist[(key >> shift) & 255u], MASS ? __expf((l - mx) * invt) : 1.f);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float acc = 0.f;
+      int d = 255, last = -1;
+      for (; d >= 0; --d) {
+        if (hist[d] > 0.f) last = d;
+        if (hist[d] > 0.f && acc + hist[d] >= need) break;
+        acc += hist[d];
+      }
+      if (d < 0) d = last < 0 ? 0 : last;   // rounding left the target unmet: the lowest populated bin
+      *shared_prefix = prefix | ((uint32_t)d << shift);
+      *shared_need = need - acc;
+    }
+    __syncthreads();
+    prefix = *shared_prefix;
+    need = *shared_need;
+    mask |= 255u << shift;
+  }
+  return prefix;
+}
+
 __global__ void sample_kernel(const float* __restrict__ logits, int V, int ld, const float* __restrict__ temp,
+                              const int* __restrict__ top_k, const float* __restrict__ top_p,
                               const unsigned* __restrict__ seeds, unsigned long long step,
                               int* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
+  __shared__ float hist[256];
+  __shared__ float red[32];
+  __shared__ uint32_t s_prefix;
+  __shared__ float s_need;
   const int r = blockIdx.x;
   const float* row = logits + (size_t)r * ld;
   const float t = temp ? temp[r] : 0.f;
   const bool noisy = t > 1e-5f;
   const float invt = noisy ? 1.f / t : 1.f;
+  // the kept set is every logit whose key is >= thr (greedy rows keep all:
+  // the argmax belongs to every top-k / top-p set)
+  uint32_t thr = 0;
+  const int k = top_k ? top_k[r] : -1;
+  const float p = top_p ? top_p[r] : 1.f;
+  if (noisy && ((k > 0 && k < V) || p < 1.f)) {
+    if (k > 0 && k < V)
+      thr = radix_select<false>(row, V, 0u, (float)k, 0.f, 1.f, hist, &s_prefix, &s_need);
+    if (p < 1.f) {
+      float m = -INFINITY;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) m = fmaxf(m, row[i]);
+      m = block_max(m, red);
+      float z = 0.f;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float l = row[i];
+        if (order_key(l) >= thr) z += __expf((l - m) * invt);
+      }
+      z = block_sum(z, red);
+      // nucleus of the (top-k filtered) temperature distribution
+      thr = radix_select<true>(row, V, thr, p * z, m, invt, hist, &s_prefix, &s_need);
+    }
+  }
   const uint64_t base = noisy ? splitmix64((uint64_t)seeds[r] ^ splitmix64(step)) : 0;
   float best = -INFINITY;
   int arg = 0x7fffffff;
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     float v = row[i];
+    if (order_key(v) < thr) continue;
     if (noisy) {
       const uint64_t h = splitmix64(base + (uint64_t)i);
       // uniform in (0, 1): 24 random bits, offset by half a step
@@ -280,9 +379,9 @@ __global__ void sample_kernel(const float* __restrict__ logits, int V, int ld, c
 }
 
 void sample(const float* logits, int B, int V, int ld, const float* temp, const unsigned* seeds,
-            unsigned long long step, int* out, cudaStream_t s) {
+            unsigned long long step, int* out, cudaStream_t s, const int* top_k, const float* top_p) {
   if (B <= 0) return;
-  launch_k(sample_kernel, dim3(B), dim3(1024), 0, s, logits, V, ld, temp, seeds, step, out);
+  launch_k(sample_kernel, dim3(B), dim3(1024), 0, s, logits, V, ld, temp, top_k, top_p, seeds, step, out);
 }
 
 // ------------------------------------------------------------ chunk copy

@@ -75,8 +75,12 @@ void rmsnorm(__nv_bfloat16* x, const __nv_bfloat16* add, const __nv_bfloat16* w,
 void rope_append(__nv_bfloat16* qkv, const int* positions, const int* pages, const int* slots,
                  const float* cos_sin, const KVGeom& g, int layer, int T, int nq, int nkv, int max_pos,
                  cudaStream_t s, const float* parts = nullptr, int nparts = 0, long long pstride = 0);
+// Per-row token sampling: greedy (temperature 0) or Gumbel-max over the
+// temperature distribution restricted to the row's top-k logits (top_k[r] > 0)
+// and to its nucleus of mass top_p[r] (< 1) within them; both arrays may be null.
 void sample(const float* logits, int B, int V, int ld, const float* temp, const unsigned* seeds,
-            unsigned long long step, int* out, cudaStream_t s);
+            unsigned long long step, int* out, cudaStream_t s, const int* top_k = nullptr,
+            const float* top_p = nullptr);
 void copy_chunks(void* dst_base, const void* src_base, const long long* dst_off, const long long* src_off, int n,
                  long long chunk, int max_blocks, cudaStream_t s);
 void add_inplace(__nv_bfloat16* x, const __nv_bfloat16* y, long long n, cudaStream_t s);

@@ -17,7 +17,6 @@ import torch
 
 from ..config.runtime import ModelConfig, ParallelConfig
 from ..kv.layout import KVLayout
-from ..models.torch_llama import sample_tokens
 from ..ops import native
 from .step import StepInput
 
@@ -136,6 +135,8 @@ def pack_meta(step: StepInput, block_size: int, group: int, max_pages: int, buf:
     put(temps.view(np.int32))
     seeds = np.asarray(step.seeds if step.seeds is not None else [0] * B, dtype=np.int64) & 0xFFFFFFFF
     put(seeds.astype(np.uint32).view(np.int32))
+    put(np.asarray(step.top_k if step.top_k is not None else [-1] * B, dtype=np.int32))
+    put(np.asarray(step.top_p if step.top_p is not None else [1.0] * B, dtype=np.float32).view(np.int32))
     dec = np.nonzero(is_dec)[0].astype(np.int32)
     put(dec)
     hg = 1
@@ -201,7 +202,7 @@ class NativeRunner:
             torch.cuda.synchronize()
         self.max_pages = math.ceil(sh.max_pos / layout.block_size)
         n = (2 * (sh.max_tokens * self.group // Q_TILE_ROWS + sh.max_batch + 1) + 4 * sh.max_tokens
-             + 6 * sh.max_batch + 1 + sh.max_batch * self.max_pages + DEC_UNIT_INTS * DEC_UNIT_SLOTS + 64)
+             + 8 * sh.max_batch + 1 + sh.max_batch * self.max_pages + DEC_UNIT_INTS * DEC_UNIT_SLOTS + 64)
         self.meta = torch.empty(n, dtype=torch.int32, pin_memory=True)
         self.meta_np = self.meta.numpy()
         self.num_sms = C.num_sms()
@@ -219,6 +220,8 @@ class NativeRunner:
         self.d2h_bytes = 0
         self.num_steps = 0
         self.pack_s = 0.0      # host seconds spent packing step metadata
+        self.restore_s = 0.0   # device seconds of parameter-restore pulls, and their bytes
+        self.restore_bytes = 0.0
 
     def set_library_mode(self, on: bool) -> None:
         """Switch between this library's kernels (fused TP collectives, P2P
@@ -294,10 +297,7 @@ class NativeRunner:
         if not first:
             buf = self.comm.recv((T, self.shape.hidden), torch.bfloat16, self.device, *recv_from)
             self.eng.hidden()[:T].copy_(buf)
-        sample_mode = 0
-        if last_stage and step.top_k is not None and (any(k > 0 for k in step.top_k) or
-                                                      any(p < 1.0 for p in (step.top_p or []))):
-            sample_mode = 1
+        sample_mode = 0     # greedy, temperature, top-k and top-p all sample on the device
         if self._ev is None:
             self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         self._ev[0].record()
@@ -310,16 +310,12 @@ class NativeRunner:
         self.gpu_ms += self._ev[0].elapsed_time(self._ev[1])
         self.num_steps += 1
         self.h2d_bytes += 4 * n
-        if last_stage and sample_mode == 0:
+        if last_stage:
             self.d2h_bytes += 4 * B
         if send_to is not None:
             self.comm.send(self.eng.hidden()[:T], *send_to)
         if not last_stage:
             return None
-        if sample_mode == 1:
-            logits = self.eng.logits()[:B]
-            return sample_tokens(logits, step.temperature, step.top_k, step.top_p, step.seeds,
-                                 step.step_id).tolist()
         return list(out)
 
     # -------------------------------------------------------- peer memory
@@ -396,6 +392,8 @@ class NativeRunner:
             side.wait_stream(torch.cuda.current_stream(self.device))
             budget = int(os.environ.get("KUNSERVE_RESTORE_CTAS", str(self.num_sms)))
             with torch.cuda.stream(side):
+                self._restore_t = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                self._restore_t[0].record(side)
                 for l in restored:
                     nb = self.eng.layer_segment_bytes(l)
                     offs = list(range(0, nb, chunk))
@@ -403,8 +401,9 @@ class NativeRunner:
                     self._pull(self.eng.layer_ptr(l), nb, peer.layers[l], peer.layer_bytes[l], offs, offs, chunk,
                                max_blocks=budget)
                     moved += nb
-                self._restore_ev = torch.cuda.Event()
-                self._restore_ev.record(side)
+                self._restore_t[1].record(side)
+                self._restore_ev = self._restore_t[1]
+                self._restore_moved = moved
         elif self.comm is not None and n > 1:
             moved = self._pull_layers(restored, keepers, my_rank, n)
         return moved
@@ -421,6 +420,9 @@ class NativeRunner:
             torch.cuda.current_stream(self.device).wait_event(ev)
             ev.synchronize()
             self._restore_ev = None
+            # device time of the pulls (side stream), for the restore bandwidth
+            self.restore_s += self._restore_t[0].elapsed_time(self._restore_t[1]) / 1000.0
+            self.restore_bytes += self._restore_moved
 
     def _side_stream(self) -> torch.cuda.Stream:
         if getattr(self, "_side", None) is None:

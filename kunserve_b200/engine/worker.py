@@ -430,11 +430,12 @@ class Worker:
         """Launch, step, byte and device-time counters of the native runner."""
         if self.backend != "native":
             return {"launches": 0, "steps": self.steps_done, "gpu_ms": 0.0, "h2d": 0, "d2h": 0, "pack_s": 0.0,
-                    "step_s": float(self.step_wall_s)}
+                    "step_s": float(self.step_wall_s), "restore_s": 0.0, "restore_bytes": 0.0}
         r = self.runner
         return {"launches": int(r.eng.launches()), "steps": self.steps_done, "gpu_ms": float(r.gpu_ms),
                 "h2d": int(r.h2d_bytes), "d2h": int(r.d2h_bytes), "pack_s": float(r.pack_s),
-                "step_s": float(self.step_wall_s)}
+                "step_s": float(self.step_wall_s), "restore_s": float(r.restore_s),
+                "restore_bytes": float(r.restore_bytes)}
 
     def last_logits(self, n: int) -> torch.Tensor:
         """fp32 logits of the last step's ``n`` rows (left by sample mode 1)."""

@@ -7,10 +7,9 @@ Parity: ``kunserve/request.py`` — ``SamplingParams`` (:17-165),
 
 Differences by design:
 
-* Sampling parameters reach the engine (the reference always decodes
-  greedily): greedy and temperature sampling run in the sampling kernel;
-  a batch with top-k or top-p is sampled on the host path in torch from the
-  engine's fp32 logits.
+* Sampling parameters reach the device (the reference always decodes
+  greedily): the sampling kernel applies temperature, top-k and top-p
+  (radix select on the logits, then Gumbel-max over the kept tokens).
 * ``start_position()`` is the RoPE position of the first input token of the
   next step (prefill chunk start, or ``len(prompt) + len(generated) - 1`` for
   a decode step).  The reference passes ``input_len + output_len`` for decode

@@ -307,6 +307,57 @@ def test_sample_greedy_and_temperature(C):
     assert (freq - p).abs().max() < 0.04
 
 
+def _nucleus(probs, p):
+    sp, idx = torch.sort(probs, descending=True)
+    keep = torch.cumsum(sp, 0) - sp < p
+    return set(idx[keep].tolist())
+
+
+def test_sample_top_k_top_p_on_device(C):
+    """Top-k and top-p restrict the sampled set (radix select in the kernel):
+    frequencies on a 4-token vocabulary match the filtered, renormalised
+    softmax, and on a 32000-token vocabulary every sample lies in the set a
+    PyTorch reference keeps."""
+    n = 4000
+    lg = torch.tensor([[0.0, 1.0, 2.0, 3.0]], device="cuda").repeat(n, 1)
+    t = torch.ones(n, device="cuda")
+    sd = torch.arange(n, device="cuda", dtype=torch.int32)
+    o = torch.empty(n, device="cuda", dtype=torch.int32)
+    p_full = torch.softmax(lg[0], 0)
+    cases = [(2, 1.0, {2, 3}), (-1, 0.7, {2, 3}), (3, 0.8, {2, 3}), (-1, 0.95, {1, 2, 3}), (1, 1.0, {3})]
+    for k, p, keep in cases:
+        C.sample(lg, t, sd, 0, o, torch.full((n,), k, device="cuda", dtype=torch.int32),
+                 torch.full((n,), p, device="cuda"))
+        freq = torch.bincount(o.long(), minlength=4).float().cpu() / n
+        want = torch.zeros(4)
+        idx = sorted(keep)
+        want[idx] = p_full.cpu()[idx] / p_full.cpu()[idx].sum()
+        assert (freq - want).abs().max() < 0.04, (k, p, freq, want)
+    # a real vocabulary: every sample inside the reference's kept set
+    torch.manual_seed(3)
+    B, V = 64, 32000
+    logits = torch.randn(B, V, device="cuda") * 3
+    temps = torch.full((B,), 0.8, device="cuda")
+    top_k = torch.tensor([50, -1, 7, 1000] * 16, device="cuda", dtype=torch.int32)
+    top_p = torch.tensor([1.0, 0.5, 0.9, 0.2] * 16, device="cuda")
+    out = torch.empty(B, device="cuda", dtype=torch.int32)
+    for step in range(4):
+        C.sample(logits, temps, torch.arange(B, device="cuda", dtype=torch.int32), step, out, top_k, top_p)
+        for r in range(B):
+            lr = logits[r] / 0.8
+            k = int(top_k[r])
+            if k > 0:
+                kth = torch.topk(lr, k).values[-1]
+                lr = torch.where(lr < kth, torch.full_like(lr, float("-inf")), lr)
+            allowed = _nucleus(torch.softmax(lr, 0), float(top_p[r])) if float(top_p[r]) < 1 else \
+                set(torch.nonzero(torch.isfinite(lr)).flatten().tolist())
+            assert int(out[r]) in allowed, (r, k, float(top_p[r]))
+    # greedy rows ignore the filters
+    C.sample(logits, torch.zeros(B, device="cuda"), torch.arange(B, device="cuda", dtype=torch.int32), 0, out,
+             top_k, top_p)
+    assert torch.equal(out.long(), logits.argmax(-1))
+
+
 def test_copy_chunks(C):
     src = torch.randint(0, 255, (1 << 20,), device="cuda", dtype=torch.uint8)
     dst = torch.zeros_like(src)
