@@ -25,9 +25,12 @@ over all workers.  After the window the burst ends (queued requests are
 dropped) and serving continues untimed until every group is back in its
 initial state, which measures parameter restore.
 
-``value`` is the SLO goodput: requests that finished inside the window with
-TTFT <= ``--ttft-slo`` and TPOT (mean inter-token time) <= ``--tpot-slo``,
-per second of window, over the whole job.  ``vs_baseline`` divides it by the
+``value`` is the SLO goodput in request-equivalents per second of window,
+over the whole job: every token emitted inside the window counts
+1/output-length of a request when its request met TTFT <= ``--ttft-slo`` and
+keeps a mean inter-token time <= ``--tpot-slo`` (``summarize``); the plain
+count of requests that finished inside the window within both objectives is
+reported as ``finished_goodput``.  ``vs_baseline`` divides it by the
 same measurement in library-baseline mode, run in the same invocation on the
 same job and trace: every GEMM through ATen/cuBLAS with unfused epilogues,
 NCCL all-reduce, NCCL send/recv for KV migration and parameter restore.
@@ -181,13 +184,24 @@ def serving_shape(args, world):
 
 def summarize(recs, t0, t1, slo_ttft, slo_tpot):
     """SLO accounting of one window [t0, t1] (host clock).  ``recs``:
-    rid -> (arrival, token times, finished).  Returns (requests that finished
-    inside the window within both objectives, requests that finished inside
-    it, TTFT of requests whose first token came inside it, running TPOT of
-    requests that emitted tokens inside it, inter-token gaps that ended
-    inside it)."""
-    good, finished, ttft, tpot, gaps = 0, 0, [], [], 0
-    for arrival, times, fin in recs.values():
+    rid -> (arrival, token times, finished, output length).  Returns a dict:
+
+    * ``equiv``: SLO goodput in request-equivalents: every token a request
+      emitted inside the window counts 1/output-length of a request, when
+      the request met the TTFT objective and its mean inter-token time up to
+      the window's end meets the TPOT objective (a request that finishes
+      inside the window within both objectives thus counts in full over its
+      lifetime).  In steady state this equals the rate of requests finished
+      within the objectives, with far less sampling noise over a short
+      window, and it rises when steps get faster.
+    * ``good`` / ``finished``: requests that finished inside the window
+      within both objectives / at all;
+    * ``ttft``: TTFT of requests whose first token came inside the window;
+    * ``tpot``: running TPOT of requests with two or more tokens, emitting
+      inside the window;
+    * ``gaps``: inter-token gaps that ended inside the window."""
+    good, finished, ttft, tpot, gaps, equiv = 0, 0, [], [], 0, 0.0
+    for arrival, times, fin, out_len in recs.values():
         inside = [t for t in times if t <= t1]
         if not inside or inside[-1] < t0:
             continue
@@ -198,11 +212,13 @@ def summarize(recs, t0, t1, slo_ttft, slo_tpot):
         per_tok = (inside[-1] - first) / (len(inside) - 1) if len(inside) > 1 else 0.0
         if len(inside) > 1:
             tpot.append(per_tok)
+        ok = first - arrival <= slo_ttft and per_tok <= slo_tpot
+        if ok:
+            equiv += sum(1 for t in inside if t >= t0) / max(out_len, 1)
         if fin and len(inside) == len(times):
             finished += 1
-            if first - arrival <= slo_ttft and per_tok <= slo_tpot:
-                good += 1
-    return good, finished, ttft, tpot, gaps
+            good += int(ok)
+    return {"equiv": equiv, "good": good, "finished": finished, "ttft": ttft, "tpot": tpot, "gaps": gaps}
 
 
 class Job:
@@ -346,7 +362,7 @@ class Job:
                             prompt_range=tuple(a.prompt_range), output_range=tuple(a.output_range),
                             vocab=self.mc.get_vocab_size(), backlog=a.backlog * ninst)
         sp = lambda r: SamplingParams(temperature=0.0, max_tokens=r.output_len, ignore_eos=True)
-        recs = {}          # rid -> [arrival, token times, finished]
+        recs = {}          # rid -> [arrival, token times, finished, output length]
         tasks = []
 
         def on_out(outs):
@@ -370,7 +386,7 @@ class Job:
             recs[i][2] = True
 
         def submit(i, r, arrival):
-            recs[i] = [arrival, [], False]
+            recs[i] = [arrival, [], False, r.output_len]
             if via_api:
                 tasks.append(asyncio.create_task(api_one(i, r, arrival)))
             else:
@@ -482,7 +498,7 @@ class Job:
         spans = [(t - dt, t) for inst in self.instances for t, name, dt in inst.event_log
                  if name == "pmm_restore" and t >= t_drain]
         gaps_in, gaps_before = [], []
-        for _, times, _ in recs.values():
+        for _, times, _, _ in recs.values():
             for x, y in zip(times, times[1:]):
                 for r0, r1 in spans:
                     if r0 <= y <= r1:
@@ -502,13 +518,13 @@ class Job:
 
         win_s = win_ms / 1000.0
         t_end = t0 + (win_s if not via_api else (t1 - t0))
-        good, finished, ttft, tpot, gaps = summarize({k: tuple(v) for k, v in recs.items()}, t0, t_end,
-                                                     a.ttft_slo, a.tpot_slo)
+        sm = summarize({k: tuple(v) for k, v in recs.items()}, t0, t_end, a.ttft_slo, a.tpot_slo)
+        span = win_s if not via_api else (t1 - t0)
         dsteps = [y["steps"] - x["steps"] for x, y in zip(c0, c1)]
         return {
-            "label": label, "window_s": win_s, "host_window_s": t1 - t0, "good": good, "finished": finished,
-            "value": good / (win_s if not via_api else (t1 - t0)),
-            "ttft": ttft, "tpot": tpot, "tpot_samples": gaps,
+            "label": label, "window_s": win_s, "host_window_s": t1 - t0, "good": sm["good"],
+            "finished": sm["finished"], "value": sm["equiv"] / span, "finished_goodput": sm["good"] / span,
+            "ttft": sm["ttft"], "tpot": sm["tpot"], "tpot_samples": sm["gaps"],
             "running_at_start": running0, "queued_at_start": pending0, "kv_used_at_start": round(kv_used0, 3),
             "fill_steps": fill_steps, "preemptions": preempt1 - preempt0,
             "launches": sum(y["launches"] - x["launches"] for x, y in zip(c0, c1)),
@@ -694,7 +710,8 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
                    "policy": "mixed prefill+decode batches, recompute preemption"},
         "p99_ttft_s": round(pct(nat["ttft"], 99), 4), "p99_tpot_s": round(pct(nat["tpot"], 99), 5),
         "p50_ttft_s": round(pct(nat["ttft"], 50), 4), "p50_tpot_s": round(pct(nat["tpot"], 50), 5),
-        "finished": nat["finished"], "good": nat["good"], "window_s": round(nat["window_s"], 4),
+        "finished": nat["finished"], "good": nat["good"], "finished_goodput": round(nat["finished_goodput"], 4),
+        "window_s": round(nat["window_s"], 4),
         "running_at_start": nat["running_at_start"], "queued_at_start": nat["queued_at_start"],
         "kv_used_at_start": nat["kv_used_at_start"], "fill_steps": nat["fill_steps"],
         "preemptions": nat["preemptions"], "tpot_samples": nat["tpot_samples"],
@@ -706,7 +723,9 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
     }
     if base is not None:
         line["baseline"] = {"impl": "library baseline: ATen/cuBLAS GEMMs, NCCL all-reduce and NCCL KV/weight moves",
-                            "value": round(base["value"], 4), "ms_per_step": round(base["window_s"] * 1000.0 /
+                            "value": round(base["value"], 4),
+                            "finished_goodput": round(base["finished_goodput"], 4),
+                            "ms_per_step": round(base["window_s"] * 1000.0 /
                                                                                   args.steps, 3),
                             "p99_ttft_s": round(pct(base["ttft"], 99), 4),
                             "p99_tpot_s": round(pct(base["tpot"], 99), 5), "finished": base["finished"],
@@ -715,6 +734,7 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
                             "clocks": base["clocks"]}
     if e2e is not None:
         line["e2e"] = {"value": round(e2e["value"], 4), "unit": "req/s", "api": "AsyncLLM.generate",
+                       "finished_goodput": round(e2e["finished_goodput"], 4),
                        "p99_ttft_s": round(pct(e2e["ttft"], 99), 4), "p99_tpot_s": round(pct(e2e["tpot"], 99), 5),
                        "h2d_bytes_per_step": int(e2e["h2d_per_step"]), "d2h_bytes_per_step": int(e2e["d2h_per_step"]),
                        "window_s": round(e2e["host_window_s"], 4), "finished": e2e["finished"]}

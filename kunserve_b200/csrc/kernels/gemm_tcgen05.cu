@@ -24,6 +24,7 @@
 #include "gemm.h"
 #include "gemm_sched.cuh"
 #include <cudaTypedefs.h>
+#include <cstdlib>
 
 namespace kus {
 
@@ -658,6 +659,17 @@ size_t plan_workspace_floats(const GemmPlan& p) {
   return (size_t)p.args.sk_tiles * tile;
 }
 
+// Stream-K for the regular kernel when whole tiles leave SMs idle
+// (KUNSERVE_REGULAR_SK: 0 off, 1 on; read once).
+static bool regular_stream_k() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = std::getenv("KUNSERVE_REGULAR_SK");
+    on = (e && e[0] == '0') ? 0 : (e && e[0] == '1') ? 1 : 0;
+  }
+  return on == 1;
+}
+
 GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
   GemmPlan p{};
   p.epi = epi;
@@ -693,6 +705,21 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
       dp = tiles;
       sk = 0;
       grid = tiles < sms ? tiles : sms;
+    }
+  } else if (stream_k && !p.swap && regular_stream_k() && tiles % sms != 0 && tiles % sms < sms / 2 &&
+             num_kb >= 16) {
+    // regular kernel: the last wave is less than half full, so whole tiles
+    // leave most SMs idle at its end; that wave plus one full wave (if any)
+    // is spread over every SM along K, at least 8 k-blocks per CTA
+    const int waves = tiles / sms;
+    const int d = waves > 0 ? (waves - 1) * sms : 0;
+    const int s_t = tiles - d;
+    long long g = sms;
+    if ((long long)s_t * num_kb / g < 8) g = (long long)s_t * num_kb / 8;
+    if (g > s_t) {
+      dp = d;
+      sk = s_t;
+      grid = (int)g;
     }
   }
   p.args.M = M;

@@ -16,19 +16,22 @@ import bench  # noqa: E402
 def test_only_requests_finished_inside_the_window_count():
     t0, t1 = 100.0, 101.0
     recs = {
-        1: (99.0, [100.2, 100.25, 100.3], True),         # finished inside, good
-        2: (90.0, [96.0, 100.1, 100.3], True),            # finished inside, TTFT 6 s: bad
-        3: (99.9, [100.0, 100.5], True),                  # finished inside, TPOT 0.5 s: bad
-        4: (99.0, [99.5, 100.5, 100.6, 100.7], False),    # running: not finished, counted in TPOT
-        5: (99.0, [99.1, 99.2], True),                    # finished before the window: ignored
-        6: (100.5, [100.9, 101.5], True),                 # finishes after the window: not counted
-        7: (100.8, [], False),                            # queued: no token
+        1: (99.0, [100.2, 100.25, 100.3], True, 3),      # finished inside, good
+        2: (90.0, [96.0, 100.1, 100.3], True, 3),         # finished inside, TTFT 6 s: bad
+        3: (99.9, [100.0, 100.5], True, 2),               # finished inside, TPOT 0.5 s: bad
+        4: (99.0, [99.5, 99.55, 99.6, 100.5], False, 8),  # running, on track: 1 of 8 tokens inside
+        5: (99.0, [99.1, 99.2], True, 2),                 # finished before the window: ignored
+        6: (100.5, [100.9, 101.5], True, 4),              # first token inside, finishes after the window
+        7: (100.8, [], False, 4),                         # queued: no token
     }
-    good, finished, ttft, tpot, gaps = bench.summarize(recs, t0, t1, 2.0, 0.1)
+    sm = bench.summarize(recs, t0, t1, 2.0, 0.1)
+    good, finished, ttft, tpot, gaps = sm["good"], sm["finished"], sm["ttft"], sm["tpot"], sm["gaps"]
     assert (good, finished) == (1, 3)
+    # request-equivalents: 3/3 of request 1, 1/8 of request 4 (TPOT 0.33 s: bad), 1/4 of request 6
+    assert abs(sm["equiv"] - (1.0 + 0.25)) < 1e-9
     assert sorted(round(x, 3) for x in ttft) == [0.1, 0.4, 1.2]   # first tokens inside the window: 3, 6, 1
-    assert len(tpot) == 4                                      # requests 1-4 have two or more tokens inside
-    assert gaps == 2 + 2 + 1 + 3
+    assert len(tpot) == 4                                      # requests 1-4 have two or more tokens
+    assert gaps == 2 + 2 + 1 + 1
 
 
 def _run(cmd, timeout=900):
