@@ -223,6 +223,29 @@ class NativeRunner:
         self.restore_s = 0.0   # device seconds of parameter-restore pulls, and their bytes
         self.restore_bytes = 0.0
 
+    def _send_async(self, T: int, send_to) -> None:
+        """Hand this stage's activations to the next stage without holding up
+        the compute stream: copy them into a send buffer behind this step's
+        kernels, then send from a communication stream.  The compute stream
+        does not wait for the receiver, so this stage's next micro-batch
+        (another virtual engine's step) starts at once.  Finished sends are
+        released here; a bounded number stay in flight."""
+        if getattr(self, "_comm_stream", None) is None:
+            self._comm_stream = torch.cuda.Stream(self.device)
+            self._sends = []
+        self._sends = [(w, b) for w, b in self._sends if not w.is_completed()]
+        while len(self._sends) >= 4:           # bound the buffers in flight
+            w, _ = self._sends.pop(0)
+            w.wait()
+        cur = torch.cuda.current_stream(self.device)
+        buf = torch.empty((T, self.shape.hidden), dtype=torch.bfloat16, device=self.device)
+        buf.copy_(self.eng.hidden()[:T])
+        self._comm_stream.wait_stream(cur)
+        with torch.cuda.stream(self._comm_stream):
+            buf.record_stream(self._comm_stream)
+            work = self.comm.isend(buf, *send_to)
+        self._sends.append((work, buf))
+
     def set_library_mode(self, on: bool) -> None:
         """Switch between this library's kernels (fused TP collectives, P2P
         copies) and the comparison baseline: ATen/cuBLAS GEMMs, NCCL
@@ -313,7 +336,7 @@ class NativeRunner:
         if last_stage:
             self.d2h_bytes += 4 * B
         if send_to is not None:
-            self.comm.send(self.eng.hidden()[:T], *send_to)
+            self._send_async(T, send_to)
         if not last_stage:
             return None
         return list(out)

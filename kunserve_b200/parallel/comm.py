@@ -75,6 +75,11 @@ class Communicator:
     def send(self, x: torch.Tensor, comm: str, idx: int) -> None:
         dist.send(x.contiguous(), self.peer(comm, idx), group=self.groups[comm])
 
+    def isend(self, x: torch.Tensor, comm: str, idx: int):
+        """Start a point-to-point send; returns the work handle (the caller
+        keeps ``x`` alive until it completes)."""
+        return dist.isend(x, self.peer(comm, idx), group=self.groups[comm])
+
     def recv(self, shape, dtype, device, comm: str, idx: int) -> torch.Tensor:
         out = torch.empty(shape, dtype=dtype, device=device)
         dist.recv(out, self.peer(comm, idx), group=self.groups[comm])
