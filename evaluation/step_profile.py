@@ -7,6 +7,11 @@ events around ``--iters`` back-to-back steps after ``--warmup`` steps; the
 decode roofline is (weight bytes + KV bytes read) / measured HBM bandwidth.
 
     python evaluation/step_profile.py --model llama-3-8b --mode decode --batch 1 16 64 --ctx 512 2048
+    python evaluation/step_profile.py --model llama-2-13b --mode mixed --batch 114 --ctx 100 --lens 64 --prompts 8
+
+``--mode mixed`` is the serving benchmark's step shape: ``--batch`` decode
+requests at ``--ctx`` tokens plus ``--prompts`` prompts of ``--lens`` tokens
+prefilled in the same step.
 """
 import argparse
 import json
@@ -34,7 +39,8 @@ def main(argv=None):
 
     p = argparse.ArgumentParser()
     p.add_argument("--model", default="llama-3-8b")
-    p.add_argument("--mode", choices=["decode", "prefill"], default="decode")
+    p.add_argument("--mode", choices=["decode", "prefill", "mixed"], default="decode")
+    p.add_argument("--prompts", type=int, default=8, help="mixed: prompts prefilled with the decodes")
     p.add_argument("--batch", type=int, nargs="+", default=[1, 16, 64, 128])
     p.add_argument("--ctx", type=int, nargs="+", default=[512, 2048])
     p.add_argument("--lens", type=int, nargs="+", default=[512, 2048])
@@ -46,9 +52,15 @@ def main(argv=None):
     bs = a.block_size
     w = Worker(0, mc, CacheConfig(block_size=bs), ParallelConfig(), backend="native", device="cuda:0")
     span = max(a.ctx) + 1 if a.mode == "decode" else max(a.lens)
+    if a.mode == "mixed":
+        span = max(max(a.ctx) + 1, max(a.lens))
     pages_per = (span + bs - 1) // bs
     max_tok = max(a.batch) if a.mode == "decode" else max(b * n for b in a.batch for n in a.lens)
-    w.init_model(pages_per * max(a.batch), max_batch_tokens=max(max_tok, 256), max_batch_size=max(a.batch))
+    max_req = max(a.batch)
+    if a.mode == "mixed":
+        max_tok = max(a.batch) + a.prompts * max(a.lens)
+        max_req = max(a.batch) + a.prompts
+    w.init_model(pages_per * max_req, max_batch_tokens=max(max_tok, 256), max_batch_size=max_req)
     L = mc.get_num_layers()
     arch = mc.arch
     hd = arch.head_size
@@ -57,11 +69,16 @@ def main(argv=None):
                        + 3 * arch.hidden_size * arch.intermediate_size)
                   + arch.vocab_size * arch.hidden_size)
     bw, src = hbm_bytes_per_s()
-    cases = ([(B, c) for B in a.batch for c in a.ctx] if a.mode == "decode"
+    cases = ([(B, c) for B in a.batch for c in a.ctx] if a.mode in ("decode", "mixed")
              else [(B, n) for B in a.batch for n in a.lens])
     for B, n in cases:
         tables = [list(range(i * pages_per, (i + 1) * pages_per)) for i in range(B)]
-        if a.mode == "decode":
+        if a.mode == "mixed":
+            P, ln = a.prompts, max(a.lens)
+            tables += [list(range((B + j) * pages_per, (B + j + 1) * pages_per)) for j in range(P)]
+            step = StepInput(list(range(B + P)), [[1]] * B + [[1] * ln] * P, [n] * B + [0] * P, tables,
+                             [0] * B + [1] * P, 0, L, temperature=[0.0] * (B + P), seeds=[0] * (B + P))
+        elif a.mode == "decode":
             step = StepInput(list(range(B)), [[1]] * B, [n] * B, tables, [0] * B, 0, L,
                              temperature=[0.0] * B, seeds=[0] * B)
         else:
@@ -85,6 +102,8 @@ def main(argv=None):
             kv = B * (n + 1) * L * arch.num_key_value_heads * hd * 2 * 2
             roof = (wbytes + kv) / bw * 1e3
             row.update({"roofline_ms": round(roof, 3), "hbm_frac": round(roof / ms, 3), "peaks": src})
+        elif a.mode == "mixed":
+            row.update({"prompts": a.prompts, "prompt_len": max(a.lens), "tokens": B + a.prompts * max(a.lens)})
         else:
             row["tok_s"] = round(B * n / ms * 1e3, 1)
         print(json.dumps(row), flush=True)

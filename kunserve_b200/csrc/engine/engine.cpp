@@ -456,7 +456,8 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   int pend_parts = 0;     // split-K slots of down_proj still to be added to h (by the next norm)
   float* part = part_ws_.data_ptr<float>();
   bool y_ready = false;   // the fused all-reduce already produced this layer's normed input
-  // the push epilogue wins at decode sizes; NCCL's ring wins for large steps
+  // fused GEMM + push all-reduce for every step size (NCCL only in the
+  // library baseline, or past an experimental cap)
   const bool fused = tp && fused_ && !lib_ && T <= fused_max_tokens_;
   if (lib_) armed = true;   // the library baseline launches without PDL
   for (int64_t l = layer_start; l < layer_end; ++l) {

@@ -150,7 +150,7 @@ class Engine {
   std::vector<int64_t> rb_peers_;
   int tp_rank_ = 0;
   bool fused_ = false;
-  int64_t fused_max_tokens_ = 32;
+  int64_t fused_max_tokens_ = INT64_MAX;   // every step size uses the fused path
   unsigned epoch_ = 0;
   void tp_push_gemm(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, cudaStream_t s);
   void tp_reduce(__nv_bfloat16* h, const __nv_bfloat16* w, __nv_bfloat16* y, int T, cudaStream_t s);

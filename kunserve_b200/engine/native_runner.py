@@ -293,7 +293,11 @@ class NativeRunner:
         dist.barrier(group=group, device_ids=[dev])
         server.close()
         self.eng.set_tp_peers(bases)
-        self.eng.set_tp_fused_max_tokens(int(os.environ.get("KUNSERVE_TP_FUSED_MAX_TOKENS", "32")))
+        # the fused push + reduce is the TP path for every step size (measured
+        # ahead of GEMM + NCCL all-reduce at TP=2 from 1 to 16384 tokens at the
+        # serving level); the variable caps it for experiments
+        cap = os.environ.get("KUNSERVE_TP_FUSED_MAX_TOKENS")
+        self.eng.set_tp_fused_max_tokens(int(cap) if cap else self.shape.max_tokens)
 
     def load_weights(self, w) -> None:
         for l, lw in enumerate(w.layers):
