@@ -311,9 +311,10 @@ void Engine::gemm(const CUtensorMap* mA, const __nv_bfloat16* A, const WMap& mB,
 }
 
 int Engine::gemm_partials(const CUtensorMap* mA, const WMap& mB, int M, int N, int K, cudaStream_t st) {
-  if (!parts_ || lib_ || s_.tp > 1 || M > 128) return 0;
+  // decode steps (swapped kernel) and mid-size steps (regular kernel, whose
+  // whole tiles would leave SMs idle); the consumer sums the slots
+  if (!parts_ || lib_ || M > kMaxPartTokens) return 0;
   GemmPlan p = plan_gemm(M, N, K, EPI_F32, mB.has128 ? 0 : 256, false);
-  if (!p.swap) return 0;
   const long long stride = (long long)M * N;
   const int max_slots = (int)std::min<long long>(kMaxPartSlots, part_ws_.numel() / stride);
   const int S = plan_split_partials(p, max_slots, stride);

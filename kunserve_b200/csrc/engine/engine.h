@@ -165,6 +165,7 @@ class Engine {
   torch::Tensor err_host_;   // pinned copy of the device error code, read with every step's ids
   void fail_on_device_error();
   static constexpr int kMaxPartSlots = 16;
+  static constexpr int kMaxPartTokens = 1024;   // largest step that may split a GEMM into partial slots
   torch::Tensor part_ws_;
   // Decode-sized GEMM as split-K fp32 partial slots in part_ws_ (slot s at
   // s * M * N); returns the slot count, or 0 when the plan does not split

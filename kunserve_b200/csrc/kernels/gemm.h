@@ -56,7 +56,7 @@ struct GemmArgs {
   __nv_bfloat16* ag_gather;
   const __nv_bfloat16* ag_src[kMaxTpPeers];
   int* ag_ready;
-  // Split-K with partials (swapped kernel, EPI_F32): with part_splits = S > 0
+  // Split-K with partials (EPI_F32): with part_splits = S > 0
   // the K loop is cut into S ranges of part_kbs k-blocks; split s of every
   // tile writes its fp32 partial to out + s * part_stride (plain stores, no
   // reduction).  The consumer of the result sums the S slots.
@@ -91,9 +91,11 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn = 0, bool stream_k = tru
 // fp32 workspace floats and counters a plan needs (workspace all zero).
 size_t plan_workspace_floats(const GemmPlan& p);
 inline int plan_counters(const GemmPlan& p) { return p.args.sk_tiles; }
-// Turn a swapped fp32 plan into split-K with partial slots (at most
-// max_splits, at least 4 k-blocks each, about one unit per SM); returns the
-// number of slots (1 when splitting does not pay: the plan is unchanged).
+// Turn an fp32 plan into split-K with partial slots (at most max_splits;
+// swapped plans: at least 4 k-blocks each, about one unit per SM; regular
+// plans: 128 x 256 tiles, at least 8 k-blocks each, used when the tiles do
+// not fill the GPU); returns the number of slots (1 when splitting does not
+// pay: the plan is unchanged).
 int plan_split_partials(GemmPlan& p, int max_splits, long long part_stride);
 // Bind operands.  a_rows / b_rows override the rows declared to TMA (0: M / N).
 bool finalize_plan(GemmPlan& p, const void* A, int lda, const void* B, int ldb, void* out, int ldc,

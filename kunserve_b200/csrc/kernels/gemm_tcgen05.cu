@@ -123,10 +123,11 @@ KUS_DEVICE void store16(const GemmArgs& a, int row, int col, const float (&v)[16
 // Eight consecutive output columns (col..col+7) of one row, staged in
 // shared memory by the tile epilogue; 16-byte loads and stores.
 template <int EPI>
-KUS_DEVICE void out8(const GemmArgs& a, int row, int col, float (&x)[8]) {
+KUS_DEVICE void out8(const GemmArgs& a, int row, int col, float (&x)[8], int slot = 0) {
   const bool full = col + 8 <= a.n_out;
   if (EPI == EPI_F32) {
-    float* dst = reinterpret_cast<float*>(a.out) + (size_t)row * a.ldc + col;
+    // slot: split-K partial slot (0 without a split)
+    float* dst = reinterpret_cast<float*>(a.out) + (size_t)slot * a.part_stride + (size_t)row * a.ldc + col;
     if (full) {
       *reinterpret_cast<float4*>(dst) = make_float4(x[0], x[1], x[2], x[3]);
       *reinterpret_cast<float4*>(dst + 4) = make_float4(x[4], x[5], x[6], x[7]);
@@ -480,7 +481,9 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
       const int col0 = n * kOutCols;
-      if (kb0 == 0 && kb1 == num_kb) {
+      if (args.part_splits > 0 || (kb0 == 0 && kb1 == num_kb)) {
+        // a whole tile, or one split's fp32 partial into its own slot
+        const int slot = args.part_splits > 0 ? kb0 / args.part_kbs : 0;
         // 64 output columns per pass: TMEM -> registers -> E[row][col] (one
         // row per thread), then each warp writes 4 rows x 128 contiguous
         // bytes (bf16) per instruction.  The barriers run whether or not the wait
@@ -514,7 +517,7 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
               float x[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) x[e] = epi[rr * C::kEpiStride + cc + e];
-              out8<EPI>(args, grow, gcol, x);
+              out8<EPI>(args, grow, gcol, x, slot);
             }
           }
           named_barrier(2, 128);
@@ -736,12 +739,17 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
 }
 
 int plan_split_partials(GemmPlan& p, int max_splits, long long part_stride) {
-  if (!p.swap || p.epi != EPI_F32) return 1;
+  if (p.epi != EPI_F32) return 1;
   const int sms = num_sms();
-  const int tiles = p.args.m_tiles * p.args.n_tiles;
+  // regular kernel: 128 x 256 tiles (the better operand feed per SM), cut
+  // along K when they do not fill the GPU, at least 8 k-blocks per split;
+  // swapped kernel: its 256-row weight tiles, at least 4 k-blocks per split
+  const int min_kbs = p.swap ? 4 : 8;
+  const int n_tiles = p.swap ? p.args.n_tiles : (p.args.N + 255) / 256;
+  const int tiles = p.args.m_tiles * n_tiles;
   int S = sms / tiles;
   if (S > max_splits) S = max_splits;
-  if (S > p.args.num_kb / 4) S = p.args.num_kb / 4;
+  if (S > p.args.num_kb / min_kbs) S = p.args.num_kb / min_kbs;
   if (S < 2) return 1;
   int kbs = (p.args.num_kb + S - 1) / S;
   while (S > 1 && (S - 1) * kbs >= p.args.num_kb) {   // every split owns k-blocks
@@ -749,6 +757,10 @@ int plan_split_partials(GemmPlan& p, int max_splits, long long part_stride) {
     kbs = (p.args.num_kb + S - 1) / S;
   }
   if (S < 2) return 1;
+  if (!p.swap) {
+    p.bn = 256;
+    p.args.n_tiles = n_tiles;
+  }
   p.args.part_splits = S;
   p.args.part_kbs = kbs;
   p.args.part_stride = part_stride;
