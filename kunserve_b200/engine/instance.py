@@ -217,6 +217,16 @@ class InstanceEngine(AdmissionMixin):
         self.stopped = True
         while any(self.scheduler_running):
             await asyncio.sleep(0)
+        self.release_finished()
+
+    def release_finished(self) -> None:
+        """Free the pages of requests that finished in the last step before a
+        stop (the step's batch preparation, which normally frees them, is
+        skipped once the engine is stopped), so a transition starts from
+        exact page accounting."""
+        for s in self.scheduler:
+            for r in s.pop_finished_requests():
+                self._free_blocks(r)
 
     def set_engine_stopped(self, stopped: bool) -> None:
         self.stopped = stopped
