@@ -5,8 +5,9 @@
   projections (o_proj: K = H/tp; down_proj: K = F/tp) at M tokens;
 * fused GEMM + reduce-scatter (each output row block pushed only to its
   owner) against cuBLAS GEMM + NCCL reduce-scatter, same shapes;
-* fused all-gather + GEMM (the A shards of every rank read by TMA inside the
-  GEMM from the owning GPU) against NCCL all-gather + cuBLAS GEMM, for the
+* fused all-gather + GEMM (gather warps inside the GEMM copy the other
+  ranks' A shards with plain peer loads into a local buffer, once; TMA reads
+  only this GPU's memory) against NCCL all-gather + cuBLAS GEMM, for the
   column-parallel projections (qkv: N = (H + 2 kv)/tp ~ H/tp here; gate/up:
   N = 2F/tp) with K = H;
 * paged KV-block migration (blocks of 16 tokens x 8 KV heads x 128 dim, K and
