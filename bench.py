@@ -412,12 +412,20 @@ class Job:
                 raise RuntimeError("the backlog did not load the instances (KV >= 95 % and a queue): "
                                    f"(instance, used, capacity, pending, steps) = {state}")
             await asyncio.sleep(0.001)
+        # the W warm steps right before the window also time the
+        # tensor-parallel collectives (CUDA events around them, on every GPU)
+        await self.call_all("set_profile", True)
         s_w = await self.gpu0_steps()
         while await self.gpu0_steps() - s_w < a.warmup:
             self._check()
             await asyncio.sleep(0.0005)
         fill_steps = await self.gpu0_steps() - s_fill
         await self.pause()
+        prof = await self.call_all("profile")
+        await self.call_all("set_profile", False)
+        coll = sum(p[0] for p in prof)
+        tot = sum(p[1] for p in prof)
+        coll_share = round(coll / tot, 4) if tot > 0 else None
         running0 = sum(len(s.running_queue) for inst in self.live() for s in inst.scheduler)
         pending0 = sum(inst.check_pending_num() for inst in self.live())
         kv_used0 = min(inst.get_used_gpu_blocks() / max(inst.get_capacity_units(), 1) for inst in self.live())
@@ -543,7 +551,7 @@ class Job:
                                "tbt_p50_before_s": round(pct(gaps_before, 50), 4),
                                "tbt_p99_before_s": round(pct(gaps_before, 99), 4),
                                "gaps_during": len(gaps_in)} if restore_dev else None,
-            "clocks": clock_info, "host_profile": host_profile,
+            "clocks": clock_info, "host_profile": host_profile, "tp_collective_share": coll_share,
         }
 
     async def _elapsed(self, w):
@@ -720,6 +728,10 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
         "restore_device": nat["restore_device"], "drain_s": nat["drain_s"],
         "gpu_launches": int(nat["launches"]), "forward_busy_frac": round(nat["fwd_busy"], 3),
         "clocks": nat["clocks"], "host_profile": nat["host_profile"],
+        # device-time share of the W warm steps before the window spent in
+        # the tensor-parallel collective (fused push GEMM + reduce; NCCL
+        # all-reduce in the baseline), all GPUs
+        "tp_collective_share": nat["tp_collective_share"],
     }
     if base is not None:
         line["baseline"] = {"impl": "library baseline: ATen/cuBLAS GEMMs, NCCL all-reduce and NCCL KV/weight moves",
@@ -731,7 +743,7 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
                             "p99_tpot_s": round(pct(base["tpot"], 99), 5), "finished": base["finished"],
                             "preemptions": base["preemptions"], "transitions_in_window":
                             base["transitions_in_window"], "restore_gbps": base["restore_gbps"],
-                            "clocks": base["clocks"]}
+                            "tp_collective_share": base["tp_collective_share"], "clocks": base["clocks"]}
     if e2e is not None:
         line["e2e"] = {"value": round(e2e["value"], 4), "unit": "req/s", "api": "AsyncLLM.generate",
                        "finished_goodput": round(e2e["finished_goodput"], 4),

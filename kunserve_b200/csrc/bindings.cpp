@@ -389,6 +389,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("set_library_mode", &Engine::set_library_mode,
            "GEMMs through ATen/cuBLAS with unfused epilogues and NCCL all-reduce (the comparison baseline)")
       .def("library_mode", &Engine::library_mode)
+      .def("set_profile", &Engine::set_profile)
+      .def("profile", &Engine::profile, "[collective ms, step ms, steps] since set_profile(True)")
       .def("launches", &Engine::launches)
       .def("reset_launches", &Engine::reset_launches);
   py::class_<SharedBuffer>(m, "SharedBuffer")

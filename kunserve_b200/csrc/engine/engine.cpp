@@ -127,6 +127,36 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
 
 Engine::~Engine() {
   if (tp_comm_) ncclCommDestroy(tp_comm_);
+  for (cudaEvent_t e : prof_ev_) cudaEventDestroy(e);
+}
+
+void Engine::set_profile(bool on) {
+  prof_ = on;
+  prof_coll_ms_ = prof_total_ms_ = 0.0;
+  prof_steps_ = 0;
+}
+
+void Engine::prof_mark(cudaStream_t st) {
+  if ((int)prof_ev_.size() <= prof_used_) {
+    cudaEvent_t e;
+    check_cuda(cudaEventCreate(&e), "profile event");
+    prof_ev_.push_back(e);
+  }
+  check_cuda(cudaEventRecord(prof_ev_[prof_used_++], st), "profile event record");
+}
+
+void Engine::prof_collect() {
+  if (prof_used_ >= 2) {
+    float ms = 0.f;
+    check_cuda(cudaEventElapsedTime(&ms, prof_ev_[0], prof_ev_[1]), "profile step time");
+    prof_total_ms_ += ms;
+    for (int i = 2; i + 1 < prof_used_; i += 2) {
+      check_cuda(cudaEventElapsedTime(&ms, prof_ev_[i], prof_ev_[i + 1]), "profile collective time");
+      prof_coll_ms_ += ms;
+    }
+    ++prof_steps_;
+  }
+  prof_used_ = 0;
 }
 
 int64_t Engine::layer_slot_bytes() const { return 2LL * s_.block_size * s_.nkv * s_.hd * 2; }
@@ -378,6 +408,12 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   const int64_t n_meta = 2 * n_items + 4 * T + 3 * B + 1 + B * max_pages + 4 * B + n_dec + kDecUnitInts * n_units;
   KUS_CHECK(meta.numel() >= n_meta && n_meta <= meta_dev_.numel(), "meta buffer too small");
   check_cuda(cudaMemcpyAsync(meta_dev_.data_ptr(), meta.data_ptr(), n_meta * 4, cudaMemcpyHostToDevice, st), "meta H2D");
+  const bool prof = prof_;
+  prof_used_ = 0;
+  if (prof) {
+    prof_mark(st);   // [0]: step start
+    prof_mark(st);   // [1]: step end, re-recorded at the end
+  }
   // meta layout (int32): items[2n] | tokens[T] | positions[T] | kv_page[T] | kv_slot[T] |
   // q_start[B+1] | ctx_len[B] | last_idx[B] | page_table[B*max_pages] | temps[B] (f32) | seeds[B] |
   // top_k[B] | top_p[B] (f32) |
@@ -486,12 +522,16 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     if (sync_debug_) debug_check("attention", (int)T, (int)B, (int)n_dec, st);
     launches_ += 2 + (n_items > 0 ? 1 + (splits > 1 ? 1 : 0) : 0) + (n_units > 0 ? 1 : 0);
     if (fused) {
+      if (prof) prof_mark(st);
       tp_push_gemm(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, st);
       tp_reduce(h, W.post_norm, y, (int)T, st);
+      if (prof) prof_mark(st);
     } else if (tp) {
+      if (prof) prof_mark(st);
       gemm(m_attn_, attn, W.m_o, (int)T, H, s_.nq * s_.hd, EPI_BF16, tmp, H, nullptr, st);
       all_reduce(tmp, T * H, st);
       rmsnorm(h, tmp, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st);
+      if (prof) prof_mark(st);
     } else if ((np = gemm_partials(m_attn_, W.m_o, (int)T, H, s_.nq * s_.hd, st)) > 0) {
       // residual add of the partial slots fused into the post-attention norm
       rmsnorm(h, nullptr, W.post_norm, y, nullptr, (int)T, H, (float)s_.eps, st, part, np, (long long)T * H);
@@ -502,14 +542,18 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     ++launches_;
     gemm(m_y_, y, W.m_gu, (int)T, 2 * f_pad_, H, EPI_SILU, act, f_pad_, nullptr, st);
     if (fused) {
+      if (prof) prof_mark(st);
       tp_push_gemm(m_act_, W.m_down, (int)T, H, f_pad_, st);
       const bool next = l + 1 < layer_end;
       tp_reduce(h, next ? layers_[l + 1].in_norm : nullptr, y, (int)T, st);
+      if (prof) prof_mark(st);
       y_ready = next;
       pending = false;
     } else if (tp) {
+      if (prof) prof_mark(st);
       gemm(m_act_, act, W.m_down, (int)T, H, f_pad_, EPI_BF16, tmp, H, nullptr, st);
       all_reduce(tmp, T * H, st);
+      if (prof) prof_mark(st);
       pending = true;
     } else {
       // partial slots are added by the next norm; a stage that hands h to
@@ -525,7 +569,14 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
     ++launches_;
   }
   std::vector<int64_t> out;
-  if (!last_stage) return out;
+  if (!last_stage) {
+    if (prof) {
+      check_cuda(cudaEventRecord(prof_ev_[1], st), "profile step end");
+      check_cuda(cudaStreamSynchronize(st), "profile sync");
+      prof_collect();
+    }
+    return out;
+  }
   auto* yl = reinterpret_cast<__nv_bfloat16*>(ylast_.data_ptr());
   rmsnorm(h, nullptr, reinterpret_cast<const __nv_bfloat16*>(final_norm_.data_ptr()), yl, last_idx, (int)B, H,
           (float)s_.eps, st, pend_parts ? part : nullptr, pend_parts, (long long)T * H);
@@ -543,7 +594,9 @@ std::vector<int64_t> Engine::forward(torch::Tensor meta, int64_t T, int64_t B, i
   check_cuda(cudaMemcpyAsync(tokens_host_.data_ptr(), tokens_dev_.data_ptr(), B * 4, cudaMemcpyDeviceToHost, st),
              "tokens D2H");
   read_error_async(err_host_.data_ptr<int>(), st);
+  if (prof) check_cuda(cudaEventRecord(prof_ev_[1], st), "profile step end");
   check_cuda(cudaStreamSynchronize(st), "step sync");
+  if (prof) prof_collect();
   fail_on_device_error();
   const int* th = tokens_host_.data_ptr<int>();
   out.assign(th, th + B);

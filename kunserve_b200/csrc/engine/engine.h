@@ -116,6 +116,14 @@ class Engine {
   void set_library_mode(bool on) { lib_ = on; }
   bool library_mode() const { return lib_; }
 
+  // Collective profiling: with it on, every step records CUDA events around
+  // its tensor-parallel collectives (the fused push GEMM + reduce, or GEMM +
+  // NCCL all-reduce + norm in the library path) and around the whole step,
+  // and accumulates both device times (read with profile()).  Off by
+  // default: the events cost host time on every layer.
+  void set_profile(bool on);
+  std::vector<double> profile() const { return {prof_coll_ms_, prof_total_ms_, (double)prof_steps_}; }
+
  private:
   void build_layer_maps(int l);
   void gemm(const CUtensorMap* mA, const __nv_bfloat16* A, const WMap& mB, int M, int N, int K, int epi, void* out,
@@ -123,6 +131,13 @@ class Engine {
   void lib_gemm(const __nv_bfloat16* A, const WMap& mB, int M, int N, int K, int epi, void* out, int ldc,
                 const __nv_bfloat16* res);
   bool lib_ = false;
+  bool prof_ = false;
+  double prof_coll_ms_ = 0.0, prof_total_ms_ = 0.0;
+  int64_t prof_steps_ = 0;
+  std::vector<cudaEvent_t> prof_ev_;   // pool: [0, 1] step, then pairs per collective
+  int prof_used_ = 0;
+  void prof_mark(cudaStream_t st);     // records the next event of the pool
+  void prof_collect();                 // after the step's sync: sums the pairs
   torch::Tensor lib_gu_;   // [max_tokens, 2F] gate/up GEMM output of the library baseline
   void all_reduce(__nv_bfloat16* buf, int64_t n, cudaStream_t s);
 

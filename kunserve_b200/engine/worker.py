@@ -396,6 +396,18 @@ class Worker:
         self.runner.set_library_mode(on)
         return True
 
+    def set_profile(self, on: bool) -> None:
+        """Native runner: time the tensor-parallel collectives of every step
+        with CUDA events (see ``Engine::set_profile``)."""
+        if self.backend == "native":
+            self.runner.eng.set_profile(bool(on))
+
+    def profile(self) -> List[float]:
+        """[collective ms, step ms, steps] since profiling was switched on."""
+        if self.backend != "native":
+            return [0.0, 0.0, 0.0]
+        return [float(x) for x in self.runner.eng.profile()]
+
     def mark(self, tag: str) -> None:
         """Record a CUDA event named ``tag`` on this worker's stream (after
         every step issued so far)."""
