@@ -92,6 +92,10 @@ class InstanceEngine(AdmissionMixin):
         self.is_reclaiming_ex_blocks = False
         self.allocate_lock = asyncio.Lock()
         self.p2p_kv = False         # KV moves as in-kernel pulls over mapped peer memory
+        # micro-batches per virtual-engine step in the fused pipeline
+        # (KUNSERVE_PIPE_MICROBATCHES; 1: the reference's one batch per VE)
+        import os
+        self.pipe_microbatches = max(1, int(os.environ.get("KUNSERVE_PIPE_MICROBATCHES", "1")))
         # host seconds by phase (scheduling between steps, building step
         # inputs, waiting for the workers' forward), for profiling the loop
         self.host_time = {"schedule": 0.0, "build": 0.0, "forward": 0.0, "post": 0.0}
@@ -316,7 +320,16 @@ class InstanceEngine(AdmissionMixin):
             batch.set_sched_time()
             pipe, replica = batch.get_fusion_requests()
             if pipe:
-                await self._step_inner(ve, pipe, fusion_exec=True)
+                k = self.pipe_microbatches
+                if k > 1 and self.num_instances > 1 and len(pipe) >= 2 * k:
+                    # several micro-batches of this VE in flight at once, so a
+                    # stage computes the next one while the later stages work
+                    # on this one (disjoint requests: no token depends on
+                    # another micro-batch of the same step)
+                    parts = [pipe[i::k] for i in range(k)]
+                    await asyncio.gather(*[self._step_inner(ve, p, fusion_exec=True) for p in parts if p])
+                else:
+                    await self._step_inner(ve, pipe, fusion_exec=True)
             if resharding:
                 await self._reshard_blocks_batched(resharding)
             if not self.is_fusion_state and replica:
