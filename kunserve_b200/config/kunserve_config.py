@@ -93,6 +93,8 @@ class BalloonConfig:
     max_balloon_memory_ratio: float = 0.5
     max_restore_memory_ratio: float = 0.8
     restore_memory_threshold: float = 0.5
+    # cross-group transfer of running requests between unfused instances
+    enable_transfer: bool = False
 
     @classmethod
     def from_cli_args(cls, ns) -> "BalloonConfig":
@@ -109,6 +111,9 @@ class BalloonConfig:
         p.add_argument("--max-restore-memory-ratio", type=float, default=0.8)
         p.add_argument("--restore-memory-threshold", type=float, default=0.5)
         p.add_argument("--restore-batch-size", type=int, default=8)
+        p.add_argument("--enable-transfer", action="store_true", default=False,
+                       help="move running requests (with their KV) from an overloaded instance to one of "
+                            "another group")
         return p
 
     @property

@@ -879,6 +879,57 @@ class InstanceEngine(AdmissionMixin):
             r.fusion_exec = False
             r.kv_fusion_rank = home
 
+    # ------------------------------------------------- cross-group transfer
+    def pop_transferable(self, max_pages: int) -> List[Tuple[Request, List[int]]]:
+        """Running decode requests to hand to an instance of another group,
+        latest first, up to ``max_pages`` pages: they leave this instance's
+        running queues with their pages still allocated (the instance must be
+        stopped and unfused)."""
+        assert self.num_instances == 1 and not self.is_fusion_state
+        bm = self.block_managers[0]
+        out, used = [], 0
+        for s in self.scheduler:
+            for r in list(reversed(s.running_queue.requests)):
+                if r.fusion_exec or r.is_context_stage() or r.is_finished or not bm.is_allocated(r.request_id):
+                    continue
+                pages = list(bm.get_single_block_table(r.request_id))
+                if used + len(pages) > max_pages:
+                    continue
+                s.running_queue.requests.remove(r)
+                out.append((r, pages))
+                used += len(pages)
+        return out
+
+    def take_pages_for(self, items: Sequence[Tuple[Request, List[int]]]):
+        """Free pages of this pool for transferred requests, in order, until
+        one does not fit: ``[(request, source pages, destination pages)]``."""
+        bm = self.block_managers[0]
+        out = []
+        for r, pages in items:
+            got = bm.get_free_gpu_blocks(len(pages))
+            if not got:
+                break
+            out.append((r, pages, got))
+        return out
+
+    def adopt_transferred(self, moved) -> None:
+        """Requests whose KV now sits in this pool join the least loaded VE."""
+        bm = self.block_managers[0]
+        for r, _, dst in moved:
+            bm.attach_blocks(r.request_id, dst)
+            r.fusion_exec = False
+            r.kv_fusion_rank = 0
+            s = min(self.scheduler, key=lambda x: len(x.running_queue))
+            s.running_queue.requests.append(r)
+            s.next_batch_prepared = False
+
+    def return_transferable(self, items) -> None:
+        """Requests that did not move go back to a running queue here."""
+        for r, _ in items:
+            s = min(self.scheduler, key=lambda x: len(x.running_queue))
+            s.running_queue.requests.append(r)
+            s.next_batch_prepared = False
+
     def trigger_init(self) -> None:
         self.num_instances = 1
         self.state = "initial"

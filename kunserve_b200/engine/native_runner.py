@@ -213,6 +213,7 @@ class NativeRunner:
         self.gpu_ms = 0.0      # device time inside forward(), summed over steps
         self._ev = None
         self.peer_maps = {}
+        self.global_maps = {}  # instance id -> PeerMemory (cross-group page transfer)
         # KV and weight movement pulls over NVLink when peers are mapped;
         # the library baseline moves them with NCCL instead
         self.use_p2p = True
@@ -356,17 +357,54 @@ class NativeRunner:
         self._fd_server = FdServer(fds)
         return {"sock": self._fd_server.path, "sizes": sizes}
 
-    def import_peers(self, infos: dict) -> int:
-        """Map every group member's memory (``infos[member]`` from its
-        ``export_memory``); afterwards KV and weight movement pulls over NVLink."""
+    def import_peers(self, infos: dict, scope: str = "group") -> int:
+        """Map peers' memory (``infos[key]`` from their ``export_memory``):
+        ``scope="group"`` keys are balloon-group member indices (KV reshard,
+        restore, live restore); ``"global"`` keys are instance ids of the
+        whole server (cross-group page transfer).  Afterwards those moves
+        pull over NVLink inside the copy kernel."""
         from ..parallel.peer import PeerMemory, fetch_fds
         dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
-        for member, info in infos.items():
-            self.peer_maps[int(member)] = PeerMemory(self.C, dev, fetch_fds(info["sock"]), info["sizes"])
-        return len(self.peer_maps)
+        maps = self.peer_maps if scope == "group" else self.global_maps
+        for key, info in infos.items():
+            maps[int(key)] = PeerMemory(self.C, dev, fetch_fds(info["sock"]), info["sizes"])
+        return len(maps)
+
+    # ---------------------------------------------- cross-group page transfer
+    def pull_pages(self, src_instance: int, src_offs: List[int], dst_offs: List[int], chunk: int) -> bool:
+        """Copy pages of another instance's pool (mapped with scope "global")
+        into this pool over NVLink; False when that instance is not mapped
+        (the caller then uses the NCCL pair send_chunks / recv_chunks)."""
+        peer = self.global_maps.get(int(src_instance))
+        if peer is None or not self.use_p2p or not dst_offs:
+            return peer is not None and self.use_p2p
+        self._pull(self.eng.kv_base_ptr(), self.pool_extent(), peer.kv, peer.kv_bytes, dst_offs, src_offs, chunk)
+        torch.cuda.synchronize(self.device)
+        return True
+
+    def send_chunks(self, comm: str, idx: int, offs: List[int], chunk: int) -> None:
+        """NCCL path: gather ``chunk``-byte pieces of the pool into one buffer
+        (copy kernel) and send it to peer ``idx`` of ``comm``."""
+        if not offs:
+            return
+        buf = torch.empty(len(offs) * chunk, dtype=torch.uint8, device=self.device)
+        self._pull(buf.data_ptr(), buf.numel(), self.eng.kv_base_ptr(), self.pool_extent(),
+                   [i * chunk for i in range(len(offs))], list(offs), chunk)
+        self.comm.send(buf, comm, idx)
+        torch.cuda.synchronize(self.device)
+
+    def recv_chunks(self, comm: str, idx: int, offs: List[int], chunk: int) -> None:
+        """NCCL path: receive pieces from peer ``idx`` of ``comm`` and scatter
+        them to ``offs`` of the pool (copy kernel)."""
+        if not offs:
+            return
+        buf = self.comm.recv((len(offs) * chunk,), torch.uint8, self.device, comm, idx)
+        self._scatter(buf, list(offs), chunk)
+        torch.cuda.synchronize(self.device)
 
     def close_peer_memory(self) -> None:
         self.peer_maps.clear()
+        self.global_maps.clear()
         if getattr(self, "_fd_server", None) is not None:
             self._fd_server.close()
             self._fd_server = None

@@ -150,8 +150,19 @@ class Worker:
         """Share this worker's KV pool and weight segments with group peers."""
         return self.runner.export_memory() if self.backend == "native" else {}
 
-    def import_peers(self, infos: dict) -> int:
-        return self.runner.import_peers(infos) if self.backend == "native" else 0
+    def import_peers(self, infos: dict, scope: str = "group") -> int:
+        return self.runner.import_peers(infos, scope) if self.backend == "native" else 0
+
+    def pull_blocks(self, src_instance: int, src_pages: Sequence[int], dst_pages: Sequence[int]) -> bool:
+        """Cross-group transfer of whole pages from another instance's pool
+        (reference N8, ``worker.py:825-855``) over NVLink; False when there
+        is no mapping to pull from (the caller pairs send/recv_blocks)."""
+        if self.backend != "native":
+            return False
+        cb = copy_plan.chunk_bytes(self.layout, 1)
+        src = [copy_plan.slice_offset(self.layout, p, 1) for p in src_pages]
+        dst = [copy_plan.slice_offset(self.layout, p, 1) for p in dst_pages]
+        return self.runner.pull_pages(src_instance, src, dst, cb)
 
     def clear_request_resource_batched(self, requests) -> None:
         """The engine keeps no per-request state outside the KV pool."""

@@ -47,7 +47,9 @@ class AsyncLLM:
         self.server_id = server_id
         self.tokenizer = tokenizer
         self.coordinator = Coordinator(groups, cfg.dispatch_config.dispatch_strategy,
-                                       cfg.balloon_config.enable_balloon)
+                                       cfg.balloon_config.enable_balloon,
+                                       enable_transfer=cfg.balloon_config.enable_transfer,
+                                       transfer_low=cfg.balloon_config.restore_memory_threshold)
         self._ids = itertools.count()
         self._tasks: List[asyncio.Task] = []
         self._epoch_t = time.time()
@@ -75,6 +77,8 @@ class AsyncLLM:
             if os.environ.get("KUNSERVE_P2P", "1") != "0":
                 await g.setup_peer_memory()
         llm = cls(cfg, mc, groups, router, server_id, tokenizer)
+        if cfg.balloon_config.enable_transfer and os.environ.get("KUNSERVE_P2P", "1") != "0":
+            await llm.coordinator.setup_global_peer_memory()
         llm.start()
         return llm
 

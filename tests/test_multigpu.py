@@ -174,3 +174,79 @@ def test_fused_reduce_scatter_and_allgather_gemm_two_gpus():
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
     assert any("reduce_scatter" in ln for ln in lines) and any("allgather" in ln for ln in lines), r.stdout[-2000:]
+
+
+async def _transfer_native(p2p: bool):
+    import os
+    from kunserve_b200.llm import AsyncLLM
+    from kunserve_b200.runtime import aw
+    os.environ["KUNSERVE_P2P"] = "1" if p2p else "0"
+    cfg = KunServeConfig()
+    e = cfg.engine_config
+    e.ngroups, e.group_size, e.block_size = 2, 1, 16
+    e.enable_chunked_prefill, e.chunked_prefill_budget = True, 512
+    e.max_batch_tokens = 1024
+    cfg.balloon_config.enable_transfer = True
+    from kunserve_b200.runtime import get
+    mc = ModelConfig("tiny-llama-128", dtype="bf16")
+    llm = await AsyncLLM.create(cfg, model_config=mc, backend="native", actor_kind="process",
+                                devices=["cuda:0", "cuda:1"], num_gpu_blocks=96, seed=3)
+    try:
+        # every request lands on group 0's instance; the test moves some
+        llm.coordinator.get_next_assign = lambda: (0, 0)
+        llm.coordinator.enable_transfer = False
+        assert llm.coordinator.global_p2p == p2p
+        src, dst = llm.groups[0].instances[0], llm.groups[1].instances[0]
+        sp = lambda n: SamplingParams(temperature=0.0, max_tokens=n, ignore_eos=True)
+        tasks = [asyncio.create_task(llm.generate(prompt_token_ids=list(range(3 + i, 40 + 7 * i)),
+                                                  sampling_params=sp(60), request_id=i)) for i in range(8)]
+        loop = asyncio.get_running_loop()
+        t0 = loop.time()
+        while sum(len(s.running_queue.get_decode_requests()) for s in src.scheduler) < 6:
+            assert loop.time() - t0 < 120
+            await asyncio.sleep(0.01)
+        # KV bytes of every running request before the move (source pool)
+        await src.stop_and_wait()
+        ws, wd = src.workers[0][0], dst.workers[0][0]
+        bm = src.block_managers[0]
+        before = {}
+        for s in src.scheduler:
+            for r in s.running_queue.get_decode_requests():
+                n_ctx = r.get_input_len() + r.get_output_len() - 1
+                pages = list(bm.get_single_block_table(r.request_id))
+                before[r.request_id] = (n_ctx, [await aw(ws.read_kv.remote(p, l, 1)) for p in pages for l in range(2)])
+        src.stopped = False
+        moved = await llm.coordinator.transfer_requests(src, dst, 1000)
+        assert moved > 0
+        await dst.stop_and_wait()
+        checked = 0
+        for s in dst.scheduler:
+            for r in s.running_queue.requests:
+                if r.request_id not in before:
+                    continue
+                n_ctx, kv = before[r.request_id]
+                pages = list(dst.block_managers[0].get_single_block_table(r.request_id))
+                got = [await aw(wd.read_kv.remote(p, l, 1)) for p in pages for l in range(2)]
+                per_tok = kv[0].numel() // 16
+                for k in range(len(pages)):
+                    n = max(0, min(16, n_ctx - 16 * k)) * per_tok
+                    for l in range(2):
+                        assert torch.equal(got[2 * k + l][:n], kv[2 * k + l][:n])
+                checked += 1
+        assert checked > 0
+        dst.stopped = False
+        res = await asyncio.wait_for(asyncio.gather(*tasks), 300)
+        assert all(len(r["outputs"]) == 60 for r in res)
+        assert dst.finished_requests > 0
+        assert get([w.device_error.remote() for w in (ws, wd)], timeout=60) == [0, 0]
+    finally:
+        await llm.terminate()
+
+
+@pytest.mark.parametrize("p2p", [True, False], ids=["p2p-copy-kernel", "nccl"])
+def test_cross_group_transfer_two_gpus(p2p):
+    """Running requests move between two groups' instances with their KV
+    pages byte for byte (pulled over NVLink, or NCCL send/recv) and finish on
+    the destination."""
+    _need2()
+    asyncio.run(_transfer_native(p2p))

@@ -98,3 +98,47 @@ def test_queue_migration_moves_requests_to_the_idle_member(monkeypatch):
     assert finished[1] > 0, f"nothing migrated: {finished}"
     want = _reference(mc, reqs)
     assert got == want
+
+
+def test_cross_group_transfer_moves_running_requests(monkeypatch):
+    """Two balloon groups of one instance each: requests all land on
+    instance 0; the coordinator moves running requests with their KV pages
+    to instance 1 (pairs of send/recv_blocks on the ``global`` communicator
+    on CPU ranks; over NVLink pulls on GPUs), and they finish there with the
+    same tokens."""
+    monkeypatch.setenv("OMP_NUM_THREADS", "2")
+    cfg = KunServeConfig()
+    e = cfg.engine_config
+    e.ngroups, e.group_size, e.pp, e.tp, e.block_size = 2, 1, 1, 1, 16
+    e.dtype = "fp32"
+    e.enable_chunked_prefill, e.chunked_prefill_budget = True, 128
+    reqs = make_requests(10, seed=35, plen=(20, 50), olen=(24, 32))
+    import kunserve_b200.control.coordinator as co
+    monkeypatch.setattr(co.Coordinator, "get_next_assign", lambda self: (0, 0))
+
+    async def run():
+        from kunserve_b200.llm import AsyncLLM
+        mc = ModelConfig("tiny-llama", dtype="fp32")
+        llm = await AsyncLLM.create(cfg, model_config=mc, backend="torch", actor_kind="process",
+                                    devices=["cpu", "cpu"], num_gpu_blocks=64, seed=0)
+        try:
+            tasks = [_gen(llm, r) for r in reqs]
+            src, dst = llm.groups[0].instances[0], llm.groups[1].instances[0]
+            loop = asyncio.get_running_loop()
+            t0 = loop.time()
+            while sum(len(s.running_queue.get_decode_requests()) for s in src.scheduler) < 6:
+                assert loop.time() - t0 < 120
+                await asyncio.sleep(0.01)
+            moved = await llm.coordinator.transfer_requests(src, dst, 20)
+            results = await asyncio.wait_for(asyncio.gather(*tasks), 300)
+            for inst in (src, dst):
+                for bm in inst.block_managers:
+                    bm.check_invariants()
+                    assert not bm.block_table
+            return mc, {r["request_id"]: r["outputs"] for r in results}, moved, dst.finished_requests
+        finally:
+            await llm.terminate()
+
+    mc, got, moved, dst_done = asyncio.run(run())
+    assert 0 < moved <= 20 and dst_done > 0
+    assert got == _reference(mc, reqs)
