@@ -62,6 +62,9 @@ def bench_gemm(args, cublas=False):
                 elif args.partials:
                     parts = torch.empty(16 * M * N, device="cuda")
                     fn = lambda i: C.gemm_partials(A, Ws[i % len(Ws)], parts, 16)
+                elif args.epi == "silu":
+                    o2 = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+                    fn = lambda i: C.gemm(A, Ws[i % len(Ws)], o2, C.EPI_SILU, None, 256, args.max_split)
                 else:
                     fn = lambda i: C.gemm(A, Ws[i % len(Ws)], out, C.EPI_BF16, None, args.bn, args.max_split)
                 t = timeit(fn, args.warmup, args.iters)
@@ -160,6 +163,8 @@ def main():
     p.add_argument("--bn", type=int, default=0)
     p.add_argument("--max-split", type=int, default=16)
     p.add_argument("--partials", action="store_true", help="split-K into fp32 partial slots (decode GEMMs)")
+    p.add_argument("--epi", default="bf16", choices=["bf16", "silu"],
+                   help="silu: the gate/up epilogue (N interleaved gate/up rows, N/2 outputs)")
     p.add_argument("--batch", type=int, nargs="+", default=[1, 16, 64, 256])
     p.add_argument("--ctx", type=int, nargs="+", default=[512, 2048])
     p.add_argument("--nq", type=int, default=32)
