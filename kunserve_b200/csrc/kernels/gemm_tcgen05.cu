@@ -719,7 +719,12 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
     const int s_t = tiles - d;
     long long g = sms;
     if ((long long)s_t * num_kb / g < 8) g = (long long)s_t * num_kb / 8;
-    if (g > s_t) {
+    // in units of one tile's K loop: whole tiles take ceil(tiles / sms)
+    // rounds; the hybrid takes the data-parallel rounds plus the stream-K
+    // share of each CTA (reductions not counted, hence the margin)
+    const double whole = (double)((tiles + sms - 1) / sms);
+    const double hybrid = (double)d / sms + (double)((long long)s_t * num_kb + g - 1) / g / num_kb;
+    if (g > 0 && hybrid < whole - 0.5) {
       dp = d;
       sk = s_t;
       grid = (int)g;

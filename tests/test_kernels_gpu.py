@@ -97,6 +97,48 @@ def test_gemm_f32_add_silu(C):
     torch.cuda.synchronize()
 
 
+_REGULAR_SK_CHECK = """
+import torch
+from kunserve_b200.ops import native, check_error
+C = native()
+torch.manual_seed(5)
+res = []
+for M, N, K, epi in ((306, 27648, 5120, "silu"), (300, 15360, 5120, "bf16"), (140, 38400, 2048, "bf16")):
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    W = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    if epi == "silu":
+        out = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+        sk = C.gemm(A, W, out, C.EPI_SILU, None, 256, 16)
+        y = (A.float() @ W.float().t()).view(M, N // 256, 2, 128)
+        ref = (torch.nn.functional.silu(y[:, :, 0]) * y[:, :, 1]).reshape(M, N // 2)
+    else:
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        sk = C.gemm(A, W, out, C.EPI_BF16, None, 0, 16)
+        ref = A.float() @ W.float().t()
+    torch.cuda.synchronize()
+    rel = ((out.float() - ref).norm() / ref.norm()).item()
+    res.append((sk, rel))
+check_error()
+print("RES", res)
+"""
+
+
+def test_gemm_regular_stream_k():
+    """The regular kernel with its last partial wave spread along K
+    (KUNSERVE_REGULAR_SK=1): SiLU and bf16 epilogues equal the fp32 product."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, KUNSERVE_REGULAR_SK="1")
+    r = subprocess.run([sys.executable, "-c", _REGULAR_SK_CHECK], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    res = eval(r.stdout.split("RES", 1)[1])
+    assert any(sk > 0 for sk, _ in res), res
+    for sk, rel in res:
+        assert rel < 1e-2, res
+
+
 def test_rmsnorm(C):
     torch.manual_seed(2)
     for H in (512, 4096, 5120, 8192):
