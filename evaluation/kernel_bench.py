@@ -71,10 +71,17 @@ def bench_gemm(args, cublas=False):
                 check_error()
                 bytes_ = (M * K + N * K + M * N) * 2
                 flops = 2.0 * M * N * K
-                print(json.dumps({"kernel": "gemm_cublas" if cublas else "gemm_tcgen05", "M": M, "N": N, "K": K,
-                                  "us": round(t * 1e6, 2), "TB_s": round(bytes_ / t / 1e12, 3),
-                                  "bw_frac": round(bytes_ / t / bw, 3), "TFLOP_s": round(flops / t / 1e12, 1),
-                                  "flop_frac": round(flops / t / fl, 3), "peaks": src}), flush=True)
+                rec = {"kernel": "gemm_cublas" if cublas else "gemm_tcgen05", "M": M, "N": N, "K": K,
+                       "us": round(t * 1e6, 2), "TB_s": round(bytes_ / t / 1e12, 3),
+                       "bw_frac": round(bytes_ / t / bw, 3), "TFLOP_s": round(flops / t / 1e12, 1),
+                       "flop_frac": round(flops / t / fl, 3), "peaks": src}
+                if not cublas and not args.partials:
+                    epi = C.EPI_SILU if args.epi == "silu" else C.EPI_BF16
+                    bn = 256 if args.epi == "silu" else args.bn
+                    pl = C.gemm_plan(M, N, K, epi, bn, args.max_split > 1)
+                    rec["plan"] = "swap" if pl["swap"] else "pair" if pl["pair"] else \
+                        f"bn{pl['bn']}" + (f"+tail{pl['tail_splits']}" if pl["tail_splits"] else "")
+                print(json.dumps(rec), flush=True)
 
 
 def bench_attention(args):

@@ -21,7 +21,7 @@ namespace {
 __nv_bfloat16* bp(const torch::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
 
 struct Scratch {
-  torch::Tensor ws, counters;
+  torch::Tensor ws, counters, tail;
 };
 Scratch& scratch(int device) {
   static std::vector<Scratch> all(16);
@@ -30,6 +30,7 @@ Scratch& scratch(int device) {
     auto f32 = torch::TensorOptions().dtype(torch::kFloat32).device(torch::kCUDA, device);
     s.ws = torch::zeros({(int64_t)2 * 148 * 128 * 256}, f32);   // stream-K tiles, zero between GEMMs
     s.counters = torch::zeros({1 << 16}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, device));
+    s.tail = torch::empty({(int64_t)148 * 128 * 256}, f32);   // split-K tail slots
   }
   return s;
 }
@@ -44,8 +45,9 @@ int64_t gemm_op(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi
   TORCH_CHECK(A.size(1) % 8 == 0, "K must be a multiple of 8");
   c10::cuda::CUDAGuard g(A.device());
   const int M = A.size(0), K = A.size(1), N = B.size(0);
-  GemmPlan p = plan_gemm(M, N, K, (int)epi, (int)bn, max_split > 1);
+  GemmPlan p = plan_gemm(M, N, K, (int)epi, (int)bn, max_split > 1, max_split > 1);
   Scratch& sc = scratch(A.get_device());
+  if (plan_tail_floats(p) > (size_t)sc.tail.numel()) p = plan_gemm(M, N, K, (int)epi, (int)bn, false);
   TORCH_CHECK(plan_workspace_floats(p) <= (size_t)sc.ws.numel() && plan_counters(p) < sc.counters.numel(),
               "stream-K workspace too small");
   const __nv_bfloat16* res = nullptr;
@@ -58,6 +60,7 @@ int64_t gemm_op(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi
   TORCH_CHECK(finalize_plan(p, A.data_ptr(), K, B.data_ptr(), K, out.data_ptr(), (int)out.size(1), res,
                             (int)out.size(1), sc.ws.data_ptr<float>(), sc.counters.data_ptr<int>()),
               "tensor map encoding failed");
+  p.args.tail_ws = sc.tail.data_ptr<float>();
   run_gemm(p, at::cuda::getCurrentCUDAStream());
   return p.args.sk_tiles;
 }
@@ -404,6 +407,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("bytes", &PeerMapping::bytes);
   m.def("gemm", &gemm_op, py::arg("A"), py::arg("B"), py::arg("out"), py::arg("epi") = 0,
         py::arg("residual") = py::none(), py::arg("bn") = 0, py::arg("max_split") = 16);
+  m.def(
+      "gemm_plan",
+      [](int64_t M, int64_t N, int64_t K, int64_t epi, int64_t bn, bool stream_k) {
+        // the plan gemm() would run on the current device (tests, benchmarks)
+        GemmPlan p = plan_gemm((int)M, (int)N, (int)K, (int)epi, (int)bn, stream_k, stream_k);
+        py::dict d;
+        d["swap"] = p.swap;
+        d["pair"] = p.pair;
+        d["bn"] = p.bn;
+        d["grid"] = p.grid;
+        d["dp_tiles"] = p.args.dp_tiles;
+        d["sk_tiles"] = p.args.sk_tiles;
+        d["tail_splits"] = p.args.tail_splits;
+        return d;
+      },
+      py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi") = 0, py::arg("bn") = 0, py::arg("stream_k") = true);
   m.def("rmsnorm", &rmsnorm_op);
   m.def("rope_append", &rope_append_op);
   m.def("attention", &attention_op);

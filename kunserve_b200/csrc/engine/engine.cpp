@@ -83,6 +83,8 @@ Engine::Engine(const EngineShape& s, int device) : s_(s), device_(device) {
   // tiles); kept all zero between GEMMs by the kernels themselves
   const int64_t ws_floats = (int64_t)2 * 148 * 128 * 256;
   gemm_ws_ = torch::zeros({ws_floats}, f32);
+  // split-K tail slots: at most one unit per SM, each a 128 x 256 fp32 tile
+  tail_ws_ = torch::empty({(int64_t)148 * 128 * 256}, f32);
   // split-K partial slots of decode-sized GEMMs (up to 128 tokens)
   part_ws_ = torch::empty({(int64_t)kMaxPartSlots * 128 * std::max<int64_t>(qkv_n_, s.hidden)}, f32);
   counters_ = torch::zeros({1 << 16}, i32);
@@ -281,10 +283,11 @@ bool make_wmap(WMap* m, const void* w, int rows, int cols, bool with128) {
   m->rows = rows;
   m->cols = cols;
   if (!make_tmap_bf16(&m->b256, w, rows, cols, cols, 256)) return false;
-  return !with128 || make_tmap_bf16(&m->b128, w, rows, cols, cols, 128);
+  // 128-row boxes: 128-wide tiles (when allowed) and CTA-pair tiles
+  return make_tmap_bf16(&m->b128, w, rows, cols, cols, 128);
 }
 
-static const CUtensorMap& pick(const WMap& m, const GemmPlan& p) { return p.bn == 128 ? m.b128 : m.b256; }
+static const CUtensorMap& pick(const WMap& m, const GemmPlan& p) { return b_box_rows(p) == 128 ? m.b128 : m.b256; }
 
 void Engine::lib_gemm(const __nv_bfloat16* A, const WMap& mB, int M, int N, int K, int epi, void* out, int ldc,
                       const __nv_bfloat16* res) {
@@ -322,8 +325,9 @@ void Engine::gemm(const CUtensorMap* mA, const __nv_bfloat16* A, const WMap& mB,
     return;
   }
   const int bn = mB.has128 ? 0 : 256;
-  GemmPlan p = plan_gemm(M, N, K, epi, bn, true);
-  if (plan_workspace_floats(p) > (size_t)gemm_ws_.numel() || plan_counters(p) >= counters_.numel())
+  GemmPlan p = plan_gemm(M, N, K, epi, bn, true, true);
+  if (plan_workspace_floats(p) > (size_t)gemm_ws_.numel() || plan_counters(p) >= counters_.numel() ||
+      plan_tail_floats(p) > (size_t)tail_ws_.numel())
     p = plan_gemm(M, N, K, epi, bn, false);
   KUS_CHECK(p.bn == 256 || (p.bn == 128 && mB.has128), "no weight map for the planned tile");
   const int box = a_box_rows(p);
@@ -334,6 +338,7 @@ void Engine::gemm(const CUtensorMap* mA, const __nv_bfloat16* A, const WMap& mB,
   p.args.residual = res;
   p.args.ld_res = ldc;
   p.args.workspace = gemm_ws_.data_ptr<float>();
+  p.args.tail_ws = tail_ws_.data_ptr<float>();
   p.args.tile_counters = counters_.data_ptr<int>();
   run_gemm(p, st);
   ++launches_;

@@ -36,8 +36,8 @@ struct EngineShape {
 // Weight tensor maps for 256-row tiles and, where the planner may pick
 // them, 128-row tiles.
 struct WMap {
-  CUtensorMap b256, b128;
-  bool has128 = false;
+  CUtensorMap b256, b128;   // TMA maps with 256- and 128-row boxes
+  bool has128 = false;      // 128-wide output tiles allowed (the SiLU weights pair 128-row halves)
   const void* ptr = nullptr;   // the weight itself (library baseline GEMMs)
   int rows = 0, cols = 0;
 };
@@ -151,6 +151,7 @@ class Engine {
   torch::Tensor embed_, final_norm_, lm_head_;
   WMap m_lm_head_;
   // workspaces
+  torch::Tensor tail_ws_;   // split-K tail slots of the regular GEMM kernel
   torch::Tensor h_, y_, qkv_, attn_, act_, tmp_, ylast_, logits_, gemm_ws_, counters_, attn_o_, attn_ml_,
       meta_dev_, tokens_dev_, tokens_host_, cos_sin_, dec_o_, dec_ml_, dec_count_;
   // activation TMA descriptors per token-box height (16, 32, 64, 128 rows)

@@ -63,6 +63,16 @@ struct GemmArgs {
   int part_splits;
   int part_kbs;
   long long part_stride;
+  // Split-K tail (regular kernel): with tail_splits = S > 0 the sk_tiles
+  // tiles after the dp_tiles whole ones are cut along K into S ranges of
+  // tail_kbs k-blocks, one work unit each; a unit stores its fp32 partial
+  // into slot (tail tile, s) of tail_ws with plain stores and counts itself
+  // in tile_counters[tail tile]; the unit that arrives last sums the S slots
+  // and runs the tile's epilogue (no CTA waits for another).  tail_ws needs
+  // no initial value.
+  int tail_splits;
+  int tail_kbs;
+  float* tail_ws;
 };
 
 struct GemmPlan {
@@ -74,7 +84,11 @@ struct GemmPlan {
   int grid;
   int swap;   // 1: decode-shaped, operands swapped (gemm_swap.cu), token tile of `bnt` rows
   int bnt;
+  int pair;   // 1: CTA pairs (cta_group::2) on 256 x bn tiles; B's TMA box is bn/2 rows
 };
+
+// Rows of the B (weight) TMA box a plan needs.
+inline int b_box_rows(const GemmPlan& p) { return p.pair ? p.bn / 2 : p.bn; }
 
 // Rows of the A (token) TMA box a plan needs: 128, or bnt when swapped.
 inline int a_box_rows(const GemmPlan& p) { return p.swap ? p.bnt : 128; }
@@ -84,13 +98,20 @@ int num_sms();
 bool make_tmap_bf16(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
                     uint32_t box_rows);
 int choose_bn(int M, int N, int epi);
-// Tiles and work split for an M x N x K problem (bn <= 0: choose).  Stream-K
-// applies to the swapped decode kernel only; with stream_k false, or for the
-// regular kernel, every tile is a whole-tile unit (no workspace traffic).
-GemmPlan plan_gemm(int M, int N, int K, int epi, int bn = 0, bool stream_k = true);
+// Tiles and work split for an M x N x K problem (bn <= 0: choose).  With
+// stream_k, the swapped decode kernel spreads its last waves along K
+// (stream-K) and the regular kernel cuts the tiles of its last partial wave
+// into split-K units (tail_splits); with stream_k false every tile is a
+// whole-tile unit (no workspace traffic).
+// A split-K tail is planned only with split_tail (the caller then binds
+// args.tail_ws, plan_tail_floats(p) floats).
+GemmPlan plan_gemm(int M, int N, int K, int epi, int bn = 0, bool stream_k = true, bool split_tail = false);
 // fp32 workspace floats and counters a plan needs (workspace all zero).
 size_t plan_workspace_floats(const GemmPlan& p);
 inline int plan_counters(const GemmPlan& p) { return p.args.sk_tiles; }
+inline size_t plan_tail_floats(const GemmPlan& p) {
+  return p.args.tail_splits > 0 ? (size_t)p.args.sk_tiles * p.args.tail_splits * 128 * p.bn : 0;
+}
 // Turn an fp32 plan into split-K with partial slots (at most max_splits;
 // swapped plans: at least 4 k-blocks each, about one unit per SM; regular
 // plans: 128 x 256 tiles, at least 8 k-blocks each, used when the tiles do

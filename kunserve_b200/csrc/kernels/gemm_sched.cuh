@@ -16,19 +16,27 @@ namespace kus {
 struct SegWalk {
   int t, stride, dp_tiles, num_kb;
   int parts, part_kbs, units;   // split-K with partial slots
+  int tails, tail_kbs, tu, tail_units;   // split-K tail units
   long long i, end;
 
-  __device__ __forceinline__ SegWalk(const GemmArgs& a) {
-    t = blockIdx.x;
-    stride = gridDim.x;
+  __device__ __forceinline__ SegWalk(const GemmArgs& a) : SegWalk(a, blockIdx.x, gridDim.x) {}
+
+  // walker `id` of `nwalk` (a CTA pair walks as one: id = pair index)
+  __device__ __forceinline__ SegWalk(const GemmArgs& a, int id, int nwalk) {
+    t = id;
+    stride = nwalk;
     dp_tiles = a.dp_tiles;
     num_kb = a.num_kb;
     parts = a.part_splits;
     part_kbs = a.part_kbs;
     units = parts > 0 ? a.n_tiles * a.m_tiles * parts : 0;
-    const long long total = (long long)a.sk_tiles * a.num_kb;
-    i = total * blockIdx.x / gridDim.x;
-    end = total * (blockIdx.x + 1) / gridDim.x;
+    tails = a.tail_splits;
+    tail_kbs = a.tail_kbs;
+    tu = id;
+    tail_units = tails > 0 ? a.sk_tiles * tails : 0;
+    const long long total = tails > 0 ? 0 : (long long)a.sk_tiles * a.num_kb;
+    i = total * id / nwalk;
+    end = total * (id + 1) / nwalk;
   }
 
   // Next segment of this CTA; false when the walk is over.
@@ -46,6 +54,15 @@ struct SegWalk {
       kb0 = 0;
       kb1 = num_kb;
       t += stride;
+      return true;
+    }
+    if (tails > 0) {   // unit u = (tail tile, split) after the whole tiles
+      if (tu >= tail_units) return false;
+      const int lt = tu / tails;
+      tile = dp_tiles + lt;
+      kb0 = (tu - lt * tails) * tail_kbs;
+      kb1 = min(kb0 + tail_kbs, num_kb);
+      tu += stride;
       return true;
     }
     if (i >= end) return false;
@@ -81,6 +98,28 @@ __device__ __forceinline__ void take16(float* src, float (&v)[16]) {
     v[4 * i + 3] = x[i].w;
     __stcg(reinterpret_cast<float4*>(src) + i, make_float4(0.f, 0.f, 0.f, 0.f));
   }
+}
+
+// Epilogue threads of a CTA that just stored split `kb0 / tail_kbs` of tail
+// tile `lt` into its workspace slot: count the split; true for every thread
+// of the CTA whose split arrived last (it then sums the slots).
+__device__ __forceinline__ bool tail_arrive(const GemmArgs& a, int lt, int et, int* flag_smem) {
+  __threadfence();
+  named_barrier(1, 128);
+  if (et == 0) {
+    int last = 0;
+    if (!error_set()) {
+      const int prev = atomicAdd(&a.tile_counters[lt], 1);
+      last = (prev + 1 == a.tail_splits);
+      if (last) a.tile_counters[lt] = 0;   // ready for the next GEMM
+    }
+    *flag_smem = last;
+  }
+  named_barrier(1, 128);
+  const bool last = *flag_smem != 0;
+  named_barrier(1, 128);
+  if (last) __threadfence();
+  return last;
 }
 
 // Epilogue threads of a CTA that just reduced `kbs` k-blocks of stream-K

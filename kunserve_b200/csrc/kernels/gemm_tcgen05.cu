@@ -14,12 +14,15 @@
 //
 // Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
 // owner, warps 2-5 epilogue.  The grid is persistent (<= one CTA per SM) and
-// walks the segments of gemm_sched.cuh: whole tiles, then an equal share of
-// the stream-K tiles' K loops.  A partial segment adds its fp32 tile into
-// the workspace with L2 reductions and counts its k-blocks; the CTA that
-// completes a tile's K loop reads the sum back (zeroing it) and runs the
-// epilogue, so no CTA ever waits for another.  All mbarrier waits are
-// bounded (common.cuh).
+// walks the segments of gemm_sched.cuh: whole tiles, then the tiles of the
+// last partial wave.  By default those are cut along K into split units
+// (one per SM the whole tiles would leave idle): a unit stores its fp32
+// partial into its own workspace slot and counts itself; the unit that
+// arrives last sums the slots and runs the epilogue.  The alternative
+// stream-K mode spreads the K loops evenly and adds partials with L2
+// reductions, the CTA completing a tile's K loop reading the sum back
+// (zeroing it).  Either way no CTA ever waits for another.  All mbarrier
+// waits are bounded (common.cuh).
 #include "../common.cuh"
 #include "gemm.h"
 #include "gemm_sched.cuh"
@@ -35,10 +38,12 @@ constexpr int BK = 64;
 constexpr int kThreads = 192;
 constexpr int kSmemBudget = 200 * 1024;
 
-template <int BN>
+// PAIR: a CTA pair computes 256 x BN tiles (cta_group::2); each CTA holds
+// its 128 rows of A and BN/2 rows of B per stage.
+template <int BN, int PAIR = 0>
 struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kBBytes = (PAIR ? BN / 2 : BN) * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kStages = (kSmemBudget / kStageBytes) > 8 ? 8 : (kSmemBudget / kStageBytes);
   static constexpr int kTmemCols = 2 * BN;
@@ -48,6 +53,20 @@ struct Cfg {
 };
 
 KUS_DEVICE float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+// x[0..7] += the 8 floats at src (read at L2: written by other CTAs)
+KUS_DEVICE void add8_cg(float (&x)[8], const float* src) {
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
+  const float4 b = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+  x[0] += a.x;
+  x[1] += a.y;
+  x[2] += a.z;
+  x[3] += a.w;
+  x[4] += b.x;
+  x[5] += b.y;
+  x[6] += b.z;
+  x[7] += b.w;
+}
 
 template <int EPI>
 KUS_DEVICE void store16(const GemmArgs& a, int row, int col, const float (&v)[16]) {
@@ -211,6 +230,14 @@ KUS_DEVICE void tile_mn(const GemmArgs& a, int tile, int& m, int& n) {
   m = mr < first ? mr : mr + L;
 }
 
+// First A row of single-CTA m-tile m.  With a ragged M (> 128) the last
+// m-tile is shifted up to end at row M, so that its TMA box reads no rows
+// past M; its rows below 128 m belong to tile m - 1 and are not written.
+KUS_DEVICE int tile_row0(const GemmArgs& a, int m) {
+  const int r = m * BM;
+  return (a.ag_rows <= 0 && r + BM > a.M && a.M > BM) ? a.M - BM : r;
+}
+
 KUS_DEVICE bool ag_local(const GemmArgs& a, int m) {
   const int L = a.ag_rows / BM;
   return m >= a.ag_rank * L && m < (a.ag_rank + 1) * L;
@@ -285,10 +312,17 @@ KUS_DEVICE void ag_gather_slices(const GemmArgs& a, int gt) {
   }
 }
 
-template <int BN, int EPI, int GW>
+// PAIR = 1: launched in clusters of two CTAs; pair tile t covers rows
+// [256 m, 256 m + 256) and columns [BN n, BN n + BN).  CTA rank r loads A rows
+// 256 m + 128 r and B rows BN n + r BN/2 into its own shared memory, with the
+// transaction bytes counted on the leader's (rank 0) full barrier; the
+// leader's MMA thread issues cta_group::2 MMAs over both CTAs' stages and its
+// commits arrive on both CTAs' barriers; each CTA's epilogue reads its own
+// TMEM rows and reports the accumulator free on the leader's tempty.
+template <int BN, int EPI, int GW, int PAIR = 0>
 __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
@@ -305,6 +339,10 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
   const int lane = threadIdx.x % 32;
 
   const int num_kb = args.num_kb;
+  const uint32_t prank = PAIR ? cluster_rank() : 0u;
+  const bool leader = prank == 0;
+  const int walk_id = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int walk_n = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
@@ -313,15 +351,24 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], PAIR ? 2 : 128);
     }
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_holder, C::kTmemCols);
+  if (warp == 1) {
+    if (PAIR)
+      tmem_alloc_pair(tmem_holder, C::kTmemCols);
+    else
+      tmem_alloc(tmem_holder, C::kTmemCols);
+  }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();   // both CTAs' barriers initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // the leader's full[0] and tempty[0] in the cluster window (PAIR)
+  const uint32_t lead_full = PAIR ? mapa_shared(smem_u32(&full[0]), 0) : 0u;
+  const uint32_t lead_tempty = PAIR ? mapa_shared(smem_u32(&tempty[0]), 0) : 0u;
 
   // everything below except the producer's weight prefetch may depend on
   // the previous kernel (activations, residual, workspace)
@@ -338,15 +385,14 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
     if (elect_one_sync()) {
       prefetch_tmap(&tmA);
       prefetch_tmap(&tmB);
-      // A tile source: this GPU's A, or (all-gather) the owning rank's rows
-      SegWalk walk(args);
+      SegWalk walk(args, walk_id, walk_n);
       int tile = 0, kb0 = 0, kb1 = 0;
       bool have = walk.next(tile, kb0, kb1);
       // A tile source: this GPU's A, or (all-gather) the own shard for local
       // rows and the gathered copy for remote rows once it has landed
       const unsigned ready_target = args.ag_epoch * (unsigned)args.ag_chunks;
       auto a_src = [&](int m, int& row) -> const CUtensorMap* {
-        row = m * BM;
+        row = tile_row0(args, m);
         if (args.ag_rows <= 0) return &tmA;
         if (ag_local(args, m)) {
           row -= args.ag_rank * args.ag_rows;
@@ -370,20 +416,42 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
         asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(args.ag_maps) : "memory");
       // weights are not written by earlier kernels: the first stages get
       // their weight tiles while the previous kernel drains
+      // PAIR: the leader expects both CTAs' bytes; each CTA loads its halves
+      constexpr uint32_t kTx = PAIR ? 2u * C::kStageBytes : (uint32_t)C::kStageBytes;
+      constexpr int kBRows = PAIR ? BN / 2 : BN;
+      auto load_b = [&](int st, int kb, int n) {
+        if (PAIR)
+          tma_load_2d_pair(smem_b + st * C::kBBytes, &tmB, lead_full + 8u * st, kb * BK, n * BN + (int)prank * kBRows);
+        else
+          tma_load_2d(smem_b + st * C::kBBytes, &tmB, &full[st], kb * BK, n * BN);
+      };
+      auto load_a = [&](int st, int kb, const CUtensorMap* am, int arow) {
+        if (PAIR)
+          tma_load_2d_pair(smem_a + st * C::kABytes, am, lead_full + 8u * st, kb * BK, arow);
+        else
+          tma_load_2d(smem_a + st * C::kABytes, am, &full[st], kb * BK, arow);
+      };
+      auto a_row = [&](int m, int& arow) -> const CUtensorMap* {
+        if (PAIR) {
+          arow = (2 * m + (int)prank) * BM;
+          return &tmA;
+        }
+        return a_src(m, arow);
+      };
       const int pre = have ? min(C::kStages, kb1 - kb0) : 0;
       for (int j = 0; j < pre; ++j) {
-        mbar_arrive_expect_tx(&full[j], C::kStageBytes);
+        if (leader) mbar_arrive_expect_tx(&full[j], kTx);
         int m0, n0;
         tile_mn(args, tile, m0, n0);
-        tma_load_2d(smem_b + j * C::kBBytes, &tmB, &full[j], (kb0 + j) * BK, n0 * BN);
+        load_b(j, kb0 + j, n0);
       }
       pdl_wait();
       pdl_trigger();
       for (int j = 0; j < pre; ++j) {
         int arow, m0, n0;
         tile_mn(args, tile, m0, n0);
-        const CUtensorMap* am = a_src(m0, arow);
-        tma_load_2d(smem_a + j * C::kABytes, am, &full[j], (kb0 + j) * BK, arow);
+        const CUtensorMap* am = a_row(m0, arow);
+        load_a(j, kb0 + j, am, arow);
       }
       int stage = pre == C::kStages ? 0 : pre;
       uint32_t phase = pre == C::kStages ? 1u : 0u;
@@ -393,15 +461,15 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
         int m, n;
         tile_mn(args, tile, m, n);
         int arow;
-        const CUtensorMap* am = a_src(m, arow);   // once per tile (a bounded wait for remote rows)
+        const CUtensorMap* am = a_row(m, arow);   // once per tile (a bounded wait for remote rows)
         for (int kb = kb_from; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, kErrWaitEmpty)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C::kStageBytes);
-          tma_load_2d(smem_a + stage * C::kABytes, am, &full[stage], kb * BK, arow);
-          tma_load_2d(smem_b + stage * C::kBBytes, &tmB, &full[stage], kb * BK, n * BN);
+          if (leader) mbar_arrive_expect_tx(&full[stage], kTx);
+          load_a(stage, kb, am, arow);
+          load_b(stage, kb, n);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
@@ -422,17 +490,19 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    if (elect_one_sync()) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    if (leader && elect_one_sync()) {
+      constexpr uint32_t idesc = idesc_bf16_f32(PAIR ? 2 * BM : BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      SegWalk walk(args);
+      SegWalk walk(args, walk_id, walk_n);
       int tile, kb0, kb1;
       while (ok && walk.next(tile, kb0, kb1)) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, kErrWaitTmemEmpty)) break;
+        const bool freed = PAIR ? mbar_wait_cluster(&tempty[acc], acc_phase ^ 1, kErrWaitTmemEmpty)
+                                : mbar_wait(&tempty[acc], acc_phase ^ 1, kErrWaitTmemEmpty);
+        if (!freed) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -446,15 +516,24 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // advance 16 bf16 = 32 bytes along K inside the swizzle atom
-            umma_f16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            if (PAIR)
+              umma_f16_pair(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            else
+              umma_f16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if (PAIR)
+            umma_commit_pair(&empty[stage]);
+          else
+            umma_commit(&empty[stage]);
           if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1;
           }
         }
-        umma_commit(&tfull[acc]);
+        if (PAIR)
+          umma_commit_pair(&tfull[acc]);
+        else
+          umma_commit(&tfull[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -469,12 +548,16 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     constexpr int kOutCols = (EPI == EPI_SILU) ? BN / 2 : BN;
-    SegWalk walk(args);
+    SegWalk walk(args, walk_id, walk_n);
     int tile, kb0, kb1;
     while (walk.next(tile, kb0, kb1)) {
       int m, n;
       tile_mn(args, tile, m, n);
-      const int row = m * BM + r_in_tile;
+      if (PAIR) m = 2 * m + (int)prank;   // this CTA's 128-row half of the pair tile
+      // rows [row0, row0 + 128) are in TMEM; rows below lo belong to tile m - 1
+      const int lo = m * BM;
+      const int row0 = PAIR ? lo : tile_row0(args, m);
+      const int row = row0 + r_in_tile;
       // A failed (timed-out) wait skips the work but keeps every thread on the
       // same barrier sequence; once the error flag is set later waits fail fast.
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, kErrWaitTmemFull));
@@ -512,8 +595,8 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
           for (int it = 0; it < 8; ++it) {
             const int rr = we * 32 + it * 4 + (lane >> 3);   // 4 rows x 8 lanes of 16 B per pass
             const int cc = (lane & 7) * 8;
-            const int grow = m * BM + rr, gcol = col0 + c0 + cc;
-            if (ok && grow < args.M && gcol < args.n_out) {
+            const int grow = row0 + rr, gcol = col0 + c0 + cc;
+            if (ok && grow >= lo && grow < args.M && gcol < args.n_out) {
               float x[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) x[e] = epi[rr * C::kEpiStride + cc + e];
@@ -523,7 +606,85 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
           named_barrier(2, 128);
         }
         tc_fence_before();
+        if (PAIR) {
+          // both CTAs' epilogues report to the leader, which owns the MMA
+          named_barrier(2, 128);
+          if (et == 0) mbar_arrive_remote(lead_tempty + 8u * acc);
+        } else {
+          mbar_arrive(&tempty[acc]);
+        }
+      } else if (args.tail_splits > 0) {
+        // split-K tail unit: this split's raw fp32 partial into its own
+        // workspace slot, staged through shared memory for 16-byte stores
+        const int lt = tile - args.dp_tiles;
+        float* slots = args.tail_ws + (size_t)lt * args.tail_splits * (BM * BN);
+        float* slot = slots + (size_t)(kb0 / args.tail_kbs) * (BM * BN);
+        float* erow = epi + r_in_tile * C::kEpiStride;
+        const int we = warp - 2;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+#pragma unroll
+          for (int c = 0; c < 64; c += 16) {
+            float v[16];
+            tmem_ld16(taddr + c0 + c, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) erow[c + i] = v[i];
+          }
+          named_barrier(2, 128);
+          if (ok) {
+#pragma unroll
+            for (int it = 0; it < 8; ++it) {
+              const int rr = we * 32 + it * 4 + (lane >> 3);
+              const int cc = (lane & 7) * 8;
+              const float* e = epi + rr * C::kEpiStride + cc;
+              float* d = slot + (size_t)rr * BN + c0 + cc;
+              __stcg(reinterpret_cast<float4*>(d), make_float4(e[0], e[1], e[2], e[3]));
+              __stcg(reinterpret_cast<float4*>(d + 4), make_float4(e[4], e[5], e[6], e[7]));
+            }
+          }
+          named_barrier(2, 128);
+        }
+        tc_fence_before();
         mbar_arrive(&tempty[acc]);
+        if (tail_arrive(args, lt, et, flag_smem)) {
+          // the last split sums the slots and runs the tile's epilogue: 8
+          // output columns of one row per item, kU items per thread in
+          // flight (a warp reads 512 or 1024 contiguous bytes of a slot)
+          constexpr int kVec = kOutCols / 8;
+          constexpr int kItems = BM * kVec / 128;
+          constexpr int kU = 4;
+          static_assert(kItems % kU == 0, "fix-up items");
+#pragma unroll 1
+          for (int i0 = 0; i0 < kItems; i0 += kU) {
+            float x[kU][8], u[kU][8];
+#pragma unroll
+            for (int j = 0; j < kU; ++j)
+#pragma unroll
+              for (int e = 0; e < 8; ++e) x[j][e] = u[j][e] = 0.f;
+#pragma unroll 2
+            for (int sp = 0; sp < args.tail_splits; ++sp) {
+              const float* base = slots + (size_t)sp * (BM * BN);
+#pragma unroll
+              for (int j = 0; j < kU; ++j) {
+                const int it = et + (i0 + j) * 128;
+                const int rr = it / kVec, cc = (it - rr * kVec) * 8;
+                add8_cg(x[j], base + (size_t)rr * BN + cc);
+                if (EPI == EPI_SILU) add8_cg(u[j], base + (size_t)rr * BN + BN / 2 + cc);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < kU; ++j) {
+              const int it = et + (i0 + j) * 128;
+              const int rr = it / kVec, cc = (it - rr * kVec) * 8;
+              const int grow = row0 + rr;
+              if (EPI == EPI_SILU) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x[j][e] = silu(x[j][e]) * u[j][e];
+              }
+              if (grow >= lo && grow < args.M && col0 + cc < args.n_out) out8<EPI>(args, grow, col0 + cc, x[j]);
+            }
+          }
+        }
       } else {
         // stream-K: add the partial into the tile's fp32 accumulator
         const int sk = tile - args.dp_tiles;
@@ -534,13 +695,13 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
           for (int c = 0; c < BN; c += 16) {
             float v[16];
             tmem_ld16(taddr + c, v);
-            if (row < args.M) red_add16(ws + c, v);
+            if (row >= lo && row < args.M) red_add16(ws + c, v);
           }
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
         const bool last = sk_arrive(args, sk, kb1 - kb0, et, flag_smem);
-        if (last && row < args.M) {
+        if (last && row >= lo && row < args.M) {
           if (EPI == EPI_SILU) {
 #pragma unroll 1
             for (int c = 0; c < BN / 2; c += 16) {
@@ -570,7 +731,13 @@ __global__ void __launch_bounds__(kThreads + 32 * GW, 1)
   if (EPI == EPI_PUSH && warp >= 2 && warp < 6) signal_push_done(args, threadIdx.x - 64);
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem_base, C::kTmemCols);
+  if (PAIR) cluster_sync();   // the pair is done with both TMEMs and barriers
+  if (warp == 1) {
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    else
+      tmem_dealloc(tmem_base, C::kTmemCols);
+  }
 }
 
 // -------------------------------------------------------------- host side
@@ -591,6 +758,14 @@ void launch(const GemmPlan& p, cudaStream_t stream) {
   ensure_smem_attr(reinterpret_cast<const void*>(gemm_kernel<BN, EPI, GW>), C::kSmemBytes);
   launch_k(gemm_kernel<BN, EPI, GW>, dim3(p.grid), dim3(kThreads + 32 * GW), C::kSmemBytes, stream, p.tmA, p.tmB,
            p.args);
+}
+
+template <int BN, int EPI>
+void launch_pair(const GemmPlan& p, cudaStream_t stream) {
+  using C = Cfg<BN, 1>;
+  ensure_smem_attr(reinterpret_cast<const void*>(gemm_kernel<BN, EPI, 0, 1>), C::kSmemBytes);
+  launch_kc(gemm_kernel<BN, EPI, 0, 1>, dim3(p.grid), dim3(kThreads), C::kSmemBytes, stream, 2, p.tmA, p.tmB,
+            p.args);
 }
 
 template <int EPI>
@@ -658,24 +833,84 @@ int choose_bn(int M, int N, int epi) {
 }
 
 size_t plan_workspace_floats(const GemmPlan& p) {
+  if (p.args.tail_splits > 0) return 0;   // slots live in tail_ws
   const size_t tile = p.swap ? (size_t)256 * p.bnt : (size_t)BM * p.bn;
   return (size_t)p.args.sk_tiles * tile;
 }
 
-// Stream-K for the regular kernel when whole tiles leave SMs idle
-// (KUNSERVE_REGULAR_SK: 0 off, 1 on; read once).
-static bool regular_stream_k() {
-  static int on = -1;
-  if (on < 0) {
+// How the regular kernel treats the last partial wave of tiles
+// (KUNSERVE_REGULAR_SK, read once): 0 (default) whole tiles, 1 stream-K
+// with L2 reductions, 2 split-K tail units with partial slots.  Measured on
+// B200 at 256-384 rows (Llama-2-13B gate/up and qkv) neither split beat
+// whole tiles: the weight stream, not the idle SMs, bounds these GEMMs.
+static int regular_tail_mode() {
+  static int mode = -1;
+  if (mode < 0) {
     const char* e = std::getenv("KUNSERVE_REGULAR_SK");
-    on = (e && e[0] == '0') ? 0 : (e && e[0] == '1') ? 1 : 0;
+    mode = (e && e[0] == '1') ? 1 : (e && e[0] == '2') ? 2 : 0;
   }
-  return on == 1;
+  return mode;
 }
 
-GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
+// Split-K tail plan: S splits per tail tile (0: none pays).  Costs are in
+// units of one whole tile's K loop: whole tiles spend a full round on the
+// tail; split units spend 1/S of it, plus about 3 % of a tile for each
+// slot the last split reads back and for the partial it stores.
+static int tail_splits_for(int tiles, int sms, int num_kb) {
+  const int tail = tiles % sms;
+  if (tail == 0 || tail > sms / 2) return 0;
+  int smax = sms / tail;
+  if (smax > num_kb / 8) smax = num_kb / 8;   // at least 8 k-blocks per split
+  if (smax > 8) smax = 8;
+  static int forced = -1;                      // KUNSERVE_TAIL_SPLITS: fixed S (tuning)
+  if (forced < 0) {
+    const char* e = std::getenv("KUNSERVE_TAIL_SPLITS");
+    forced = e ? std::atoi(e) : 0;
+  }
+  if (forced > 0) return forced >= 2 && forced <= smax ? forced : 0;
+  int best = 0;
+  double best_cost = 1.0 - 0.15;              // must save 15 % of a tile round
+  for (int S = 2; S <= smax; ++S) {
+    const double cost = 1.0 / S + 0.03 + 0.03 * S;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = S;
+    }
+  }
+  return best;
+}
+
+// CTA-pair tiles (KUNSERVE_GEMM_PAIR, read once): 0 never, 1 (default)
+// where they pay, 2 wherever they apply.
+static int gemm_pair_mode() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = std::getenv("KUNSERVE_GEMM_PAIR");
+    mode = (e && e[0] == '0') ? 0 : (e && e[0] == '2') ? 2 : 1;
+  }
+  return mode;
+}
+
+// Whether 256 x 256 pair tiles beat 128 x 256 single-CTA tiles.  Measured on
+// B200 (Llama shapes, K = 5120): a pair round is 5-7 % faster than a
+// single-CTA round (32 instead of 48 KB of operands per k-block and SM), but
+// a pair tile over a ragged M computes up to 255 padding rows, where the
+// single-CTA kernel shifts its last tile onto real rows.  Pairs therefore
+// run when M is a multiple of 256, when the last pair tile is more than half
+// full, or from 1024 rows on.
+static bool use_pair(int M, int epi) {
+  const int mode = gemm_pair_mode();
+  if (mode == 0 || M <= BM || !(epi == EPI_BF16 || epi == EPI_SILU || epi == EPI_ADD || epi == EPI_F32)) return false;
+  if (mode == 2) return true;
+  const int rem = M % (2 * BM);
+  return rem == 0 || rem > BM || M >= 1024;
+}
+
+GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k, bool split_tail) {
   GemmPlan p{};
   p.epi = epi;
+  const int num_kb = (K + BK - 1) / BK;
+  const int sms = num_sms();
   // up to 128 tokens: swap operands so the weight tile fills the 128-row MMA side
   if ((bn == 0 || bn == 256) && M <= 128 && N >= 256) {
     p.swap = 1;
@@ -683,13 +918,18 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
     p.bn = 256;
   } else {
     p.bn = bn > 0 ? bn : choose_bn(M, N, epi);
+    if (stream_k && (bn == 0 || bn == 256) && use_pair(M, epi)) {
+      p.pair = 1;
+      p.bn = 256;
+    }
   }
-  const int m_tiles = p.swap ? 1 : (M + BM - 1) / BM;
+  const int tile_rows = p.pair ? 2 * BM : BM;
+  const int m_tiles = p.swap ? 1 : (M + tile_rows - 1) / tile_rows;
   const int n_tiles = (N + p.bn - 1) / p.bn;
-  const int num_kb = (K + BK - 1) / BK;
-  const int sms = num_sms();
   const int tiles = m_tiles * n_tiles;
-  int dp = tiles, sk = 0, grid = tiles < sms ? tiles : sms;
+  const int walkers = p.pair ? sms / 2 : sms;
+  int dp = tiles, sk = 0, grid = tiles < walkers ? tiles : walkers;
+  if (p.pair) grid *= 2;
   // Stream-K only for the memory-bound swapped kernel, and only where the
   // whole-tile grid would leave most SMs idle: its fp32 reductions grow with
   // the token tile, and measured on B200 whole tiles win from 17 tokens up
@@ -709,7 +949,24 @@ GemmPlan plan_gemm(int M, int N, int K, int epi, int bn, bool stream_k) {
       sk = 0;
       grid = tiles < sms ? tiles : sms;
     }
-  } else if (stream_k && !p.swap && regular_stream_k() && tiles % sms != 0 && tiles % sms < sms / 2 &&
+  } else if (stream_k && split_tail && !p.swap && !p.pair && regular_tail_mode() == 2 &&
+             tail_splits_for(tiles, sms, num_kb) > 0) {
+    // the tiles of the last partial wave are cut along K so that the SMs the
+    // whole tiles would leave idle share them
+    int S = tail_splits_for(tiles, sms, num_kb);
+    int kbs = (num_kb + S - 1) / S;
+    while (S > 1 && (S - 1) * kbs >= num_kb) {   // every split owns k-blocks
+      --S;
+      kbs = (num_kb + S - 1) / S;
+    }
+    if (S > 1) {
+      sk = tiles % sms;
+      dp = tiles - sk;
+      grid = sms;
+      p.args.tail_splits = S;
+      p.args.tail_kbs = kbs;
+    }
+  } else if (stream_k && !p.swap && !p.pair && regular_tail_mode() == 1 && tiles % sms != 0 && tiles % sms < sms / 2 &&
              num_kb >= 16) {
     // regular kernel: the last wave is less than half full, so whole tiles
     // leave most SMs idle at its end; that wave plus one full wave (if any)
@@ -771,6 +1028,7 @@ int plan_split_partials(GemmPlan& p, int max_splits, long long part_stride) {
   p.args.part_stride = part_stride;
   p.args.dp_tiles = 0;
   p.args.sk_tiles = 0;
+  p.args.tail_splits = 0;
   p.grid = tiles * S < sms ? tiles * S : sms;
   return S;
 }
@@ -785,7 +1043,7 @@ bool finalize_plan(GemmPlan& p, const void* A, int lda, const void* B, int ldb, 
   p.args.workspace = workspace;
   p.args.tile_counters = counters;
   if (!make_tmap_bf16(&p.tmA, A, a_rows ? a_rows : (uint64_t)p.args.M, p.args.K, lda, a_box_rows(p))) return false;
-  if (!make_tmap_bf16(&p.tmB, B, b_rows ? b_rows : (uint64_t)p.args.N, p.args.K, ldb, p.bn)) return false;
+  if (!make_tmap_bf16(&p.tmB, B, b_rows ? b_rows : (uint64_t)p.args.N, p.args.K, ldb, b_box_rows(p))) return false;
   return true;
 }
 
@@ -793,6 +1051,15 @@ void run_gemm(const GemmPlan& p, cudaStream_t s) {
   if (p.args.M <= 0) return;
   if (p.swap) {
     run_gemm_swap(p, s);
+    return;
+  }
+  if (p.pair) {
+    switch (p.epi) {
+      case EPI_F32: launch_pair<256, EPI_F32>(p, s); break;
+      case EPI_SILU: launch_pair<256, EPI_SILU>(p, s); break;
+      case EPI_ADD: launch_pair<256, EPI_ADD>(p, s); break;
+      default: launch_pair<256, EPI_BF16>(p, s); break;
+    }
     return;
   }
   switch (p.epi) {

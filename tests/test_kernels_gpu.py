@@ -97,45 +97,112 @@ def test_gemm_f32_add_silu(C):
     torch.cuda.synchronize()
 
 
+_PAIR_CHECK = """
+import torch
+from kunserve_b200.ops import native, check_error
+C = native()
+torch.manual_seed(9)
+res = []
+for M, N, K, epi in ((256, 512, 256, "bf16"), (300, 1000, 512, "bf16"), (1000, 2304, 1024, "add"),
+                     (513, 768, 4096, "f32"), (306, 27648, 5120, "silu"), (2048, 5120, 5120, "bf16")):
+    plan = C.gemm_plan(M, N, K, {"bf16": C.EPI_BF16, "add": C.EPI_ADD, "f32": C.EPI_F32, "silu": C.EPI_SILU}[epi], 0)
+    for rep in range(2):
+        A = torch.randn(M, K, device="cuda").bfloat16()
+        W = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+        y = A.float() @ W.float().t()
+        if epi == "silu":
+            out = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+            C.gemm(A, W, out, C.EPI_SILU, None, 256, 16)
+            g = y.view(M, N // 256, 2, 128)
+            ref = (torch.nn.functional.silu(g[:, :, 0]) * g[:, :, 1]).reshape(M, N // 2)
+        elif epi == "add":
+            out = torch.randn(M, N, device="cuda").bfloat16()
+            ref = y + out.float()
+            C.gemm(A, W, out, C.EPI_ADD, out, 0, 16)
+        elif epi == "f32":
+            out = torch.empty(M, N, device="cuda")
+            ref = y
+            C.gemm(A, W, out, C.EPI_F32, None, 0, 16)
+        else:
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ref = y
+            C.gemm(A, W, out, C.EPI_BF16, None, 0, 16)
+        torch.cuda.synchronize()
+        res.append((M, N, K, epi, plan["pair"], ((out.float() - ref).norm() / ref.norm()).item()))
+check_error()
+print("RES", res)
+"""
+
+
+def test_gemm_cta_pair_tiles():
+    """CTA-pair (cta_group::2) 256 x 256 tiles, forced on with
+    KUNSERVE_GEMM_PAIR=2: every epilogue equals the fp32 product, including
+    ragged M and N and a second run."""
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, KUNSERVE_GEMM_PAIR="2")
+    r = subprocess.run([sys.executable, "-c", _PAIR_CHECK], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    res = eval(r.stdout.split("RES", 1)[1])
+    assert all(pair == 1 for *_, pair, _ in res), res
+    for *shape, pair, rel in res:
+        assert rel < 1e-2, res
+
+
 _REGULAR_SK_CHECK = """
 import torch
 from kunserve_b200.ops import native, check_error
 C = native()
 torch.manual_seed(5)
 res = []
-for M, N, K, epi in ((306, 27648, 5120, "silu"), (300, 15360, 5120, "bf16"), (140, 38400, 2048, "bf16")):
-    A = torch.randn(M, K, device="cuda").bfloat16()
-    W = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
-    if epi == "silu":
-        out = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
-        sk = C.gemm(A, W, out, C.EPI_SILU, None, 256, 16)
-        y = (A.float() @ W.float().t()).view(M, N // 256, 2, 128)
-        ref = (torch.nn.functional.silu(y[:, :, 0]) * y[:, :, 1]).reshape(M, N // 2)
-    else:
-        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        sk = C.gemm(A, W, out, C.EPI_BF16, None, 0, 16)
-        ref = A.float() @ W.float().t()
-    torch.cuda.synchronize()
-    rel = ((out.float() - ref).norm() / ref.norm()).item()
-    res.append((sk, rel))
+for rep in range(2):
+    for M, N, K, epi in ((306, 27648, 5120, "silu"), (300, 15360, 5120, "bf16"), (140, 38400, 2048, "bf16"),
+                         (130, 4096, 4096, "add"), (384, 2048, 2048, "f32")):
+        A = torch.randn(M, K, device="cuda").bfloat16()
+        W = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+        y = A.float() @ W.float().t()
+        if epi == "silu":
+            out = torch.empty(M, N // 2, device="cuda", dtype=torch.bfloat16)
+            sk = C.gemm(A, W, out, C.EPI_SILU, None, 256, 16)
+            g = y.view(M, N // 256, 2, 128)
+            ref = (torch.nn.functional.silu(g[:, :, 0]) * g[:, :, 1]).reshape(M, N // 2)
+        elif epi == "add":
+            out = torch.randn(M, N, device="cuda").bfloat16()
+            ref = y + out.float()
+            sk = C.gemm(A, W, out, C.EPI_ADD, out, 0, 16)
+        elif epi == "f32":
+            out = torch.empty(M, N, device="cuda")
+            ref = y
+            sk = C.gemm(A, W, out, C.EPI_F32, None, 0, 16)
+        else:
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ref = y
+            sk = C.gemm(A, W, out, C.EPI_BF16, None, 0, 16)
+        torch.cuda.synchronize()
+        res.append((M, N, epi, sk, ((out.float() - ref).norm() / ref.norm()).item()))
 check_error()
 print("RES", res)
 """
 
 
-def test_gemm_regular_stream_k():
-    """The regular kernel with its last partial wave spread along K
-    (KUNSERVE_REGULAR_SK=1): SiLU and bf16 epilogues equal the fp32 product."""
+@pytest.mark.parametrize("mode", ["1", "2"])
+def test_gemm_regular_last_wave_splits(mode):
+    """The regular kernel with its last partial wave split along K:
+    KUNSERVE_REGULAR_SK=1 (stream-K, L2 reductions into the shared
+    workspace) and 2 (split-K units with partial slots, the last unit
+    sums them).  Every epilogue equals the fp32 product; the second pass
+    checks that the workspace and counters were left clean."""
     import os
     import subprocess
     import sys
-    env = dict(os.environ, KUNSERVE_REGULAR_SK="1")
+    env = dict(os.environ, KUNSERVE_REGULAR_SK=mode, KUNSERVE_GEMM_PAIR="0")
     r = subprocess.run([sys.executable, "-c", _REGULAR_SK_CHECK], env=env, capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0, r.stderr[-3000:]
     res = eval(r.stdout.split("RES", 1)[1])
-    assert any(sk > 0 for sk, _ in res), res
-    for sk, rel in res:
+    assert any(sk > 0 for *_, sk, _ in res), res
+    for *_, rel in res:
         assert rel < 1e-2, res
 
 
