@@ -44,6 +44,7 @@ unavailable.
 """
 import argparse
 import asyncio
+import gc
 import json
 import os
 import subprocess
@@ -55,6 +56,29 @@ import numpy as np
 
 METRIC = "P99 TTFT/TPOT + SLO goodput (req/s) under bursty overload, max over ranks"
 
+
+# interval of the front end's polls of worker 0 during warm-up and the
+# timed window (the window's end is marked on the device by worker 0 itself)
+POLL_S = 0.002
+
+
+class GcWatch:
+    """Seconds the front end spent in garbage collections (gc.callbacks): a
+    full collection over the heap of thousands of live requests pauses the
+    event loop, and with it every step dispatch."""
+
+    def __init__(self):
+        self.total, self.longest, self.count, self._t = 0.0, 0.0, 0, None
+
+    def __call__(self, phase, info):
+        if phase == "start":
+            self._t = time.perf_counter()
+        elif self._t is not None:
+            dt = time.perf_counter() - self._t
+            self.total += dt
+            self.longest = max(self.longest, dt)
+            self.count += 1
+            self._t = None
 
 def parse():
     p = argparse.ArgumentParser()
@@ -236,6 +260,8 @@ class Job:
         from kunserve_b200.runtime.streams import StreamRouter
         a = self.args
         self.router = StreamRouter(asyncio.get_running_loop())
+        self.gcw = GcWatch()
+        gc.callbacks.append(self.gcw)
         self.groups = [GroupEngine(gi, insts, a.balloon_mode, self.cfg.balloon_config.max_balloon_memory_ratio)
                        for gi, insts in enumerate(self.inst_groups)]
         for g in self.groups:
@@ -247,6 +273,8 @@ class Job:
         for inst in self.instances:
             inst.set_vote_window(10)
         self.llm = AsyncLLM(self.cfg, self.mc, self.groups, self.router)
+        from kunserve_b200.llm import tune_gc
+        tune_gc()   # as AsyncLLM.create does
         # the bench polls load and the state machine ten times a second so a
         # balloon can start inside a window of a few hundred milliseconds
         self.llm.coordinator.load_interval = 0.05
@@ -416,9 +444,12 @@ class Job:
         # tensor-parallel collectives (CUDA events around them, on every GPU)
         await self.call_all("set_profile", True)
         s_w = await self.gpu0_steps()
+        # polls of GPU 0's step count are RPCs through the front end's event
+        # loop and worker 0's request queue: every few milliseconds, so that
+        # they do not compete with the steps being measured
         while await self.gpu0_steps() - s_w < a.warmup:
             self._check()
-            await asyncio.sleep(0.0005)
+            await asyncio.sleep(POLL_S)
         fill_steps = await self.gpu0_steps() - s_fill
         await self.pause()
         prof = await self.call_all("profile")
@@ -436,6 +467,12 @@ class Job:
         trans0 = [len(g.transitions) for g in self.groups]
 
         # ---- timed window
+        # the loaded state's objects (requests, outputs, page tables) move to
+        # the permanent generation: the window's collections scan only new
+        # objects instead of pausing the event loop over the whole heap
+        gc.collect()
+        gc.freeze()
+        gc0 = (self.gcw.total, self.gcw.count)
         t0 = time.time()
         await aw(self.workers[0].arm_mark.remote("w1", a.steps))
         self.llm.coordinator.enable_balloon = any(len(g.instances) > 1 for g in self.groups)
@@ -452,7 +489,7 @@ class Job:
         c1_gpu0 = None
         while c1_gpu0 is None:
             self._check()
-            await asyncio.sleep(0.0002)
+            await asyncio.sleep(POLL_S)
             c1_gpu0 = await aw(self.workers[0].armed_counters.remote())
         # GPU 0 marked the window's end inside its K-th step; the others mark
         # theirs behind whatever they have in flight now
@@ -464,11 +501,14 @@ class Job:
         c1[0] = c1_gpu0
         ht = {k: round(sum(inst.host_time[k] - h[k] for inst, h in zip(self.instances, ht0)), 4)
               for k in ht0[0]}
-        host_profile = {"frontend_s": ht,
+        gc_win = (round(self.gcw.total - gc0[0], 4), self.gcw.count - gc0[1])
+        host_profile = {"frontend_s": ht, "gc_s": gc_win[0], "gc_collections": gc_win[1],
                         "gpu0": {"steps": c1[0]["steps"] - c0[0]["steps"],
                                  "gpu_s": round((c1[0]["gpu_ms"] - c0[0]["gpu_ms"]) / 1000.0, 4),
                                  "step_call_s": round(c1[0]["step_s"] - c0[0]["step_s"], 4),
-                                 "pack_s": round(c1[0]["pack_s"] - c0[0]["pack_s"], 4)}}
+                                 "pack_s": round(c1[0]["pack_s"] - c0[0]["pack_s"], 4),
+                                 **{k: round(c1[0].get(k, 0.0) - c0[0].get(k, 0.0), 4)
+                                    for k in ("recv_s", "launch_s", "sync_s", "send_s")}}}
         # token times of the requests still in flight at the window's end
         for inst in self.live():
             for r in list(inst.unaccepted_queue) + [r for s in inst.scheduler for r in s.all_requests()]:
@@ -523,6 +563,7 @@ class Job:
         for g in self.groups:
             g.transitions.clear()
         await self.back_to_initial()
+        gc.unfreeze()
 
         win_s = win_ms / 1000.0
         t_end = t0 + (win_s if not via_api else (t1 - t0))
@@ -749,7 +790,8 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
                        "finished_goodput": round(e2e["finished_goodput"], 4),
                        "p99_ttft_s": round(pct(e2e["ttft"], 99), 4), "p99_tpot_s": round(pct(e2e["tpot"], 99), 5),
                        "h2d_bytes_per_step": int(e2e["h2d_per_step"]), "d2h_bytes_per_step": int(e2e["d2h_per_step"]),
-                       "window_s": round(e2e["host_window_s"], 4), "finished": e2e["finished"]}
+                       "window_s": round(e2e["host_window_s"], 4), "finished": e2e["finished"],
+                       "transitions": e2e.get("transitions")}
     return line
 
 

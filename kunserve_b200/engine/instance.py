@@ -672,6 +672,7 @@ class InstanceEngine(AdmissionMixin):
         await self.stop_and_wait()
         for m in members:
             await m.stop_and_wait()
+        t_stop = time.perf_counter() - t0   # in-flight steps finishing
         if not from_restore:
             for k, m in enumerate(members, start=1):
                 self.merge_engine(k, m)
@@ -679,11 +680,13 @@ class InstanceEngine(AdmissionMixin):
         self.set_fusion_state(True)
         for bm in self.block_managers:
             bm.convert_to_pipeline_format(n)
+        t_merge = time.perf_counter() - t0 - t_stop
         # drop parameters; their memory becomes extend pages
         drops = [self._call_instance(i, "pmm_drop", i, n) for i in range(n)]
         for i, futs in enumerate(drops):
             res = [await aw(f) for f in futs]
             self.block_managers[i].add_ex_fusion_blocks(min(res))
+        t_drop = time.perf_counter() - t0 - t_stop - t_merge
         # stale (pre-balloon) requests
         self.is_resharding = [False] * len(self.scheduler)
         mode = self.balloon_config.effective_mode
@@ -697,6 +700,7 @@ class InstanceEngine(AdmissionMixin):
             await self.reshard_blocks(stale)
         elif mode == "livereshard":
             self.is_resharding = [True] * len(self.scheduler)
+        t_kv = time.perf_counter() - t0 - t_stop - t_merge - t_drop
         for bm in self.block_managers:
             bm.convert_all_reserved_blocks_into_fusion()
         # even out VE loads, then admit again
@@ -716,8 +720,9 @@ class InstanceEngine(AdmissionMixin):
                 await self._get_next_batch(ve)
         dt = time.perf_counter() - t0
         self.event_log.append((time.time(), "balloon", dt))
-        logger.info(f"instance {self.instance_id}: balloon with {n} instances in {dt:.3f}s, "
-                    f"free pages now {self.get_free_gpu_blocks()}")
+        logger.info(f"instance {self.instance_id}: balloon with {n} instances in {dt:.3f}s "
+                    f"(in-flight steps {t_stop:.3f}s, merge {t_merge:.3f}s, parameter drop {t_drop:.3f}s, "
+                    f"stale KV {t_kv:.3f}s), free pages now {self.get_free_gpu_blocks()}")
         return self.get_free_gpu_blocks()
 
     def prepare_reshard_blocks(self, requests: Sequence[Request]) -> Tuple[List[Request], List[Request]]:

@@ -221,6 +221,9 @@ class NativeRunner:
         self.d2h_bytes = 0
         self.num_steps = 0
         self.pack_s = 0.0      # host seconds spent packing step metadata
+        # host seconds of a step's other phases: activation receive (enqueue),
+        # forward launch, wait for the device, activation send
+        self.phase_s = {"recv": 0.0, "launch": 0.0, "sync": 0.0, "send": 0.0}
         self.restore_s = 0.0   # device seconds of parameter-restore pulls, and their bytes
         self.restore_bytes = 0.0
 
@@ -322,6 +325,7 @@ class NativeRunner:
         self.pack_s += time.perf_counter() - tp
         splits = self._splits(T, n_items, max_ctx) if n_items else 1
         first = recv_from is None
+        t1 = time.perf_counter()
         if not first:
             buf = self.comm.recv((T, self.shape.hidden), torch.bfloat16, self.device, *recv_from)
             self.eng.hidden()[:T].copy_(buf)
@@ -329,19 +333,27 @@ class NativeRunner:
         if self._ev is None:
             self._ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         self._ev[0].record()
+        t2 = time.perf_counter()
         out = self.eng.forward(self.meta, T, B, width, n_items, splits, n_dec, n_units, dec_heads, step.layer_start,
                                step.layer_end, step.fusion_size, first, last_stage, sample_mode, step.step_id)
+        t3 = time.perf_counter()
         # the forward returned after its device work (it reads the sampled ids
         # back), so this bracket is the step's time on the GPU
         self._ev[1].record()
         self._ev[1].synchronize()
+        t4 = time.perf_counter()
+        self.phase_s["recv"] += t2 - t1
+        self.phase_s["launch"] += t3 - t2
+        self.phase_s["sync"] += t4 - t3
         self.gpu_ms += self._ev[0].elapsed_time(self._ev[1])
         self.num_steps += 1
         self.h2d_bytes += 4 * n
         if last_stage:
             self.d2h_bytes += 4 * B
         if send_to is not None:
+            t5 = time.perf_counter()
             self._send_async(T, send_to)
+            self.phase_s["send"] += time.perf_counter() - t5
         if not last_stage:
             return None
         return list(out)

@@ -178,7 +178,12 @@ class Worker:
         self.dropped = [l for l in range(L) if l not in keep]
         self.fusion_size = n
         if self.backend == "native":
-            return self.runner.drop_layers(self.dropped, n)
+            t0 = time.perf_counter()
+            out = self.runner.drop_layers(self.dropped, n)
+            dt = time.perf_counter() - t0
+            if dt > 0.1:
+                logger.info(f"worker {self.worker_id}: parameter drop took {dt:.3f}s")
+            return out
         freed = 0
         for l in self.dropped:
             lw = self.runner.w.layers[l]
@@ -458,7 +463,7 @@ class Worker:
         return {"launches": int(r.eng.launches()), "steps": self.steps_done, "gpu_ms": float(r.gpu_ms),
                 "h2d": int(r.h2d_bytes), "d2h": int(r.d2h_bytes), "pack_s": float(r.pack_s),
                 "step_s": float(self.step_wall_s), "restore_s": float(r.restore_s),
-                "restore_bytes": float(r.restore_bytes)}
+                "restore_bytes": float(r.restore_bytes), **{k + "_s": float(v) for k, v in r.phase_s.items()}}
 
     def last_logits(self, n: int) -> torch.Tensor:
         """fp32 logits of the last step's ``n`` rows (left by sample mode 1)."""

@@ -8,6 +8,7 @@ prompt, prompt_len, outputs, metrics}``), ``batch_generate``, per-epoch
 reference's no-op, stops every loop and worker).
 """
 import asyncio
+import gc
 import itertools
 import os
 import time
@@ -35,6 +36,19 @@ def runtime_configs(cfg: KunServeConfig, model_config: Optional[ModelConfig] = N
                      chunked_prefill_size=ec.chunked_prefill_size,
                      chunked_prefill_budget=ec.chunked_prefill_budget, use_tensor_cores=ec.use_tensor_cores)
     return mc, cc, sc
+
+
+def tune_gc() -> None:
+    """The front end's event loop drives every step: a full garbage
+    collection over thousands of live requests pauses it (and the GPUs
+    waiting for their next step) for up to seconds.  The objects built at
+    start-up go to the permanent generation and full collections run ten
+    times less often (the youngest generations, where per-step garbage
+    dies, keep their defaults)."""
+    gc.collect()
+    gc.freeze()
+    g0, g1, g2 = gc.get_threshold()
+    gc.set_threshold(g0, g1, max(g2, 100))
 
 
 class AsyncLLM:
@@ -79,6 +93,7 @@ class AsyncLLM:
         llm = cls(cfg, mc, groups, router, server_id, tokenizer)
         if cfg.balloon_config.enable_transfer and os.environ.get("KUNSERVE_P2P", "1") != "0":
             await llm.coordinator.setup_global_peer_memory()
+        tune_gc()
         llm.start()
         return llm
 
