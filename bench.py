@@ -738,6 +738,16 @@ def main():
     return rc
 
 
+def weight_gb_per_gpu(model: str, tp: int) -> float:
+    """bf16 weights of `model` held by one of `tp` tensor-parallel GPUs."""
+    from kunserve_b200.config import ModelConfig
+    a = ModelConfig(model, dtype="bf16").arch
+    hd = a.head_dim or a.hidden_size // a.num_attention_heads
+    H, F = a.hidden_size, a.intermediate_size
+    layer = H * (a.num_attention_heads + 2 * a.num_key_value_heads) * hd + a.num_attention_heads * hd * H + 3 * H * F
+    return 2.0 * (a.num_hidden_layers * layer + 2 * a.vocab_size * H) / tp / 1e9
+
+
 def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
     par = f"tp{tp}xdp{ninst}" + (f" (balloon groups of {gs} -> tp{tp}xpp{gs})" if gs > 1 else "")
     line = {
@@ -755,7 +765,8 @@ def result_line(args, world, tp, gs, ngroups, ninst, nat, e2e, base):
                    if gs > 1 else 0, "balloon_mode": args.balloon_mode, "kv_budget_gb_per_gpu": args.kv_gb,
                    "block_size": args.block_size, "chunked_prefill_budget": args.budget,
                    "slo": {"ttft_s": args.ttft_slo, "tpot_s": args.tpot_slo},
-                   "l2": "inputs larger than L2: every step streams the weights (13 GB per TP2 GPU) and the KV pages",
+                   "l2": f"inputs larger than L2: every step streams the weights ({weight_gb_per_gpu(args.model, tp):.0f} "
+                         f"GB per TP{tp} GPU) and the KV pages",
                    "policy": "mixed prefill+decode batches, recompute preemption"},
         "p99_ttft_s": round(pct(nat["ttft"], 99), 4), "p99_tpot_s": round(pct(nat["tpot"], 99), 5),
         "p50_ttft_s": round(pct(nat["ttft"], 50), 4), "p50_tpot_s": round(pct(nat["tpot"], 50), 5),
