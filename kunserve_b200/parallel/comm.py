@@ -55,6 +55,36 @@ class Communicator:
                 if rank in ranks:
                     self.groups[comm] = g
                     self.members[comm] = list(ranks)
+        if os.environ.get("KUNSERVE_WARM_LINKS", "1") != "0":
+            self.warm_links()
+
+    def warm_links(self) -> None:
+        """Set up every communicator's collective and point-to-point links
+        now: NCCL creates them at their first use, and the first use of the
+        fused pipeline's activation sends (or of a KV or parameter exchange)
+        would otherwise pay that set-up inside serving, right after a balloon
+        transition.  Every rank calls this at the same point (groups of one
+        comm type are disjoint, and each group's sends and receives go in one
+        batch), so no rank waits on another's order."""
+        dev = torch.device("cuda", torch.cuda.current_device()) if self.backend == "nccl" else torch.device("cpu")
+        for comm in COMMS:
+            g, members = self.groups.get(comm), self.members.get(comm, [])
+            if g is None or len(members) < 2:
+                continue
+            x = torch.zeros(1, device=dev)
+            dist.all_reduce(x, group=g)
+            ops, bufs = [], []
+            for peer in members:
+                if peer == self.rank:
+                    continue
+                b = torch.zeros(1, device=dev)
+                bufs.append(b)
+                ops.append(dist.P2POp(dist.isend, torch.ones(1, device=dev), peer, group=g))
+                ops.append(dist.P2POp(dist.irecv, b, peer, group=g))
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        if self.backend == "nccl":
+            torch.cuda.synchronize()
 
     def size(self, comm: str) -> int:
         return len(self.members[comm])
