@@ -1,10 +1,11 @@
-// Per-CTA walk over the GEMM work units of a plan (see GemmArgs): first the
-// whole tiles this CTA owns round-robin, then its contiguous slice of the
-// concatenated K loops of the stream-K tiles, cut at tile boundaries.  The
-// producer, MMA and epilogue roles each run their own copy of the walk and
-// see the same sequence of segments.
+// Per-walker walk over the GEMM work units of a plan (see GemmArgs): first
+// the whole tiles the walker owns round-robin, then either its contiguous
+// slice of the concatenated K loops of the stream-K tiles (cut at tile
+// boundaries) or its split-K tail units.  A walker is a CTA, or a CTA pair
+// for cta_group::2 tiles.  The producer, MMA and epilogue roles each run
+// their own copy of the walk and see the same sequence of segments.
 //
-// The split follows Osama et al., "Stream-K: Work-centric Parallel
+// The stream-K split follows Osama et al., "Stream-K: Work-centric Parallel
 // Decomposition for Dense Matrix-Matrix Multiplication on the GPU" (PPoPP
 // 2023), "data-parallel + one-tile stream-K" hybrid; the partial tiles are
 // summed with fp32 reductions at L2 instead of a fixed-up partials array.
