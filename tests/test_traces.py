@@ -84,3 +84,19 @@ def test_builder_cli_round_trip(tmp_path):
     listing = subprocess.run([sys.executable, "evaluation/trace_builder.py", "--list"], cwd=ROOT,
                              capture_output=True, text=True, timeout=120)
     assert listing.returncode == 0 and "maf" in listing.stdout
+
+
+def test_workload_reports(tmp_path):
+    sys.path.insert(0, os.path.join(ROOT, "evaluation"))
+    import dataset_profile as dp
+    r = dp.length_report([100, 16000, 50], [10, 1000, 5], max_len=16384)
+    assert r["requests"] == 3 and r["capped"] == 1
+    assert r["prompt_max"] == 15384 and r["output_max"] == 1000      # the prompt is cut, the output kept
+    tr = dp.trace_report([5.0, 1.0, 3.0, 9.0], until=4.0)
+    assert tr["requests"] == 4 and tr["span_s"] == 8.0
+    assert tr["index_at_until"] == 2                                  # arrivals at 0, 2, 4, 8 s after the first
+    table = tmp_path / "t.parquet"
+    pd.DataFrame({"prompt": ["a", "b"], "prompt_len": [3, 4], "response_len": [1, 2]}).to_parquet(table)
+    out = subprocess.run([sys.executable, "evaluation/dataset_profile.py", "--table", str(table)], cwd=ROOT,
+                         capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0 and '"requests": 2' in out.stdout
