@@ -73,7 +73,7 @@ class AsyncLLM:
     async def create(cls, cfg: KunServeConfig, model_config: Optional[ModelConfig] = None, server_id: int = 0,
                      backend: str = "auto", actor_kind: str = "auto", devices=None, seed: int = 0,
                      num_gpu_blocks: Optional[int] = None, cache_config: Optional[CacheConfig] = None,
-                     tokenizer=None) -> "AsyncLLM":
+                     tokenizer=None, weights_path: str = "") -> "AsyncLLM":
         from .bootstrap import build_instances
 
         mc, cc, sc = runtime_configs(cfg, model_config)
@@ -87,7 +87,8 @@ class AsyncLLM:
                               cfg.balloon_config.max_balloon_memory_ratio)
                   for gi, insts in enumerate(inst_groups)]
         for g in groups:
-            await asyncio.gather(*[i.initialize(num_gpu_blocks=num_gpu_blocks) for i in g.instances])
+            await asyncio.gather(*[i.initialize(num_gpu_blocks=num_gpu_blocks, weights_path=weights_path)
+                                   for i in g.instances])
             if os.environ.get("KUNSERVE_P2P", "1") != "0":
                 await g.setup_peer_memory()
         llm = cls(cfg, mc, groups, router, server_id, tokenizer)

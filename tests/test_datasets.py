@@ -74,3 +74,21 @@ def test_cli_builds_from_a_local_directory(tmp_path):
     assert r.returncode == 0, r.stderr
     df = pd.read_parquet(out)
     assert len(df) == 5 and list(df.columns)[:3] == ["prompt", "prompt_len", "response_len"]
+
+
+def test_generated_responses_replace_the_lengths(tmp_path):
+    """The vLLM generation step of the reference, through this framework:
+    prompts over the limit are skipped, a short table repeats, and the
+    response lengths are the generated token counts (PyTorch backend)."""
+    table = tmp_path / "t.parquet"
+    pd.DataFrame({"prompt": ["p0", "p1", "long"], "prompt_len": [12, 20, 30000],
+                  "response_len": [100, 100, 100]}).to_parquet(table)
+    out = tmp_path / "gen.parquet"
+    r = subprocess.run([sys.executable, "evaluation/data/generate_responses.py", "--table", str(table), "--out",
+                        str(out), "--model", "tiny-llama", "--device", "cpu", "--n", "3", "--max-tokens", "5",
+                        "--kv-pages", "64"], cwd=ROOT, capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, OMP_NUM_THREADS="2"))
+    assert r.returncode == 0, r.stderr[-3000:]
+    df = pd.read_parquet(out)
+    assert df["prompt"].tolist() == ["p0", "p1", "p0"]
+    assert (df["response_len"] == 5).all()
