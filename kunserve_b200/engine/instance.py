@@ -185,8 +185,16 @@ class InstanceEngine(AdmissionMixin):
                 if getattr(self, "_terminate", False):
                     return
                 continue
-            await asyncio.sleep(0 if any(s.running_queue.requests for s in self.scheduler)
-                                else SLEEP_IN_EACH_EVENT_LOOP)
+            busy = any(s.running_queue.requests for s in self.scheduler)
+            pending = [t for t in tasks.values() if not t.done()]
+            if busy and pending:
+                # wake when a VE step finishes (or after the idle interval, so
+                # that a VE without work looks for new requests) instead of
+                # spinning: a spinning loop holds the interpreter lock that the
+                # actor reader threads need to hand back step results
+                await asyncio.wait(pending, timeout=SLEEP_IN_EACH_EVENT_LOOP, return_when=asyncio.FIRST_COMPLETED)
+            else:
+                await asyncio.sleep(0 if busy else SLEEP_IN_EACH_EVENT_LOOP)
 
     def launch(self) -> asyncio.Task:
         self._loop_task = asyncio.create_task(self.start_event_loop())
