@@ -228,7 +228,9 @@ class InstanceEngine(AdmissionMixin):
     async def stop_and_wait(self) -> None:
         self.stopped = True
         while any(self.scheduler_running):
-            await asyncio.sleep(0)
+            # a short sleep, not a spin: the steps in flight finish only once
+            # the actor reader threads get the interpreter lock back
+            await asyncio.sleep(SLEEP_IN_EACH_EVENT_LOOP)
         self.release_finished()
 
     def release_finished(self) -> None:
