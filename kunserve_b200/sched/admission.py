@@ -20,7 +20,7 @@ This is a mixin: the instance engine provides ``scheduler``,
 ``is_fusion_state`` and ``pp_size``.
 """
 from collections import deque
-from typing import Tuple
+from typing import Optional, Tuple
 
 from ..kv.block_manager import NoFreeBlocksError
 from ..request import Request
@@ -42,6 +42,12 @@ class AdmissionMixin:
 
     def _allocate_blocks(self, request: Request) -> None:
         """All-or-nothing across every block manager the request needs."""
+        if not request.fusion_exec:
+            # most steps a request's pages already cover its next token
+            bm = self.block_managers[request.kv_fusion_rank]
+            table = bm.block_table.get(request.request_id)
+            if table is not None and len(table) * bm.block_size >= request.get_num_tokens():
+                return
         done = []
         try:
             for bm in self._bms_for(request):
@@ -120,9 +126,12 @@ class AdmissionMixin:
         return self.block_managers[kv_rank].num_free_whole()
 
     # ---------------------------------------------------------- admission
-    def check_add(self, ve: int, request: Request, is_waiting: bool = False) -> Tuple[int, int, int]:
+    def check_add(self, ve: int, request: Request, is_waiting: bool = False,
+                  batch_tokens: Optional[int] = None) -> Tuple[int, int, int]:
         """(overflow pages, overflow requests, overflow tokens) if ``request``
-        joined VE ``ve`` now; all zero means it fits."""
+        joined VE ``ve`` now; all zero means it fits.  ``batch_tokens``: the
+        input tokens of VE ``ve``'s running batch, when the caller keeps that
+        sum (chunked or mixed batching only)."""
         kv_rank = ve // self.pp_size
         if not is_waiting:
             request.fusion_exec = self.is_fusion_state
@@ -131,14 +140,15 @@ class AdmissionMixin:
         over_blocks = 0 if is_waiting else max(0, need - self._free_units(request, kv_rank))
         s = self.scheduler[ve]
         mixed = self.sched_config.policy == "mixed"
-        if request.is_context_stage() and not self.sched_config.enable_chunked_prefill and not mixed:
-            cur = s.running_queue.get_context_requests()
-        else:
-            cur = s.running_queue.requests
+        whole_batch = not (request.is_context_stage() and not self.sched_config.enable_chunked_prefill and not mixed)
+        cur = s.running_queue.requests if whole_batch else s.running_queue.get_context_requests()
         over_reqs = max(0, len(cur) + 1 - self.sched_config.max_batch_size)
         limit = (self.sched_config.chunked_prefill_budget if self.sched_config.enable_chunked_prefill
                  else self.sched_config.max_tokens_per_batch)
-        used = sum(r.get_num_input_tokens() for r in cur)
+        if whole_batch and batch_tokens is not None:
+            used = batch_tokens
+        else:
+            used = sum(r.get_num_input_tokens() for r in cur)
         over_tokens = max(0, used + request.get_num_input_tokens() - limit)
         return over_blocks, over_reqs, over_tokens
 
@@ -172,11 +182,18 @@ class AdmissionMixin:
         Returns True if admission stopped on KV pages (queueing)."""
         if self.sched_config.enable_chunked_prefill:
             self._advance_chunks(ve)
+        # the running batch's input tokens, kept up to date as requests join
+        # (chunked or mixed batching: every running request counts)
+        keep = self.sched_config.enable_chunked_prefill or self.sched_config.policy == "mixed"
+        batch = self.scheduler[ve].running_queue.requests
+        used = sum(q.get_num_input_tokens() for q in batch) if keep else None
         while (r := self._fetch_unaccepted(ve, use_global)) is not None:
-            ob, oreq, otok = self.check_add(ve, r)
+            ob, oreq, otok = self.check_add(ve, r, batch_tokens=used)
             if (ob, oreq, otok) == (0, 0, 0):
                 if not self._admit(ve, r):
                     return True
+                if keep:
+                    used += r.get_num_input_tokens()
             elif self.sched_config.enable_chunked_prefill and ob == 0 and oreq == 0:
                 avail = r.get_num_input_tokens() - otok
                 if avail <= 0:
@@ -184,6 +201,8 @@ class AdmissionMixin:
                 r.set_chunk(avail)
                 if not self._admit(ve, r):
                     return True
+                if keep:
+                    used += r.get_num_input_tokens()
                 if r.have_follow_up_chunk():
                     break
             else:
